@@ -1,0 +1,138 @@
+/*
+ * unbox_b200 -- C ABI of the B200 (sm_100a) paged decode-attention path.
+ *
+ * These entry points replace, for one decode step of the unbox.ai inference
+ * engine, the per-sequence KV write loop and the paged attention call
+ * (reference: unbox_platform/infer/engine.py:213-224). All pointers are device
+ * pointers unless stated otherwise; strides are in ELEMENTS; the innermost
+ * (head_dim) dimension of every tensor is contiguous. Every call is
+ * asynchronous on `stream` (a cudaStream_t passed as void*, NULL = legacy
+ * default stream), allocates nothing, and never synchronises the host, so a
+ * decode step made of these calls can be captured in a CUDA graph.
+ *
+ * Return value: UBX_OK or a UBX_ERR_* status for host-side validation and
+ * launch failures (ubx_last_error() gives the message). Data-dependent problems
+ * found on the device (a page id outside the pool, a context longer than its
+ * block-table row, ...) do not fault: the kernel skips the access, writes a
+ * UBX_DEVERR_* bit into the workspace's error word and carries on; read it with
+ * ubx_read_device_error().
+ */
+#ifndef UNBOX_B200_H_
+#define UNBOX_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types of q / k / v / out (the pool dtype, configs/infer/serve.yaml `dtype`) */
+#define UBX_DTYPE_F32 0
+#define UBX_DTYPE_BF16 1
+#define UBX_DTYPE_F16 2
+
+/* host-side status codes */
+#define UBX_OK 0
+#define UBX_ERR_INVALID_ARGUMENT 1 /* shape, stride, alignment or pointer rejected */
+#define UBX_ERR_UNSUPPORTED 2      /* valid but not built: head_dim, block_size, GQA ratio */
+#define UBX_ERR_WORKSPACE 3        /* workspace missing or too small */
+#define UBX_ERR_CUDA 4             /* a CUDA runtime/driver call failed */
+
+/* device error bits, OR-ed into the workspace error word */
+#define UBX_DEVERR_BAD_PAGE 1      /* block-table entry outside [0, num_blocks): tile read as zeros */
+#define UBX_DEVERR_CTX_TOO_LONG 2  /* context_len > max_blocks_per_seq * block_size: clamped */
+#define UBX_DEVERR_NEG_CTX 4       /* negative context_len: treated as 0 */
+#define UBX_DEVERR_TIMEOUT 8       /* a pipeline wait exceeded its bound; output undefined */
+#define UBX_DEVERR_BAD_SLOT 16     /* kv_append slot >= num_blocks * block_size: row skipped */
+
+/* work schedules of the attention kernel */
+#define UBX_SCHEDULE_AUTO 0     /* library picks */
+#define UBX_SCHEDULE_BALANCED 1 /* persistent grid, equal pages per CTA, in-kernel LSE merge */
+#define UBX_SCHEDULE_SPLIT 2    /* fixed split-KV chunks per sequence + LSE combine kernel */
+
+const char* ubx_status_string(int status);
+/* Message of the last failing call on this host thread ("" if none). */
+const char* ubx_last_error(void);
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+int ubx_version(void);
+
+/*
+ * KV append: k_cache[slot / bs, slot % bs, h, :] = k_new[t, h, :] (and V) for
+ * every token t with slot = slot_mapping[t] >= 0; a negative slot is padding.
+ * Byte copy, bit-exact.
+ * Replaces: KVPool.write_kv (unbox_platform/infer/kvcache.py:253-262) reached
+ * through PagedKVCache.write_kv (kvcache.py:330-340) once per sequence from
+ * InferenceEngine.decode_step (unbox_platform/infer/engine.py:213-215).
+ *   k_new, v_new:  (num_tokens, num_kv_heads, head_dim), strides (new_s_tok, new_s_head)
+ *   k_cache, v_cache: (num_blocks, block_size, num_kv_heads, head_dim) -- the
+ *                  per-layer views KVPool.get_kv_layer returns (kvcache.py:264-266),
+ *                  strides (c_s_block, c_s_tok, c_s_head), identical for K and V
+ *   slot_mapping:  (num_tokens,) int64
+ *   error_word:    device int32 for UBX_DEVERR_BAD_SLOT, may be NULL
+ */
+int ubx_kv_append(const void* k_new, const void* v_new, int64_t new_s_tok, int64_t new_s_head,
+                  void* k_cache, void* v_cache, int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head,
+                  const int64_t* slot_mapping, int64_t num_tokens, int num_kv_heads, int head_dim,
+                  int block_size, int64_t num_blocks, int dtype, int32_t* error_word, void* stream);
+
+/*
+ * Slot mapping of one decode step: slot[b] = block_table[b, pos // bs] * bs + pos % bs
+ * with pos = positions[b] (the index arithmetic of PagedKVCache.write_kv,
+ * kvcache.py:338-339). A negative position or page gives slot -1.
+ * Computed once per step and shared by all layers (engine.py:179-187 builds the
+ * block table once per step).
+ */
+int ubx_slot_mapping(const int32_t* block_table, int64_t bt_s_row, const int32_t* positions,
+                     int64_t* slot_mapping, int batch, int max_blocks_per_seq, int block_size, void* stream);
+
+/*
+ * Bytes of device workspace the attention entry points need for these sizes on
+ * the current device (partial results of split sequences, merge counters, the
+ * error word). The workspace must be zeroed once with ubx_workspace_init before
+ * its first use; the kernels leave it ready for the next call.
+ */
+int ubx_paged_decode_workspace_size(int batch, int num_heads, int head_dim, int max_blocks_per_seq,
+                                    int split_pages, size_t* bytes);
+int ubx_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Paged GQA decode attention for one new token per sequence:
+ *   out[b, h, :] = softmax_j(scale * q[b,h,:] . K_j) V_j over the first
+ *   context_lens[b] positions of sequence b, position j living in page
+ *   block_table[b, j // block_size], slot j % block_size, KV head
+ *   h // (num_heads / num_kv_heads).
+ * Replaces: paged_decode_attention / paged_decode_attention_ref
+ * (unbox_platform/infer/kernels/paged_decode_attention.py:106-150, 157-191),
+ * called at unbox_platform/infer/engine.py:221-224 with
+ * scale = head_dim ** -0.5 (paged_decode_attention.py:134,169).
+ *   q:            (batch, num_heads, head_dim), strides (q_s_b, q_s_h)
+ *   k/v_cache:    (num_blocks, block_size, num_kv_heads, head_dim), strides
+ *                 (c_s_block, c_s_tok, c_s_head); base 16-byte aligned and
+ *                 strides multiples of 16 bytes (TMA)
+ *   block_table:  (batch, max_blocks_per_seq) int32, row stride bt_s_row, -1 padded
+ *   context_lens: (batch,) int32, includes the token just appended
+ *   out:          (batch, num_heads, head_dim), strides (o_s_b, o_s_h), dtype of q
+ * A sequence with context_len 0 gets a zero row (the reference raises there).
+ * Supported: head_dim 64/112/128, block_size 16, num_heads/num_kv_heads in {1,2,4,8},
+ * dtype f32/bf16/f16 (q, caches and out share it).
+ */
+int ubx_paged_decode_attention(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache,
+                               const void* v_cache, int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head,
+                               const int32_t* block_table, int64_t bt_s_row, const int32_t* context_lens,
+                               void* out, int64_t o_s_b, int64_t o_s_h, int batch, int num_heads,
+                               int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
+                               int max_blocks_per_seq, float scale, int dtype, int schedule, int split_pages,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Read (and optionally clear) the device error word of a workspace. This one
+ * call synchronises `stream`.
+ */
+int ubx_read_device_error(const void* workspace, int32_t* value, int clear, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* UNBOX_B200_H_ */

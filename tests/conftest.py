@@ -1,0 +1,72 @@
+import glob
+import hashlib
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+GOLDEN_DIR = os.path.join(ROOT, "tests", "golden")
+sys.path.insert(0, ROOT)
+
+from __graft_entry__ import load_package  # noqa: E402
+
+PKG = load_package()
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
+
+
+def pytest_collection_modifyitems(config, items):
+    try:
+        import torch
+        has_gpu = torch.cuda.is_available()
+    except Exception:  # pragma: no cover
+        has_gpu = False
+    if has_gpu:
+        return
+    skip = pytest.mark.skip(reason="no CUDA device")
+    for it in items:
+        if "gpu" in it.keywords:
+            it.add_marker(skip)
+
+
+def sha(t) -> str:
+    import torch
+    x = t.contiguous()
+    if x.dtype == torch.bfloat16:
+        x = x.view(torch.int16)
+    return hashlib.sha256(x.numpy().tobytes()).hexdigest()
+
+
+GOLDEN_NAMES = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
+
+
+def load_golden(name: str):
+    """Fixture record, its layout and the regenerated host inputs (checked by SHA-256)."""
+    z = dict(np.load(os.path.join(GOLDEN_DIR, name + ".npz")))
+    wl = PKG.workloads
+    lay = wl.Layout(z["context_lens"], z["block_table"], int(z["num_blocks"]), int(z["num_heads"]),
+                    int(z["num_kv_heads"]), int(z["head_dim"]), int(z["block_size"]))
+    if "unique_pages" in z:
+        lay.unique_pages = int(z["unique_pages"])
+        lay.unique_pages_tokens = int(z["unique_pages_tokens"])
+    t = wl.materialize_host(lay, int(z["seed"]), dtype=str(z["dtype"]), value_scale=float(z["value_scale"]))
+    for k in ("q", "k_cache", "v_cache", "k_new", "v_new"):
+        assert sha(t[k]) == str(z["sha_" + k]), f"{name}: regenerated {k} differs from the fixture's inputs"
+    assert np.array_equal(t["slot_mapping"].numpy(), z["slot_mapping"])
+    return z, lay, t
+
+
+@pytest.fixture(scope="session")
+def pkg():
+    return PKG
+
+
+@pytest.fixture(scope="session")
+def oracle():
+    from oracle import oracle as o
+    o.build()
+    return o

@@ -1,0 +1,92 @@
+"""CPU: the C-ABI library loads, exports every entry point the header declares,
+and its host-side validation rejects bad arguments before touching the GPU."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "unbox_b200.h")
+
+
+def declared_symbols():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(ubx_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    for s in ("ubx_kv_append", "ubx_paged_decode_attention", "ubx_slot_mapping", "ubx_paged_decode_workspace_size",
+              "ubx_workspace_init", "ubx_read_device_error"):
+        assert s in syms
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    lib = pkg.library.load()
+    for s in declared_symbols():
+        assert hasattr(lib, s), f"{s} declared in the header but not exported"
+        assert s in pkg.library.SIGNATURES, f"{s} has no ctypes signature"
+    nm = os.popen(f"nm -D --defined-only {pkg.library.LIB_PATH}").read()
+    for s in declared_symbols():
+        assert re.search(rf"\bT {s}\b", nm), s
+
+
+def test_host_only_entry_points(pkg):
+    lib = pkg.library.load()
+    assert lib.ubx_version() >= 100
+    assert lib.ubx_status_string(0) == b"ok"
+    assert lib.ubx_status_string(3) == b"workspace missing or too small"
+
+
+def test_validation_rejects_before_any_launch(pkg):
+    lib = pkg.library.load()
+    # unknown dtype
+    st = lib.ubx_paged_decode_attention(None, 0, 0, None, None, 0, 0, 0, None, 0, None, None, 0, 0,
+                                        1, 16, 8, 112, 16, 1, 1, 1.0, 7, 0, 0, None, 0, None)
+    assert st == pkg.library.ERR_INVALID_ARGUMENT and b"dtype" in lib.ubx_last_error()
+    # head_dim not built
+    st = lib.ubx_paged_decode_attention(None, 0, 0, None, None, 0, 0, 0, None, 0, None, None, 0, 0,
+                                        1, 16, 8, 96, 16, 1, 1, 1.0, 1, 0, 0, None, 0, None)
+    assert st == pkg.library.ERR_UNSUPPORTED and b"head_dim" in lib.ubx_last_error()
+    # GQA ratio 3
+    st = lib.ubx_paged_decode_attention(None, 0, 0, None, None, 0, 0, 0, None, 0, None, None, 0, 0,
+                                        1, 12, 4, 112, 16, 1, 1, 1.0, 1, 0, 0, None, 0, None)
+    assert st == pkg.library.ERR_UNSUPPORTED
+    # page size other than 16
+    st = lib.ubx_paged_decode_attention(None, 0, 0, None, None, 0, 0, 0, None, 0, None, None, 0, 0,
+                                        1, 16, 8, 112, 32, 1, 1, 1.0, 1, 0, 0, None, 0, None)
+    assert st == pkg.library.ERR_UNSUPPORTED and b"block_size" in lib.ubx_last_error()
+    # null pointers with a real batch
+    st = lib.ubx_paged_decode_attention(None, 0, 0, None, None, 0, 0, 0, None, 0, None, None, 0, 0,
+                                        1, 16, 8, 112, 16, 1, 1, 1.0, 1, 0, 0, None, 0, None)
+    assert st == pkg.library.ERR_INVALID_ARGUMENT
+    # empty batch is a no-op
+    st = lib.ubx_paged_decode_attention(None, 0, 0, None, None, 0, 0, 0, None, 0, None, None, 0, 0,
+                                        0, 16, 8, 112, 16, 1, 1, 1.0, 1, 0, 0, None, 0, None)
+    assert st == 0
+    st = lib.ubx_kv_append(None, None, 0, 0, None, None, 0, 0, 0, None, 0, 8, 112, 16, 4, 1, None, None)
+    assert st == 0
+
+
+def test_ops_refuse_cpu_tensors(pkg):
+    """No CPU fallback: host tensors are an error, not a slow path."""
+    lay = pkg.workloads.layout_uniform(3, 2, 1, 20, num_blocks=4)
+    t = pkg.workloads.materialize_host(lay, 3, dtype="bfloat16")
+    with pytest.raises(ValueError, match="CUDA"):
+        pkg.paged_attention(t["q"], t["k_cache"], t["v_cache"], t["block_table"], t["context_lens"])
+    with pytest.raises(ValueError, match="CUDA"):
+        pkg.kv_append(t["k_new"], t["v_new"], t["k_cache"], t["v_cache"], t["slot_mapping"])
+    with pytest.raises(ValueError, match="CUDA"):
+        pkg.paged_decode_attention(t["q"], t["k_cache"], t["v_cache"], t["block_table"], t["context_lens"], 16)
+
+
+def test_missing_library_fails_loudly(pkg, monkeypatch, tmp_path):
+    lib_mod = pkg.library
+    monkeypatch.setattr(lib_mod, "_lib", None)
+    monkeypatch.setattr(lib_mod, "LIB_PATH", str(tmp_path / "absent.so"))
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        lib_mod.load()

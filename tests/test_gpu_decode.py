@@ -1,0 +1,280 @@
+"""GPU parity of the CUDA path (through the C ABI) against the reference's golden
+outputs and the CPU oracle.
+
+Tolerances (attention output, absolute): fp32 inputs max 1e-5; bf16/fp16 inputs
+max 2e-2 and mean 2e-3 against the fp32 reference on the same low-precision
+values. KV append and page indexing: bit-exact.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN_NAMES, load_golden, sha
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+TOL = {"float32": (1e-5, 1e-6), "bfloat16": (2e-2, 2e-3), "float16": (2e-2, 2e-3)}
+
+
+def close(out, ref, dtype):
+    err = np.abs(out.float().cpu().numpy().astype(np.float64) - ref)
+    mx, mean = TOL[dtype]
+    assert err.max() <= mx and err.mean() <= mean, (err.max(), err.mean())
+    return err
+
+
+def to_dev(t):
+    return {k: v.to(DEV) for k, v in t.items()}
+
+
+@pytest.mark.parametrize("schedule", ["auto", "balanced", "split"])
+@pytest.mark.parametrize("name", GOLDEN_NAMES)
+def test_golden_parity(name, schedule, pkg):
+    z, lay, t = load_golden(name)
+    d = to_dev(t)
+    pkg.kv_append(d["k_new"], d["v_new"], d["k_cache"], d["v_cache"], d["slot_mapping"])
+    out = pkg.paged_attention(d["q"], d["k_cache"], d["v_cache"], d["block_table"], d["context_lens"],
+                              lay.head_dim ** -0.5, schedule=schedule, split_pages=4)
+    torch.cuda.synchronize()
+    pkg.check_device_errors()
+    # append: the same bytes the reference's PagedKVCache.write_kv produced
+    assert sha(d["k_cache"].cpu()) == str(z["sha_k_after"])
+    assert sha(d["v_cache"].cpu()) == str(z["sha_v_after"])
+    close(out, z["out_ref"].astype(np.float64), str(z["dtype"]))
+
+
+def test_engine_signature_dropin(pkg):
+    """paged_decode_attention(q, k_pool, v_pool, block_tables, seq_lens, block_size)
+    as called at engine.py:221-224."""
+    z, lay, t = load_golden("correctness_fp32")
+    d = to_dev(t)
+    pkg.kv_append(d["k_new"], d["v_new"], d["k_cache"], d["v_cache"], d["slot_mapping"])
+    out = pkg.paged_decode_attention(d["q"], d["k_cache"], d["v_cache"], d["block_table"], d["context_lens"], 16)
+    assert out.dtype == d["q"].dtype and out.shape == d["q"].shape
+    close(out, z["out_ref"].astype(np.float64), "float32")
+    with pytest.raises(ValueError):
+        pkg.paged_decode_attention(d["q"], d["k_cache"], d["v_cache"], d["block_table"], d["context_lens"], 32)
+
+
+CASES = []
+for dtype in ("float32", "bfloat16", "float16"):
+    for heads in ((16, 8, 112), (16, 16, 64), (32, 8, 128), (16, 2, 64), (8, 8, 112)):
+        CASES.append((dtype, heads))
+
+
+@pytest.mark.parametrize("schedule", ["balanced", "split"])
+@pytest.mark.parametrize("dtype,heads", CASES)
+def test_random_parity(dtype, heads, schedule, pkg, oracle):
+    H, KVH, D = heads
+    wl = pkg.workloads
+    seed = 100 + 2 * CASES.index((dtype, heads)) + (schedule == "split")
+    lay = wl.layout_uniform(seed, 7, 1, 600, num_heads=H, num_kv_heads=KVH, head_dim=D)
+    t = wl.materialize_host(lay, seed, dtype=dtype, value_scale=0.7)
+    d = to_dev(t)
+    out = pkg.paged_attention(d["q"], d["k_cache"], d["v_cache"], d["block_table"], d["context_lens"], 0.3,
+                              schedule=schedule, split_pages=3)
+    ref, st = oracle.paged_decode_attention(t["q"], t["k_cache"], t["v_cache"], t["block_table"],
+                                            t["context_lens"], 0.3)
+    assert st == 0
+    close(out, ref, dtype)
+    pkg.check_device_errors()
+
+
+def test_edge_cases(pkg, oracle):
+    wl = pkg.workloads
+    ctx = np.array([1, 16, 17, 15, 32, 33, 0, 48, 1, 257], dtype=np.int32)
+    nb = 64
+    perm = wl.portable_permutation(9, 2, nb)
+    bt = np.full((ctx.shape[0], 24), -1, dtype=np.int32)
+    cur = 0
+    for b, c in enumerate(ctx):
+        n = (int(c) + 15) // 16
+        bt[b, :n] = perm[cur:cur + n]
+        cur += n
+    lay = wl.Layout(ctx, bt, nb)
+    t = wl.materialize_host(lay, 9, dtype="bfloat16")
+    d = to_dev(t)
+    for sched in ("balanced", "split"):
+        out = pkg.paged_attention(d["q"], d["k_cache"], d["v_cache"], d["block_table"], d["context_lens"],
+                                  schedule=sched, split_pages=1)
+        ref, st = oracle.paged_decode_attention(t["q"], t["k_cache"], t["v_cache"], t["block_table"],
+                                                t["context_lens"])
+        assert st == 1  # row 6 is empty: the reference would raise, the kernel writes zeros
+        close(out, ref, "bfloat16")
+        assert torch.count_nonzero(out[6]) == 0
+    pkg.check_device_errors()
+
+
+def test_single_long_sequence_spans_many_ctas(pkg, oracle):
+    wl = pkg.workloads
+    lay = wl.layout_uniform(21, 1, 9000, 9000)
+    t = wl.materialize_host(lay, 21, dtype="bfloat16")
+    d = to_dev(t)
+    out = pkg.paged_attention(d["q"], d["k_cache"], d["v_cache"], d["block_table"], d["context_lens"])
+    ref, st = oracle.paged_decode_attention(t["q"], t["k_cache"], t["v_cache"], t["block_table"], t["context_lens"])
+    close(out, ref, "bfloat16")
+
+
+def test_many_tiny_sequences_fewer_pages_than_ctas(pkg, oracle):
+    wl = pkg.workloads
+    lay = wl.layout_uniform(22, 40, 1, 16)  # 40 pages total, fewer than the CTAs
+    t = wl.materialize_host(lay, 22, dtype="float32")
+    d = to_dev(t)
+    out = pkg.paged_attention(d["q"], d["k_cache"], d["v_cache"], d["block_table"], d["context_lens"])
+    ref, _ = oracle.paged_decode_attention(t["q"], t["k_cache"], t["v_cache"], t["block_table"], t["context_lens"])
+    close(out, ref, "float32")
+
+
+def test_radix_shared_pages(pkg, oracle):
+    wl = pkg.workloads
+    lay = wl.layout_radix_prefix(23, batch=24, prefix_pages=20, suffix_lo=1, suffix_hi=100)
+    t = wl.materialize_host(lay, 23, dtype="bfloat16")
+    d = to_dev(t)
+    out = pkg.paged_attention(d["q"], d["k_cache"], d["v_cache"], d["block_table"], d["context_lens"])
+    ref, _ = oracle.paged_decode_attention(t["q"], t["k_cache"], t["v_cache"], t["block_table"], t["context_lens"])
+    close(out, ref, "bfloat16")
+
+
+def test_bad_page_is_flagged_not_faulted(pkg):
+    wl = pkg.workloads
+    lay = wl.layout_uniform(24, 4, 20, 60, num_blocks=32)
+    t = wl.materialize_host(lay, 24, dtype="bfloat16")
+    d = to_dev(t)
+    d["block_table"][1, 0] = 10_000          # outside the pool: the tile reads as zeros
+    d["block_table"][2, 0] = -1              # padding marker inside the context
+    pkg.paged_attention(d["q"], d["k_cache"], d["v_cache"], d["block_table"], d["context_lens"])
+    with pytest.raises(RuntimeError, match="page id outside the pool"):
+        pkg.check_device_errors()
+    # the workspace is re-armed: a clean call afterwards reports nothing
+    d = to_dev(t)
+    pkg.paged_attention(d["q"], d["k_cache"], d["v_cache"], d["block_table"], d["context_lens"])
+    pkg.check_device_errors()
+
+
+def test_context_longer_than_table_is_flagged(pkg):
+    wl = pkg.workloads
+    lay = wl.layout_uniform(25, 3, 20, 40, num_blocks=16)
+    t = wl.materialize_host(lay, 25, dtype="bfloat16")
+    d = to_dev(t)
+    d["context_lens"][0] = 16 * d["block_table"].shape[1] + 5
+    pkg.paged_attention(d["q"], d["k_cache"], d["v_cache"], d["block_table"], d["context_lens"])
+    with pytest.raises(RuntimeError, match="context longer"):
+        pkg.check_device_errors()
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16", "float16"])
+def test_kv_append_bit_exact(dtype, pkg, oracle):
+    wl = pkg.workloads
+    lay = wl.layout_uniform(26, 37, 1, 300)
+    t = wl.materialize_host(lay, 26, dtype=dtype)
+    sm = t["slot_mapping"].clone()
+    sm[3] = -1  # padding token: skipped
+    d = to_dev(t)
+    pkg.kv_append(d["k_new"], d["v_new"], d["k_cache"], d["v_cache"], sm.to(DEV))
+    kc, vc = t["k_cache"].clone(), t["v_cache"].clone()
+    assert oracle.kv_append(t["k_new"], t["v_new"], kc, vc, sm) == 0
+    assert torch.equal(d["k_cache"].cpu(), kc) and torch.equal(d["v_cache"].cpu(), vc)
+    pkg.check_device_errors()
+
+
+def test_kv_append_strided_rows(pkg, oracle):
+    """New rows taken as a view of a fused (T, 3, KVH, D) projection output."""
+    wl = pkg.workloads
+    lay = wl.layout_uniform(27, 9, 1, 100)
+    t = wl.materialize_host(lay, 27, dtype="bfloat16")
+    fused = torch.randn(9, 3, 8, 112, dtype=torch.bfloat16)
+    k_new, v_new = fused[:, 1], fused[:, 2]
+    d = to_dev(t)
+    fd = fused.to(DEV)
+    pkg.kv_append(fd[:, 1], fd[:, 2], d["k_cache"], d["v_cache"], d["slot_mapping"])
+    kc, vc = t["k_cache"].clone(), t["v_cache"].clone()
+    oracle.kv_append(k_new, v_new, kc, vc, t["slot_mapping"])
+    assert torch.equal(d["k_cache"].cpu(), kc) and torch.equal(d["v_cache"].cpu(), vc)
+
+
+def test_kv_append_bad_slot_flagged(pkg, oracle):
+    wl = pkg.workloads
+    lay = wl.layout_uniform(28, 4, 1, 50, num_blocks=8)
+    t = wl.materialize_host(lay, 28, dtype="bfloat16")
+    d = to_dev(t)
+    sm = t["slot_mapping"].clone()
+    sm[0] = 8 * 16 + 3                      # one past the pool: skipped and reported
+    pkg.kv_append(d["k_new"], d["v_new"], d["k_cache"], d["v_cache"], sm.to(DEV))
+    with pytest.raises(RuntimeError, match="slot outside"):
+        pkg.check_device_errors()
+    kc, vc = t["k_cache"].clone(), t["v_cache"].clone()
+    assert oracle.kv_append(t["k_new"], t["v_new"], kc, vc, sm) == 2
+    assert torch.equal(d["k_cache"].cpu(), kc) and torch.equal(d["v_cache"].cpu(), vc)
+
+
+def test_slot_mapping_kernel(pkg, oracle):
+    lay = pkg.workloads.named_layout("decode_760m")
+    bt = torch.from_numpy(lay.block_table).to(DEV)
+    pos = torch.from_numpy(lay.positions()).to(DEV)
+    sm = pkg.slot_mapping(bt, pos, 16)
+    ref, st = oracle.slot_mapping(lay.block_table, lay.positions(), 16)
+    assert np.array_equal(sm.cpu().numpy(), ref)
+
+
+def test_cuda_graph_capture(pkg):
+    wl = pkg.workloads
+    lay = wl.layout_uniform(29, 8, 100, 400)
+    t = wl.materialize_host(lay, 29, dtype="bfloat16")
+    d = to_dev(t)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        ref = pkg.paged_attention(d["q"], d["k_cache"], d["v_cache"], d["block_table"], d["context_lens"])
+        out = torch.empty_like(ref)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        pkg.paged_attention(d["q"], d["k_cache"], d["v_cache"], d["block_table"], d["context_lens"], out=out)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+
+
+def test_deterministic_and_page_relabel_invariant(pkg):
+    """Same inputs -> same bits; relabelling physical pages (pool permuted, table
+    remapped) changes nothing either: the kernel's arithmetic depends only on
+    the logical order of positions."""
+    wl = pkg.workloads
+    lay = wl.layout_uniform(30, 16, 200, 1500)
+    t = wl.materialize_host(lay, 30, dtype="bfloat16")
+    d = to_dev(t)
+    a = pkg.paged_attention(d["q"], d["k_cache"], d["v_cache"], d["block_table"], d["context_lens"])
+    b = pkg.paged_attention(d["q"], d["k_cache"], d["v_cache"], d["block_table"], d["context_lens"])
+    assert torch.equal(a, b)
+    perm = torch.randperm(lay.num_blocks, generator=torch.Generator().manual_seed(1)).to(DEV)
+    inv = torch.empty_like(perm)
+    inv[perm] = torch.arange(lay.num_blocks, device=DEV)
+    k2 = d["k_cache"][perm]          # new page p holds old page perm[p]
+    v2 = d["v_cache"][perm]
+    bt = d["block_table"].long()
+    bt2 = torch.where(bt >= 0, inv[bt.clamp(min=0)], bt).int()
+    c = pkg.paged_attention(d["q"], k2, v2, bt2, d["context_lens"])
+    assert torch.equal(a, c)
+
+
+@pytest.mark.parametrize("name", ["decode_760m", "long_context"])
+def test_full_size_sampled_rows_and_schedules(name, pkg, oracle):
+    """Full-size workloads: every schedule agrees, and sampled rows match the oracle."""
+    wl = pkg.workloads
+    spec = wl.NAMED[name]
+    lay = wl.named_layout(name, seed=0)
+    dev = wl.materialize_device(lay, 0, spec["dtype"], spec["scale_values"], num_layers=1)
+    q, kc, vc = dev["q"][0], dev["k_caches"][0], dev["v_caches"][0]
+    bt, cl = dev["block_table"], dev["context_lens"]
+    pkg.kv_append(dev["k_new"][0], dev["v_new"][0], kc, vc, dev["slot_mapping"])
+    a = pkg.paged_attention(q, kc, vc, bt, cl, schedule="balanced")
+    b = pkg.paged_attention(q, kc, vc, bt, cl, schedule="split", split_pages=32)
+    pkg.check_device_errors()
+    assert (a.float() - b.float()).abs().max().item() <= 2e-2
+    rows = np.unique(np.linspace(0, lay.batch - 1, 4).astype(int))
+    kch, vch = kc.cpu(), vc.cpu()
+    ref, st = oracle.paged_decode_attention(q[rows].cpu(), kch, vch, bt[rows].cpu(), cl[rows].cpu())
+    assert st == 0
+    close(a[rows], ref, spec["dtype"])

@@ -1,0 +1,46 @@
+"""unbox_b200: B200-native paged decode attention and KV append for the unbox.ai engine.
+
+The package directory is ``unbox.ai_b200/`` and it is imported under the name
+``unbox_b200`` (the directory name is not a Python identifier), e.g.::
+
+    import importlib.util, sys
+    spec = importlib.util.spec_from_file_location(
+        "unbox_b200", "<repo>/unbox.ai_b200/__init__.py",
+        submodule_search_locations=["<repo>/unbox.ai_b200"])
+    unbox_b200 = importlib.util.module_from_spec(spec)
+    sys.modules["unbox_b200"] = unbox_b200
+    spec.loader.exec_module(unbox_b200)
+
+Public API (mirrors unbox_platform/infer/kernels/paged_decode_attention.py and
+unbox_platform/infer/kvcache.py of the reference):
+
+* ``paged_decode_attention(q, k_pool, v_pool, block_tables, seq_lens, block_size)``
+  -- drop-in for the reference function of the same name (engine.py:221-224).
+* ``paged_attention(q, k_cache, v_cache, block_table, context_lens, scale)``
+  -- the same op with an explicit softmax scale.
+* ``kv_append(k_new, v_new, k_cache, v_cache, slot_mapping)`` -- batched
+  replacement for the per-sequence ``PagedKVCache.write_kv`` loop.
+* ``slot_mapping(block_table, positions, block_size)`` -- device-side slot
+  computation (kvcache.py:338-339) for one decode step.
+"""
+from . import workloads  # noqa: F401  (pure Python, no CUDA needed)
+
+__all__ = [
+    "paged_decode_attention", "paged_attention", "paged_attention_split", "kv_append",
+    "slot_mapping", "DecodeWorkspace", "workloads", "library", "sharding",
+]
+
+
+_OPS = ("paged_decode_attention", "paged_attention", "paged_attention_split", "kv_append", "slot_mapping",
+        "DecodeWorkspace", "check_device_errors", "workspace_for")
+
+
+def __getattr__(name):
+    # submodules that need torch / the CUDA library load lazily, so that the
+    # fixture generator and CPU-only host logic import without them
+    import importlib
+    if name in _OPS:
+        return getattr(importlib.import_module(__name__ + ".ops"), name)
+    if name in ("library", "sharding", "ops", "build"):
+        return importlib.import_module(__name__ + "." + name)
+    raise AttributeError(name)

@@ -1,0 +1,354 @@
+// C ABI of unbox_b200: argument validation, launch planning, TMA descriptor
+// encoding and the extern "C" entry points declared in include/unbox_b200.h.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "ubx_internal.h"
+#include "../../include/unbox_b200.h"
+
+namespace ubx {
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int status, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(UBX_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int dtype_bytes(int dtype) { return dtype == UBX_DTYPE_F32 ? 4 : 2; }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---- workspace layout (fixed prefix so that counters stay zero across calls)
+constexpr size_t kHeaderBytes = 256;                   // error word + reserved
+constexpr size_t kCounterEntries = 65536;              // merge counters, re-armed by the kernel
+constexpr size_t kCounterBytes = kCounterEntries * 4;  // zeroed once by ubx_workspace_init
+constexpr int kDefaultSplitPages = 32;                 // 512-token split-KV chunks
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct WsLayout {
+  size_t ml_off, o_off, total;
+  int64_t slots;
+};
+
+WsLayout ws_layout(int64_t slots, int num_heads, int head_dim) {
+  WsLayout w;
+  w.slots = slots;
+  w.ml_off = kHeaderBytes + kCounterBytes;
+  w.o_off = w.ml_off + align256((size_t)slots * num_heads * sizeof(float2));
+  w.total = w.o_off + (size_t)slots * num_heads * head_dim * sizeof(float);
+  return w;
+}
+
+int num_sms_current_device(int* n) {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev >= 0 && dev < 64 && cache[dev] > 0) {
+    *n = cache[dev];
+    return UBX_OK;
+  }
+  int sms = 0;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(MultiProcessorCount)");
+  if (dev >= 0 && dev < 64) cache[dev] = sms;
+  *n = sms;
+  return UBX_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Tensor map over one per-layer K or V pool: dims (D, token, head, page) with
+// element strides (1, c_s_tok, c_s_head, c_s_block); box (D, 16, HG, 1).
+int encode_pool_map(CUtensorMap* map, const void* base, int dtype, int head_dim, int block_size, int kv_heads,
+                    int64_t num_blocks, int64_t s_tok, int64_t s_head, int64_t s_block, int heads_per_cta) {
+  auto fn = encode_fn();
+  if (!fn) return fail(UBX_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const int es = dtype_bytes(dtype);
+  CUtensorMapDataType dt = dtype == UBX_DTYPE_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                           : dtype == UBX_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[4] = {(cuuint64_t)head_dim, (cuuint64_t)block_size, (cuuint64_t)kv_heads, (cuuint64_t)num_blocks};
+  cuuint64_t strides[3] = {(cuuint64_t)(s_tok * es), (cuuint64_t)(s_head * es), (cuuint64_t)(s_block * es)};
+  cuuint32_t box[4] = {(cuuint32_t)head_dim, (cuuint32_t)block_size, (cuuint32_t)heads_per_cta, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(UBX_ERR_INVALID_ARGUMENT, "cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
+  return UBX_OK;
+}
+
+struct Plan {
+  int gw, wpk, hg, n_hg, stages, smem;
+  bool balanced;
+  int split_pages, max_chunks;
+  dim3 grid, block;
+  int64_t slots;
+};
+
+int make_plan(int batch, int num_heads, int num_kv_heads, int head_dim, int dtype, int max_blocks, int schedule,
+              int split_pages, int num_sms, Plan* pl) {
+  const int G = num_heads / num_kv_heads;
+  const int es = dtype_bytes(dtype);
+  pl->gw = G < 2 ? G : 2;
+  pl->wpk = G / pl->gw;
+  pl->hg = 1;
+  for (int hg = num_kv_heads; hg >= 1; --hg) {
+    if (num_kv_heads % hg) continue;
+    if (hg * pl->wpk > kMaxConsumerWarps) continue;
+    if (kBlockSize * hg * head_dim * es > kMaxTileBytes) continue;
+    pl->hg = hg;
+    break;
+  }
+  pl->n_hg = num_kv_heads / pl->hg;
+  const bool can_balance = batch <= kMaxBatchSmem && (int64_t)batch * num_kv_heads * pl->wpk <= (int64_t)kCounterEntries;
+  if (schedule == UBX_SCHEDULE_BALANCED && !can_balance)
+    return fail(UBX_ERR_UNSUPPORTED, "balanced schedule needs batch <= %d (got %d)", kMaxBatchSmem, batch);
+  pl->balanced = schedule == UBX_SCHEDULE_BALANCED || (schedule == UBX_SCHEDULE_AUTO && can_balance);
+  pl->split_pages = split_pages > 0 ? split_pages : kDefaultSplitPages;
+  pl->max_chunks = (max_blocks + pl->split_pages - 1) / pl->split_pages;
+  const int tile = kBlockSize * pl->hg * head_dim * es;
+  const int fixed = decode_smem_bytes(es, head_dim, pl->hg, pl->wpk, pl->gw, 0, pl->balanced ? batch + 1 : 0);
+  pl->stages = std::min(6, (kSmemLimit - fixed) / (2 * tile));
+  if (pl->stages < 2) return fail(UBX_ERR_UNSUPPORTED, "shared memory too small for a 2-stage pipeline");
+  pl->smem = decode_smem_bytes(es, head_dim, pl->hg, pl->wpk, pl->gw, pl->stages, pl->balanced ? batch + 1 : 0);
+  pl->block = dim3((pl->hg * pl->wpk + 1) * 32);
+  if (pl->balanced) {
+    pl->grid = dim3(std::max(1, num_sms / pl->n_hg), pl->n_hg);
+    pl->slots = 2 * (int64_t)pl->grid.x;
+  } else {
+    pl->grid = dim3((unsigned)((int64_t)batch * pl->max_chunks), pl->n_hg);
+    pl->slots = (int64_t)batch * pl->max_chunks;
+  }
+  return UBX_OK;
+}
+
+int check_shape(int num_heads, int num_kv_heads, int head_dim, int block_size, int dtype) {
+  if (dtype != UBX_DTYPE_F32 && dtype != UBX_DTYPE_BF16 && dtype != UBX_DTYPE_F16)
+    return fail(UBX_ERR_INVALID_ARGUMENT, "unknown dtype code %d", dtype);
+  if (num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads)
+    return fail(UBX_ERR_INVALID_ARGUMENT, "num_heads (%d) must be a positive multiple of num_kv_heads (%d)",
+                num_heads, num_kv_heads);
+  const int G = num_heads / num_kv_heads;
+  if (G != 1 && G != 2 && G != 4 && G != 8)
+    return fail(UBX_ERR_UNSUPPORTED, "GQA ratio %d not built (1, 2, 4, 8)", G);
+  if (head_dim != 64 && head_dim != 112 && head_dim != 128)
+    return fail(UBX_ERR_UNSUPPORTED, "head_dim %d not built (64, 112, 128)", head_dim);
+  if (block_size != kBlockSize) return fail(UBX_ERR_UNSUPPORTED, "block_size %d not built (16)", block_size);
+  return UBX_OK;
+}
+
+}  // namespace
+}  // namespace ubx
+
+using namespace ubx;
+
+extern "C" {
+
+const char* ubx_status_string(int status) {
+  switch (status) {
+    case UBX_OK: return "ok";
+    case UBX_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case UBX_ERR_UNSUPPORTED: return "unsupported configuration";
+    case UBX_ERR_WORKSPACE: return "workspace missing or too small";
+    case UBX_ERR_CUDA: return "CUDA error";
+    default: return "unknown status";
+  }
+}
+
+const char* ubx_last_error(void) { return g_last_error.c_str(); }
+
+int ubx_version(void) { return 100; }
+
+int ubx_kv_append(const void* k_new, const void* v_new, int64_t new_s_tok, int64_t new_s_head, void* k_cache,
+                  void* v_cache, int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head, const int64_t* slot_mapping,
+                  int64_t num_tokens, int num_kv_heads, int head_dim, int block_size, int64_t num_blocks, int dtype,
+                  int32_t* error_word, void* stream) {
+  g_last_error.clear();
+  if (dtype != UBX_DTYPE_F32 && dtype != UBX_DTYPE_BF16 && dtype != UBX_DTYPE_F16)
+    return fail(UBX_ERR_INVALID_ARGUMENT, "unknown dtype code %d", dtype);
+  if (num_tokens < 0 || num_kv_heads <= 0 || head_dim <= 0 || block_size <= 0 || num_blocks <= 0)
+    return fail(UBX_ERR_INVALID_ARGUMENT, "non-positive size");
+  if (num_tokens == 0) return UBX_OK;
+  if (!k_new || !v_new || !k_cache || !v_cache || !slot_mapping)
+    return fail(UBX_ERR_INVALID_ARGUMENT, "null pointer");
+  const int es = dtype_bytes(dtype);
+  const int row = head_dim * es;
+  // widest copy unit that every address and stride allows
+  int vec = 16;
+  auto ok_for = [&](int v) {
+    auto a = [&](const void* p) { return (reinterpret_cast<uintptr_t>(p) % v) == 0; };
+    auto s = [&](int64_t st) { return ((st * es) % v) == 0; };
+    return row % v == 0 && a(k_new) && a(v_new) && a(k_cache) && a(v_cache) && s(new_s_tok) && s(new_s_head) &&
+           s(c_s_block) && s(c_s_tok) && s(c_s_head);
+  };
+  while (vec > es && !ok_for(vec)) vec >>= 1;
+  if (!ok_for(vec)) return fail(UBX_ERR_INVALID_ARGUMENT, "misaligned K/V row");
+  cudaError_t e = launch_kv_append(k_new, v_new, new_s_tok * es, new_s_head * es, k_cache, v_cache, c_s_block * es,
+                                   c_s_tok * es, c_s_head * es, slot_mapping, num_tokens, num_kv_heads, row,
+                                   block_size, num_blocks, vec, error_word, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "kv_append launch");
+  return UBX_OK;
+}
+
+int ubx_slot_mapping(const int32_t* block_table, int64_t bt_s_row, const int32_t* positions, int64_t* slot_mapping,
+                     int batch, int max_blocks_per_seq, int block_size, void* stream) {
+  g_last_error.clear();
+  if (batch < 0 || block_size <= 0 || max_blocks_per_seq < 0) return fail(UBX_ERR_INVALID_ARGUMENT, "bad size");
+  if (batch == 0) return UBX_OK;
+  if (!block_table || !positions || !slot_mapping) return fail(UBX_ERR_INVALID_ARGUMENT, "null pointer");
+  cudaError_t e = launch_slot_mapping(block_table, bt_s_row, positions, slot_mapping, batch, max_blocks_per_seq,
+                                      block_size, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "slot_mapping launch");
+  return UBX_OK;
+}
+
+int ubx_paged_decode_workspace_size(int batch, int num_heads, int head_dim, int max_blocks_per_seq, int split_pages,
+                                    size_t* bytes) {
+  g_last_error.clear();
+  if (!bytes || batch < 0 || num_heads <= 0 || head_dim <= 0 || max_blocks_per_seq < 0)
+    return fail(UBX_ERR_INVALID_ARGUMENT, "bad workspace size query");
+  int sms = 0;
+  int st = num_sms_current_device(&sms);
+  if (st != UBX_OK) return st;
+  const int sp = split_pages > 0 ? split_pages : kDefaultSplitPages;
+  const int64_t chunks = (max_blocks_per_seq + sp - 1) / sp;
+  const int64_t slots = std::max<int64_t>(2 * (int64_t)sms, (int64_t)batch * chunks);
+  *bytes = ws_layout(slots, num_heads, head_dim).total;
+  return UBX_OK;
+}
+
+int ubx_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  if (!workspace || workspace_bytes < kHeaderBytes + kCounterBytes)
+    return fail(UBX_ERR_WORKSPACE, "workspace smaller than its fixed header (%zu bytes)", kHeaderBytes + kCounterBytes);
+  cudaError_t e = cudaMemsetAsync(workspace, 0, kHeaderBytes + kCounterBytes, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "workspace memset");
+  return UBX_OK;
+}
+
+int ubx_read_device_error(const void* workspace, int32_t* value, int clear, void* stream) {
+  g_last_error.clear();
+  if (!workspace || !value) return fail(UBX_ERR_INVALID_ARGUMENT, "null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(value, workspace, sizeof(int32_t), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess && clear) e = cudaMemsetAsync(const_cast<void*>(workspace), 0, sizeof(int32_t), s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "read device error word");
+  return UBX_OK;
+}
+
+int ubx_paged_decode_attention(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache, const void* v_cache,
+                               int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head, const int32_t* block_table,
+                               int64_t bt_s_row, const int32_t* context_lens, void* out, int64_t o_s_b, int64_t o_s_h,
+                               int batch, int num_heads, int num_kv_heads, int head_dim, int block_size,
+                               int64_t num_blocks, int max_blocks_per_seq, float scale, int dtype, int schedule,
+                               int split_pages, void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  int st = check_shape(num_heads, num_kv_heads, head_dim, block_size, dtype);
+  if (st != UBX_OK) return st;
+  if (batch < 0) return fail(UBX_ERR_INVALID_ARGUMENT, "negative batch");
+  if (batch == 0) return UBX_OK;
+  if (schedule != UBX_SCHEDULE_AUTO && schedule != UBX_SCHEDULE_BALANCED && schedule != UBX_SCHEDULE_SPLIT)
+    return fail(UBX_ERR_INVALID_ARGUMENT, "unknown schedule %d", schedule);
+  if (!q || !k_cache || !v_cache || !block_table || !context_lens || !out)
+    return fail(UBX_ERR_INVALID_ARGUMENT, "null pointer");
+  if (num_blocks <= 0 || num_blocks > (int64_t)0x7fffffff)
+    return fail(UBX_ERR_INVALID_ARGUMENT, "num_blocks %lld out of range", (long long)num_blocks);
+  if (max_blocks_per_seq <= 0) return fail(UBX_ERR_INVALID_ARGUMENT, "max_blocks_per_seq must be positive");
+  const int es = dtype_bytes(dtype);
+  auto m16 = [&](int64_t s) { return ((s * es) & 15) == 0; };
+  if (!aligned16(q) || !aligned16(out) || !m16(q_s_b) || !m16(q_s_h) || !m16(o_s_b) || !m16(o_s_h))
+    return fail(UBX_ERR_INVALID_ARGUMENT, "q/out rows must be 16-byte aligned");
+  if (!aligned16(k_cache) || !aligned16(v_cache) || !m16(c_s_block) || !m16(c_s_tok) || !m16(c_s_head))
+    return fail(UBX_ERR_INVALID_ARGUMENT, "K/V cache base and strides must be multiples of 16 bytes (TMA)");
+  if (!(scale > 0.f) && !(scale < 0.f)) return fail(UBX_ERR_INVALID_ARGUMENT, "scale must be finite and non-zero");
+  if (!workspace) return fail(UBX_ERR_WORKSPACE, "workspace is required");
+
+  int sms = 0;
+  st = num_sms_current_device(&sms);
+  if (st != UBX_OK) return st;
+  Plan pl;
+  st = make_plan(batch, num_heads, num_kv_heads, head_dim, dtype, max_blocks_per_seq, schedule, split_pages, sms, &pl);
+  if (st != UBX_OK) return st;
+  const WsLayout wl = ws_layout(pl.slots, num_heads, head_dim);
+  if (workspace_bytes < wl.total)
+    return fail(UBX_ERR_WORKSPACE, "workspace of %zu bytes, this call needs %zu", workspace_bytes, wl.total);
+
+  CUtensorMap tk, tv;
+  st = encode_pool_map(&tk, k_cache, dtype, head_dim, block_size, num_kv_heads, num_blocks, c_s_tok, c_s_head,
+                       c_s_block, pl.hg);
+  if (st != UBX_OK) return st;
+  st = encode_pool_map(&tv, v_cache, dtype, head_dim, block_size, num_kv_heads, num_blocks, c_s_tok, c_s_head,
+                       c_s_block, pl.hg);
+  if (st != UBX_OK) return st;
+
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  DecodeParams p;
+  p.q = q;
+  p.q_sb = q_s_b;
+  p.q_sh = q_s_h;
+  p.out = out;
+  p.o_sb = o_s_b;
+  p.o_sh = o_s_h;
+  p.block_table = block_table;
+  p.bt_sb = bt_s_row;
+  p.context_lens = context_lens;
+  p.batch = batch;
+  p.num_heads = num_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.max_blocks = max_blocks_per_seq;
+  p.num_blocks = num_blocks;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.heads_per_cta = pl.hg;
+  p.warps_per_kv = pl.wpk;
+  p.stages = pl.stages;
+  p.split_pages = pl.split_pages;
+  p.max_chunks = pl.max_chunks;
+  p.part_o = reinterpret_cast<float*>(ws + wl.o_off);
+  p.part_ml = reinterpret_cast<float2*>(ws + wl.ml_off);
+  p.counters = reinterpret_cast<int32_t*>(ws + kHeaderBytes);
+  p.error = reinterpret_cast<int32_t*>(ws);
+
+  LaunchShape shape{pl.grid, pl.block, pl.smem};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = launch_paged_decode(dtype, head_dim, pl.gw, pl.balanced, tk, tv, p, shape, s);
+  if (e != cudaSuccess) return cuda_fail(e, "paged_decode launch");
+  if (!pl.balanced) {
+    e = launch_lse_combine(dtype, head_dim, p, s);
+    if (e != cudaSuccess) return cuda_fail(e, "lse_combine launch");
+  }
+  return UBX_OK;
+}
+
+}  // extern "C"

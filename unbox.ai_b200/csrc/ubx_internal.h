@@ -1,0 +1,69 @@
+// Internal launch interface between the C ABI (capi.cu) and the kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ubx {
+
+constexpr int kBlockSize = 16;          // tokens per page (configs/infer/serve.yaml block_size)
+constexpr int kMaxStages = 8;           // pipeline depth limit (mbarrier slots reserved)
+constexpr int kMaxConsumerWarps = 8;    // consumer warps per CTA
+constexpr int kMaxBatchSmem = 2048;     // balanced schedule keeps a (B+1) page prefix in smem
+constexpr int kMaxTileBytes = 32768;    // one K (or V) page tile of a head group
+constexpr int kSmemLimit = 226 * 1024;  // dynamic smem budget: 227 KB opt-in minus static smem and slack
+
+struct DecodeParams {
+  const void* q;
+  int64_t q_sb, q_sh;
+  void* out;
+  int64_t o_sb, o_sh;
+  const int32_t* block_table;
+  int64_t bt_sb;
+  const int32_t* context_lens;
+  int batch;
+  int num_heads;
+  int num_kv_heads;
+  int max_blocks;
+  int64_t num_blocks;
+  float scale_log2;      // softmax scale * log2(e): scores live in the exp2 domain
+  int heads_per_cta;     // KV heads in one page tile (HG)
+  int warps_per_kv;      // consumer warps sharing one KV head (WPK = G / GW)
+  int stages;            // pipeline depth
+  int split_pages;       // split schedule: pages per chunk
+  int max_chunks;        // split schedule: chunk slots per sequence
+  float* part_o;         // [slots][num_heads][D] unnormalised partial outputs
+  float2* part_ml;       // [slots][num_heads] (running max in log2 units, denominator)
+  int32_t* counters;     // [batch][num_kv_heads * warps_per_kv] merge counters (balanced)
+  int32_t* error;        // device error word
+};
+
+struct LaunchShape {
+  dim3 grid;
+  dim3 block;
+  int smem_bytes;
+};
+
+// Shared-memory bytes the decode kernel needs (stage ring + softmax buffers +
+// barriers + optional page prefix).
+int decode_smem_bytes(int dtype_bytes, int head_dim, int heads_per_cta, int warps_per_kv, int gw, int stages,
+                      int prefix_entries);
+
+cudaError_t launch_paged_decode(int dtype, int head_dim, int gw, bool balanced, const CUtensorMap& tmap_k,
+                                const CUtensorMap& tmap_v, const DecodeParams& p, const LaunchShape& shape,
+                                cudaStream_t stream);
+
+cudaError_t launch_lse_combine(int dtype, int head_dim, const DecodeParams& p, cudaStream_t stream);
+
+cudaError_t launch_kv_append(const void* k_new, const void* v_new, int64_t n_stok_b, int64_t n_sh_b, void* k_cache,
+                             void* v_cache, int64_t c_sblk_b, int64_t c_stok_b, int64_t c_sh_b,
+                             const int64_t* slots, int64_t num_tokens, int num_kv_heads, int row_bytes,
+                             int block_size, int64_t num_blocks, int vec_bytes, int32_t* error_word,
+                             cudaStream_t stream);
+
+cudaError_t launch_slot_mapping(const int32_t* block_table, int64_t bt_s_row, const int32_t* positions,
+                                int64_t* slot_mapping, int batch, int max_blocks, int block_size,
+                                cudaStream_t stream);
+
+}  // namespace ubx
