@@ -7,8 +7,9 @@
  * pointers unless stated otherwise; strides are in ELEMENTS; the innermost
  * (head_dim) dimension of every tensor is contiguous. Every call is
  * asynchronous on `stream` (a cudaStream_t passed as void*, NULL = legacy
- * default stream), allocates nothing, and never synchronises the host, so a
- * decode step made of these calls can be captured in a CUDA graph.
+ * default stream), allocates nothing, and never synchronises the host (except
+ * ubx_read_device_error); a decode step made of ubx_slot_mapping, ubx_kv_append
+ * and ubx_paged_decode_attention calls can be captured in a CUDA graph.
  *
  * Return value: UBX_OK or a UBX_ERR_* status for host-side validation and
  * launch failures (ubx_last_error() gives the message). Data-dependent problems
@@ -124,6 +125,35 @@ int ubx_paged_decode_attention(const void* q, int64_t q_s_b, int64_t q_s_h, cons
                                int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
                                int max_blocks_per_seq, float scale, int dtype, int schedule, int split_pages,
                                void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Allocation-free variant of ubx_paged_decode_attention. No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory -- an
+ * engine that gives all free HBM to its own KV pool at start-up and owns every
+ * later allocation, or a binding from another language that holds only the
+ * input and output buffers and no device allocator. Same arguments and results
+ * as ubx_paged_decode_attention, minus the workspace: the scratch lives in a
+ * fixed 8 MiB array inside the library (every GPU that loads the library holds
+ * it until the process exits). Sizes whose scratch would exceed it are rejected
+ * with UBX_ERR_WORKSPACE and a message naming the limit (on a 148-SM B200 the
+ * balanced schedule needs about 2.3 MiB in all at 16 heads of 112; the split
+ * schedule needs batch * ceil(max_blocks_per_seq / split_pages) * num_heads *
+ * (4*head_dim + 8) bytes beyond the 256 KiB counter prefix). The call itself
+ * allocates nothing.
+ * The first call on each device looks up the array's device address (with that
+ * device current); make that first call before any stream capture. Every call
+ * shares the one array per device and clears its counters and error word on
+ * `stream` before launching, so calls that overlap on the GPU (other streams,
+ * other host threads) race and must be serialised by the caller.
+ *   error_word: optional device int32 that receives the call's UBX_DEVERR_* bits.
+ */
+int ubx_paged_decode_attention_noalloc(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache,
+                                       const void* v_cache, int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head,
+                                       const int32_t* block_table, int64_t bt_s_row, const int32_t* context_lens,
+                                       void* out, int64_t o_s_b, int64_t o_s_h, int batch, int num_heads,
+                                       int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
+                                       int max_blocks_per_seq, float scale, int dtype, int schedule, int split_pages,
+                                       int32_t* error_word, void* stream);
 
 /*
  * Read (and optionally clear) the device error word of a workspace. This one

@@ -37,9 +37,9 @@ int dtype_bytes(int dtype) { return dtype == UBX_DTYPE_F32 ? 4 : 2; }
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // ---- workspace layout (fixed prefix so that counters stay zero across calls)
-constexpr size_t kHeaderBytes = 256;                   // error word + reserved
-constexpr size_t kCounterEntries = 65536;              // merge counters, re-armed by the kernel
-constexpr size_t kCounterBytes = kCounterEntries * 4;  // zeroed once by ubx_workspace_init
+constexpr size_t kHeaderBytes = kWsHeaderBytes;        // error word + reserved
+constexpr size_t kCounterEntries = kWsCounterEntries;  // merge counters, re-armed by the kernel
+constexpr size_t kCounterBytes = kWsCounterBytes;      // zeroed once by ubx_workspace_init
 constexpr int kDefaultSplitPages = 32;                 // 512-token split-KV chunks
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -169,6 +169,10 @@ int check_shape(int num_heads, int num_kv_heads, int head_dim, int block_size, i
 }
 
 }  // namespace
+
+void set_last_error(const char* msg) { g_last_error = msg; }
+const char* last_error() { return g_last_error.c_str(); }
+
 }  // namespace ubx
 
 using namespace ubx;

@@ -14,6 +14,11 @@ constexpr int kMaxBatchSmem = 2048;     // balanced schedule keeps a (B+1) page 
 constexpr int kMaxTileBytes = 32768;    // one K (or V) page tile of a head group
 constexpr int kSmemLimit = 226 * 1024;  // dynamic smem budget: 227 KB opt-in minus static smem and slack
 
+// Workspace layout prefix: [error word + reserved | merge counters | partials].
+constexpr size_t kWsHeaderBytes = 256;                      // error word at offset 0
+constexpr size_t kWsCounterEntries = 65536;                 // balanced-schedule merge counters
+constexpr size_t kWsCounterBytes = kWsCounterEntries * 4;   // must be zero before a call
+
 struct DecodeParams {
   const void* q;
   int64_t q_sb, q_sh;
@@ -38,6 +43,10 @@ struct DecodeParams {
   int32_t* counters;     // [batch][num_kv_heads * warps_per_kv] merge counters (balanced)
   int32_t* error;        // device error word
 };
+
+// Message returned by ubx_last_error() on this host thread (set by any entry point).
+void set_last_error(const char* msg);
+const char* last_error();
 
 struct LaunchShape {
   dim3 grid;
