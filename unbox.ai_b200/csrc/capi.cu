@@ -91,7 +91,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // Tensor map over one per-layer K or V pool: dims (D, token, head, page) with
 // element strides (1, c_s_tok, c_s_head, c_s_block); box (D, 16, HG, 1).
 int encode_pool_map(CUtensorMap* map, const void* base, int dtype, int head_dim, int block_size, int kv_heads,
-                    int64_t num_blocks, int64_t s_tok, int64_t s_head, int64_t s_block, int heads_per_cta) {
+                    int64_t num_blocks, int64_t s_tok, int64_t s_head, int64_t s_block, int heads_per_cta,
+                    int box_inner) {
   auto fn = encode_fn();
   if (!fn) return fail(UBX_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   const int es = dtype_bytes(dtype);
@@ -100,7 +101,9 @@ int encode_pool_map(CUtensorMap* map, const void* base, int dtype, int head_dim,
                                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   cuuint64_t dims[4] = {(cuuint64_t)head_dim, (cuuint64_t)block_size, (cuuint64_t)kv_heads, (cuuint64_t)num_blocks};
   cuuint64_t strides[3] = {(cuuint64_t)(s_tok * es), (cuuint64_t)(s_head * es), (cuuint64_t)(s_block * es)};
-  cuuint32_t box[4] = {(cuuint32_t)head_dim, (cuuint32_t)block_size, (cuuint32_t)heads_per_cta, 1};
+  // box_inner >= head_dim: the columns past head_dim are outside the tensor and
+  // TMA fills them with zeros (row padding in shared memory, no DRAM traffic)
+  cuuint32_t box[4] = {(cuuint32_t)box_inner, (cuuint32_t)block_size, (cuuint32_t)heads_per_cta, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = fn(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -109,7 +112,7 @@ int encode_pool_map(CUtensorMap* map, const void* base, int dtype, int head_dim,
 }
 
 struct Plan {
-  int gw, wpk, hg, n_hg, stages, smem;
+  int gw, wpk, hg, n_hg, stages, smem, pitch, tile, pbuf;
   bool balanced;
   int split_pages, max_chunks;
   dim3 grid, block;
@@ -120,13 +123,15 @@ int make_plan(int batch, int num_heads, int num_kv_heads, int head_dim, int dtyp
               int split_pages, int num_sms, Plan* pl) {
   const int G = num_heads / num_kv_heads;
   const int es = dtype_bytes(dtype);
-  pl->gw = G < 2 ? G : 2;
-  pl->wpk = G / pl->gw;
+  const bool mma = es == 2;  // 16-bit: tensor-core consumer, one warp per KV head
+  pl->gw = mma ? G : (G < 2 ? G : 2);
+  pl->wpk = mma ? 1 : G / pl->gw;
+  pl->pitch = mma ? mma_row_pitch(head_dim) : head_dim;
   pl->hg = 1;
   for (int hg = num_kv_heads; hg >= 1; --hg) {
     if (num_kv_heads % hg) continue;
     if (hg * pl->wpk > kMaxConsumerWarps) continue;
-    if (kBlockSize * hg * head_dim * es > kMaxTileBytes) continue;
+    if (kBlockSize * hg * pl->pitch * es > kMaxTileBytes) continue;
     pl->hg = hg;
     break;
   }
@@ -137,11 +142,13 @@ int make_plan(int batch, int num_heads, int num_kv_heads, int head_dim, int dtyp
   pl->balanced = schedule == UBX_SCHEDULE_BALANCED || (schedule == UBX_SCHEDULE_AUTO && can_balance);
   pl->split_pages = split_pages > 0 ? split_pages : kDefaultSplitPages;
   pl->max_chunks = (max_blocks + pl->split_pages - 1) / pl->split_pages;
-  const int tile = kBlockSize * pl->hg * head_dim * es;
-  const int fixed = decode_smem_bytes(es, head_dim, pl->hg, pl->wpk, pl->gw, 0, pl->balanced ? batch + 1 : 0);
-  pl->stages = std::min(6, (kSmemLimit - fixed) / (2 * tile));
+  pl->tile = kBlockSize * pl->hg * pl->pitch * es;
+  pl->pbuf = mma ? 0 : ((pl->hg * pl->wpk * pl->gw * kBlockSize * 4 + 15) & ~15);
+  const int prefix = pl->balanced ? batch + 1 : 0;
+  const int fixed = decode_smem_bytes(pl->tile, pl->pbuf, 0, prefix);
+  pl->stages = std::min(6, (kSmemLimit - fixed) / (2 * pl->tile));
   if (pl->stages < 2) return fail(UBX_ERR_UNSUPPORTED, "shared memory too small for a 2-stage pipeline");
-  pl->smem = decode_smem_bytes(es, head_dim, pl->hg, pl->wpk, pl->gw, pl->stages, pl->balanced ? batch + 1 : 0);
+  pl->smem = decode_smem_bytes(pl->tile, pl->pbuf, pl->stages, prefix);
   pl->block = dim3((pl->hg * pl->wpk + 1) * 32);
   if (pl->balanced) {
     pl->grid = dim3(std::max(1, num_sms / pl->n_hg), pl->n_hg);
@@ -311,10 +318,10 @@ int ubx_paged_decode_attention(const void* q, int64_t q_s_b, int64_t q_s_h, cons
 
   CUtensorMap tk, tv;
   st = encode_pool_map(&tk, k_cache, dtype, head_dim, block_size, num_kv_heads, num_blocks, c_s_tok, c_s_head,
-                       c_s_block, pl.hg);
+                       c_s_block, pl.hg, pl.pitch);
   if (st != UBX_OK) return st;
   st = encode_pool_map(&tv, v_cache, dtype, head_dim, block_size, num_kv_heads, num_blocks, c_s_tok, c_s_head,
-                       c_s_block, pl.hg);
+                       c_s_block, pl.hg, pl.pitch);
   if (st != UBX_OK) return st;
 
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -334,6 +341,8 @@ int ubx_paged_decode_attention(const void* q, int64_t q_s_b, int64_t q_s_h, cons
   p.max_blocks = max_blocks_per_seq;
   p.num_blocks = num_blocks;
   p.scale_log2 = scale * 1.4426950408889634f;
+  p.tile_bytes = pl.tile;
+  p.pbuf_bytes = pl.pbuf;
   p.heads_per_cta = pl.hg;
   p.warps_per_kv = pl.wpk;
   p.stages = pl.stages;

@@ -15,11 +15,16 @@
 //   * Warp NCW is the producer: it walks the CTA's pages, reads the block table
 //     32 entries at a time and issues the two TMA loads per page into a ring of
 //     `stages` buffers guarded by full/empty mbarriers.
-//   * Consumer warp w owns KV head w / WPK of the head group and GW (<= 2) of
-//     its query heads, so a K/V row is read from shared memory once for the GQA
-//     group. QK: two lanes per token, each holding half of q in registers.
-//     Online softmax in the exp2 domain (scale * log2 e folded into q) with
-//     warp-shuffle max. PV: lane = (16-byte chunk of D, token group).
+//   * bf16 / fp16: consumer warp w owns KV head w of the head group with all of
+//     its query heads as the rows of one tensor-core tile (mma m16n8k16 fed by
+//     ldmatrix from the TMA tiles); QK's accumulator fragments are reused as
+//     the P operand of PV, online softmax runs on them with two shuffles per row.
+//     The TMA box is padded to an odd number of 16-byte chunks per row (the pad
+//     is filled by TMA's out-of-bounds zero fill, no extra DRAM reads) so that
+//     ldmatrix rows fall in distinct banks.
+//   * fp32: CUDA-core consumer, warp = (KV head, <= 2 query heads): QK with two
+//     lanes per token holding half of q in registers, PV with lane = (16-byte
+//     chunk of D, token group).
 //   * Work split: the balanced schedule gives every CTA the same number of
 //     pages of the flattened (sequence, page) list, so a CTA may cover the tail
 //     of one sequence, whole sequences and the head of another. A sequence
@@ -249,166 +254,249 @@ __device__ __forceinline__ void page_update(const T* __restrict__ kt, const T* _
   __syncwarp();
 }
 
-}  // namespace
+// ---------------------------------------------------------------- tensor-core helpers
 
-template <typename T, int D, int GW, bool BALANCED>
-__global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
-    paged_decode_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
-                        const DecodeParams p) {
+// ldmatrix: four 8x8 b16 matrices, row addresses supplied by lanes 8i..8i+7.
+__device__ __forceinline__ void ldsm_x4(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_u32(p)));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                              uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_u32(p)));
+}
+
+// D(16x8, f32) += A(16x16) * B(16x8), A row-major, B column-major, 16-bit inputs.
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1);
+
+template <>
+__device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                                        uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <>
+__device__ __forceinline__ void mma16816<__half>(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                 uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ---------------------------------------------------------------- shared CTA plumbing
+
+struct Work {
+  int g_begin, g_end, b_first, w_eff, total, chunk, n_split;
+};
+
+struct Seg {
+  int b, s0, s1, lp0, lp1;
+};
+
+struct Smem {
+  uint8_t* stages;
+  float* p_buf;
+  uint64_t* full_bar;
+  uint64_t* empty_bar;
+  int32_t* prefix;
+};
+
+__device__ __forceinline__ Smem carve_smem(uint8_t* smem, const DecodeParams& p) {
+  Smem s;
+  const int stage_bytes = 2 * p.tile_bytes;
+  s.stages = smem;
+  s.p_buf = reinterpret_cast<float*>(smem + p.stages * stage_bytes);
+  s.full_bar = reinterpret_cast<uint64_t*>(smem + p.stages * stage_bytes + p.pbuf_bytes);
+  s.empty_bar = s.full_bar + kMaxStages;
+  s.prefix = reinterpret_cast<int32_t*>(s.empty_bar + kMaxStages);
+  return s;
+}
+
+// Pages this CTA streams: a contiguous range of the flattened (sequence, page)
+// list (balanced) or one chunk of one sequence (split). Rows with no context
+// are written as zeros here. Ends with a CTA barrier (publishes mbarrier init).
+template <typename T, int D, bool BAL>
+__device__ Work setup_work(const DecodeParams& p, const Smem& sm, int32_t* warp_tot, int head_lo, int head_hi) {
+  Work w{0, 0, 0, 1, 0, 0, 0};
+  const int B = p.batch;
+  if constexpr (BAL) {
+    build_page_prefix(p, sm.prefix, warp_tot);
+    w.total = sm.prefix[B];
+    w.w_eff = min((int)gridDim.x, w.total);
+    if ((int)blockIdx.x < w.w_eff) {
+      w.g_begin = (int)((int64_t)w.total * blockIdx.x / w.w_eff);
+      w.g_end = (int)((int64_t)w.total * (blockIdx.x + 1) / w.w_eff);
+      int lo = 0, hi = B;  // last b with prefix[b] <= g_begin
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (sm.prefix[mid] <= w.g_begin) lo = mid; else hi = mid - 1;
+      }
+      w.b_first = lo;
+    }
+    for (int b = blockIdx.x; b < B; b += gridDim.x)
+      if (sm.prefix[b + 1] == sm.prefix[b]) write_zero_row<T, D>(p, b, head_lo, head_hi, threadIdx.x, blockDim.x);
+  } else {
+    w.b_first = blockIdx.x / p.max_chunks;
+    w.chunk = blockIdx.x % p.max_chunks;
+    w.n_split = pages_of(p, w.b_first, w.chunk == 0 && blockIdx.y == 0);
+    w.g_begin = w.chunk * p.split_pages;
+    w.g_end = min(w.n_split, w.g_begin + p.split_pages);
+    if (w.n_split == 0 && w.chunk == 0)
+      write_zero_row<T, D>(p, w.b_first, head_lo, head_hi, threadIdx.x, blockDim.x);
+    __syncthreads();
+  }
+  return w;
+}
+
+// Next (sequence, page range) segment of the CTA's work; b and g are the cursor.
+template <bool BAL>
+__device__ __forceinline__ bool next_seg(const Work& w, const int32_t* prefix, int& b, int& g, Seg& s) {
+  if (g >= w.g_end) return false;
+  if constexpr (BAL) {
+    while (prefix[b + 1] <= g) ++b;
+    s.s0 = prefix[b];
+    s.s1 = prefix[b + 1];
+  } else {
+    s.s0 = 0;
+    s.s1 = w.n_split;
+  }
+  s.b = b;
+  const int seg_end = min(w.g_end, s.s1);
+  s.lp0 = g - s.s0;
+  s.lp1 = seg_end - s.s0;
+  g = seg_end;
+  ++b;
+  return true;
+}
+
+// Producer warp: reads the block table 32 entries at a time and issues the two
+// TMA tile loads (K, V) of every page into the stage ring.
+template <bool BAL>
+__device__ void produce(const DecodeParams& p, const Work& w, const Smem& sm, const CUtensorMap* tk,
+                        const CUtensorMap* tv, int head_coord, int lane) {
+  const int STAGES = p.stages;
+  const int stage_bytes = 2 * p.tile_bytes;
+  uint32_t it = 0;
+  bool ok = true;
+  int b = w.b_first, g = w.g_begin;
+  Seg s;
+  while (ok && next_seg<BAL>(w, sm.prefix, b, g, s)) {
+    const int32_t* row = p.block_table + (int64_t)s.b * p.bt_sb;
+    for (int lp = s.lp0; lp < s.lp1 && ok; lp += 32) {
+      const int cnt = min(32, s.lp1 - lp);
+      const int my_page = lane < cnt ? __ldg(row + lp + lane) : 0;
+      if (lane < cnt && (my_page < 0 || (int64_t)my_page >= p.num_blocks)) set_error(p.error, kErrBadPage);
+      for (int i = 0; i < cnt; ++i, ++it) {
+        const int page = __shfl_sync(kFull, my_page, i);
+        int good = 1;
+        if (lane == 0) {
+          const int st = it % STAGES;
+          if (!mbar_wait_bounded(&sm.empty_bar[st], ((it / STAGES) & 1) ^ 1)) {
+            good = 0;
+          } else {
+            mbar_arrive_expect_tx(&sm.full_bar[st], stage_bytes);
+            uint8_t* dst = sm.stages + st * stage_bytes;
+            // an out-of-range page (reported above) reads as zeros: TMA fills outside the tensor
+            tma_load_4d(dst, tk, 0, 0, head_coord, page, &sm.full_bar[st]);
+            tma_load_4d(dst + p.tile_bytes, tv, 0, 0, head_coord, page, &sm.full_bar[st]);
+          }
+        }
+        if (!__shfl_sync(kFull, good, 0)) {
+          ok = false;
+          break;
+        }
+      }
+    }
+  }
+  if (!ok && lane == 0) set_error(p.error, kErrTimeout);
+  // the CTA must not retire with bulk copies still writing its shared memory
+  if (lane == 0) {
+    const uint32_t n = it < (uint32_t)STAGES ? it : (uint32_t)STAGES;
+    for (uint32_t k = 1; k <= n; ++k) {
+      const uint32_t i = it - k;
+      if (!mbar_wait_bounded(&sm.full_bar[i % STAGES], (i / STAGES) & 1)) set_error(p.error, kErrTimeout);
+    }
+  }
+}
+
+// Workspace slot of a partial result.
+template <bool BAL>
+__device__ __forceinline__ int64_t partial_slot(const DecodeParams& p, const Work& w, int b, bool first_seg) {
+  if constexpr (BAL)
+    return 2 * (int64_t)blockIdx.x + (first_seg ? 0 : 1);
+  else
+    return (int64_t)b * p.max_chunks + w.chunk;
+}
+
+// Balanced schedule: after this warp wrote its partial rows of sequence b
+// (heads head0 .. head0+nh-1), count the part; the warp that completes the
+// count merges all parts and re-arms the counter. No waiting on other CTAs.
+template <typename T, int D>
+__device__ void publish_and_merge(const DecodeParams& p, const Work& w, const Seg& s, int64_t ctr_index, int head0,
+                                  int nh, int lane) {
+  __threadfence();
+  __syncwarp();
+  auto wid = [&](int gp) { return (int)(((int64_t)(gp + 1) * w.w_eff - 1) / w.total); };
+  const int w_first = wid(s.s0), w_last = wid(s.s1 - 1);
+  const int nparts = w_last - w_first + 1;
+  int last = 0;
+  if (lane == 0) {
+    const int old = atomicAdd(&p.counters[ctr_index], 1);
+    last = old == nparts - 1;
+    if (last) atomicExch(&p.counters[ctr_index], 0);
+  }
+  if (__shfl_sync(kFull, last, 0)) {
+    __threadfence();
+    const int sb0 = s.s0;
+    auto slot_of = [&](int i) -> int64_t {
+      const int wi = w_first + i;
+      const int sw = (int)((int64_t)w.total * wi / w.w_eff);
+      return 2 * (int64_t)wi + (sw < sb0 ? 1 : 0);
+    };
+    for (int h = 0; h < nh; ++h) merge_parts<T, D>(p, s.b, head0 + h, nparts, slot_of, lane);
+  }
+}
+
+// ---------------------------------------------------------------- consumers
+
+// CUDA-core consumer (used for fp32): warp = (KV head, GW query heads).
+template <typename T, int D, int GW, bool BAL>
+__device__ void consume_fma(const DecodeParams& p, const Work& w, const Smem& sm, int kh, int kvh, int r,
+                            int lane) {
   constexpr int EPC = Elem<T>::kPerChunk;
   constexpr int DCH = D / EPC;
   constexpr int CPL = DCH / 2;
   constexpr int NG = 32 / DCH;
-  static_assert(D % EPC == 0 && DCH % 2 == 0 && DCH <= 32 && kBlockSize % NG == 0, "unsupported head_dim");
-  static_assert((kBlockSize / NG) % 4 == 0, "token groups must be float4-sized");
-
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ int32_t warp_tot[32];
-
-  const int HG = p.heads_per_cta, WPK = p.warps_per_kv, NCW = HG * WPK, STAGES = p.stages;
-  const int tile_bytes = kBlockSize * HG * D * (int)sizeof(T);
-  const int stage_bytes = 2 * tile_bytes;
-  float* p_buf = reinterpret_cast<float*>(smem + STAGES * stage_bytes);
-  uint64_t* full_bar =
-      reinterpret_cast<uint64_t*>(smem + STAGES * stage_bytes + ((NCW * GW * kBlockSize * 4 + 15) & ~15));
-  uint64_t* empty_bar = full_bar + kMaxStages;
-  int32_t* prefix = reinterpret_cast<int32_t*>(empty_bar + kMaxStages);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int hg = blockIdx.y;
-  const int B = p.batch;
   const int G = p.num_heads / p.num_kv_heads;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], NCW);
-    }
-    fence_mbar_init();
-  }
-  if (warp == NCW && lane == 0) {
-    tma_prefetch_desc(&tmap_k);
-    tma_prefetch_desc(&tmap_v);
-  }
-
-  // ---------------------------------------------------------------- work range
-  int g_begin = 0, g_end = 0, b_first = 0, w_eff = 1, total = 0;
-  int chunk = 0, n_split = 0;  // split schedule: chunk index and pages of the sequence
-  if constexpr (BALANCED) {
-    build_page_prefix(p, prefix, warp_tot);  // contains __syncthreads (also publishes the barrier init)
-    total = prefix[B];
-    w_eff = min((int)gridDim.x, total);
-    if ((int)blockIdx.x < w_eff) {
-      g_begin = (int)((int64_t)total * blockIdx.x / w_eff);
-      g_end = (int)((int64_t)total * (blockIdx.x + 1) / w_eff);
-      int lo = 0, hi = B;  // last b with prefix[b] <= g_begin
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (prefix[mid] <= g_begin) lo = mid; else hi = mid - 1;
-      }
-      b_first = lo;
-    }
-    // rows with nothing to attend to are written as zeros
-    for (int b = blockIdx.x; b < B; b += gridDim.x)
-      if (prefix[b + 1] == prefix[b])
-        write_zero_row<T, D>(p, b, hg * HG * G, (hg + 1) * HG * G, threadIdx.x, blockDim.x);
-  } else {
-    b_first = blockIdx.x / p.max_chunks;
-    chunk = blockIdx.x % p.max_chunks;
-    n_split = pages_of(p, b_first, chunk == 0 && hg == 0);
-    g_begin = chunk * p.split_pages;
-    g_end = min(n_split, g_begin + p.split_pages);
-    if (n_split == 0 && chunk == 0)
-      write_zero_row<T, D>(p, b_first, hg * HG * G, (hg + 1) * HG * G, threadIdx.x, blockDim.x);
-    __syncthreads();
-  }
-  if (g_begin >= g_end) return;  // uniform over the CTA: nothing issued, nothing pending
-
-  // ---------------------------------------------------------------- producer
-  if (warp == NCW) {
-    uint32_t it = 0;
-    bool ok = true;
-    int b = b_first, g = g_begin;
-    while (g < g_end && ok) {
-      int s0 = 0, s1 = n_split;
-      if constexpr (BALANCED) {
-        while (prefix[b + 1] <= g) ++b;
-        s0 = prefix[b];
-        s1 = prefix[b + 1];
-      }
-      const int seg_end = min(g_end, s1);
-      const int32_t* row = p.block_table + (int64_t)b * p.bt_sb;
-      for (int lp = g - s0; lp < seg_end - s0 && ok; lp += 32) {
-        const int cnt = min(32, seg_end - s0 - lp);
-        int my_page = lane < cnt ? __ldg(row + lp + lane) : 0;
-        if (lane < cnt && (my_page < 0 || (int64_t)my_page >= p.num_blocks)) set_error(p.error, kErrBadPage);
-        for (int i = 0; i < cnt; ++i, ++it) {
-          const int page = __shfl_sync(kFull, my_page, i);
-          int good = 1;
-          if (lane == 0) {
-            const int s = it % STAGES;
-            const uint32_t ph = (it / STAGES) & 1;
-            if (!mbar_wait_bounded(&empty_bar[s], ph ^ 1)) {
-              good = 0;
-            } else {
-              mbar_arrive_expect_tx(&full_bar[s], stage_bytes);
-              uint8_t* dst = smem + s * stage_bytes;
-              // out-of-range pages (reported above) read as zeros: TMA fills outside the tensor
-              tma_load_4d(dst, &tmap_k, 0, 0, hg * HG, page, &full_bar[s]);
-              tma_load_4d(dst + tile_bytes, &tmap_v, 0, 0, hg * HG, page, &full_bar[s]);
-            }
-          }
-          good = __shfl_sync(kFull, good, 0);
-          if (!good) {
-            ok = false;
-            break;
-          }
-        }
-      }
-      g = seg_end;
-      ++b;
-    }
-    if (!ok && lane == 0) set_error(p.error, kErrTimeout);
-    // the CTA must not retire with bulk copies still writing its shared memory
-    if (lane == 0) {
-      const uint32_t n = it < (uint32_t)STAGES ? it : (uint32_t)STAGES;
-      for (uint32_t k = 1; k <= n; ++k) {
-        const uint32_t i = it - k;
-        if (!mbar_wait_bounded(&full_bar[i % STAGES], (i / STAGES) & 1)) set_error(p.error, kErrTimeout);
-      }
-    }
-    return;
-  }
-  if (warp > NCW) return;
-
-  // ---------------------------------------------------------------- consumers
-  const int kh = warp / WPK, r = warp % WPK;
-  const int kvh = hg * HG + kh;
   const int head0 = kvh * G + r * GW;
-  float* pw = p_buf + warp * GW * kBlockSize;
-  const int t = lane >> 1, half = lane & 1;
-  (void)t;
+  const int warp = threadIdx.x >> 5;
+  float* pw = sm.p_buf + warp * GW * kBlockSize;
+  const int half = lane & 1;
+  const int STAGES = p.stages, stage_bytes = 2 * p.tile_bytes;
 
   uint32_t it = 0;
   bool first_seg = true;
-  int b = b_first, g = g_begin;
-  while (g < g_end) {
-    int s0 = 0, s1 = n_split;
-    if constexpr (BALANCED) {
-      while (prefix[b + 1] <= g) ++b;
-      s0 = prefix[b];
-      s1 = prefix[b + 1];
-    }
-    const int n_b = s1 - s0;
-    const int seg_end = min(g_end, s1);
-    const int lp0 = g - s0, lp1 = seg_end - s0;
-    const int ctx = min(max(__ldg(&p.context_lens[b]), 0), n_b * kBlockSize);
-
-    // q of this warp's heads: this lane's half of D, prescaled into the exp2 domain
+  int b = w.b_first, g = w.g_begin;
+  Seg s;
+  while (next_seg<BAL>(w, sm.prefix, b, g, s)) {
+    const int n_b = s.s1 - s.s0;
+    const int ctx = min(max(__ldg(&p.context_lens[s.b]), 0), n_b * kBlockSize);
     float qv[GW][D / 2];
 #pragma unroll
     for (int gq = 0; gq < GW; ++gq) {
-      const uint4* qrow = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.q) + (int64_t)b * p.q_sb +
+      const uint4* qrow = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.q) + (int64_t)s.b * p.q_sb +
                                                          (int64_t)(head0 + gq) * p.q_sh) +
                           half * CPL;
 #pragma unroll
@@ -427,29 +515,26 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
 #pragma unroll
       for (int e = 0; e < EPC; ++e) acc[gq][e] = 0.f;
     }
-
     bool ok = true;
-    for (int lp = lp0; lp < lp1; ++lp, ++it) {
-      const int s = it % STAGES;
-      if (!mbar_wait_bounded(&full_bar[s], (it / STAGES) & 1)) {
+    for (int lp = s.lp0; lp < s.lp1; ++lp, ++it) {
+      const int st = it % STAGES;
+      if (!mbar_wait_bounded(&sm.full_bar[st], (it / STAGES) & 1)) {
         ok = false;
         break;
       }
-      const T* kt = reinterpret_cast<const T*>(smem + s * stage_bytes) + kh * kBlockSize * D;
-      const T* vt = reinterpret_cast<const T*>(smem + s * stage_bytes + tile_bytes) + kh * kBlockSize * D;
+      const T* kt = reinterpret_cast<const T*>(sm.stages + st * stage_bytes) + kh * kBlockSize * D;
+      const T* vt = reinterpret_cast<const T*>(sm.stages + st * stage_bytes + p.tile_bytes) + kh * kBlockSize * D;
       const int valid = ctx - lp * kBlockSize;
       if (valid >= kBlockSize)
         page_update<T, D, GW, false>(kt, vt, valid, qv, m, l, acc, pw, lane);
       else
         page_update<T, D, GW, true>(kt, vt, valid, qv, m, l, acc, pw, lane);
-      if (lane == 0) mbar_arrive(&empty_bar[s]);
+      if (lane == 0) mbar_arrive(&sm.empty_bar[st]);
     }
     if (!__all_sync(kFull, ok)) {
       if (lane == 0) set_error(p.error, kErrTimeout);
       return;
     }
-
-    // ---- segment epilogue
 #pragma unroll
     for (int gq = 0; gq < GW; ++gq) l[gq] = warp_sum(l[gq]);
     if constexpr (NG > 1) {
@@ -460,7 +545,7 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
 #pragma unroll
           for (int e = 0; e < EPC; ++e) acc[gq][e] += __shfl_down_sync(kFull, acc[gq][e], off);
     }
-    if (lp0 == 0 && lp1 == n_b) {
+    if (s.lp0 == 0 && s.lp1 == n_b) {
       if (lane < DCH) {
 #pragma unroll
         for (int gq = 0; gq < GW; ++gq) {
@@ -468,16 +553,12 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
           float o[EPC];
 #pragma unroll
           for (int e = 0; e < EPC; ++e) o[e] = acc[gq][e] * inv;
-          T* dst = reinterpret_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)(head0 + gq) * p.o_sh + lane * EPC;
+          T* dst = reinterpret_cast<T*>(p.out) + (int64_t)s.b * p.o_sb + (int64_t)(head0 + gq) * p.o_sh + lane * EPC;
           *reinterpret_cast<uint4*>(dst) = Elem<T>::pack(o);
         }
       }
     } else {
-      int64_t slot;
-      if constexpr (BALANCED)
-        slot = 2 * (int64_t)blockIdx.x + (first_seg ? 0 : 1);
-      else
-        slot = (int64_t)b * p.max_chunks + chunk;
+      const int64_t slot = partial_slot<BAL>(p, w, s.b, first_seg);
       if (lane < DCH) {
 #pragma unroll
         for (int gq = 0; gq < GW; ++gq) {
@@ -491,39 +572,223 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
 #pragma unroll
         for (int gq = 0; gq < GW; ++gq) p.part_ml[slot * p.num_heads + head0 + gq] = make_float2(m[gq], l[gq]);
       }
-      if constexpr (BALANCED) {
-        // Publish this part, count it; the warp that brings the count to the
-        // number of parts merges them (and re-arms the counter for the next call).
-        __threadfence();
-        __syncwarp();
-        const int sb0 = s0, sb1 = s1;
-        auto wid = [&](int gp) { return (int)(((int64_t)(gp + 1) * w_eff - 1) / total); };
-        const int w_first = wid(sb0), w_last = wid(sb1 - 1);
-        const int nparts = w_last - w_first + 1;
-        int last = 0;
-        if (lane == 0) {
-          int32_t* ctr = p.counters + (int64_t)b * (p.num_kv_heads * WPK) + kvh * WPK + r;
-          const int old = atomicAdd(ctr, 1);
-          last = old == nparts - 1;
-          if (last) atomicExch(ctr, 0);
-        }
-        last = __shfl_sync(kFull, last, 0);
-        if (last) {
-          __threadfence();
-          auto slot_of = [&](int i) -> int64_t {
-            const int w = w_first + i;
-            const int sw = (int)((int64_t)total * w / w_eff);
-            return 2 * (int64_t)w + (sw < sb0 ? 1 : 0);
-          };
-#pragma unroll
-          for (int gq = 0; gq < GW; ++gq) merge_parts<T, D>(p, b, head0 + gq, nparts, slot_of, lane);
-        }
+      if constexpr (BAL) {
+        const int64_t ctr = (int64_t)s.b * (p.num_kv_heads * p.warps_per_kv) + kvh * p.warps_per_kv + r;
+        publish_and_merge<T, D>(p, w, s, ctr, head0, GW, lane);
       }
     }
     first_seg = false;
-    g = seg_end;
-    ++b;
   }
+}
+
+// Tensor-core consumer (bf16 / fp16): warp = one KV head with all G <= 8 of its
+// query heads as the rows of a 16-row MMA tile (rows >= G are zero).
+//   QK:  S^T[16 q x 16 tok] = Q[16 x D] K^T   (m16n8k16, K rows via ldmatrix)
+//   PV:  O[16 q x D] += P[16 x 16 tok] V      (V rows via ldmatrix.trans)
+// The S accumulator fragments are exactly the A fragments of P, so
+// probabilities never leave registers.
+template <typename T, int D, bool BAL>
+__device__ void consume_mma(const DecodeParams& p, const Work& w, const Smem& sm, int kh, int kvh, int lane) {
+  constexpr int PITCH = mma_row_pitch(D);  // elements per smem row (odd number of 16-byte chunks)
+  constexpr int KS = D / 16;               // QK k-steps
+  constexpr int NT = D / 8;                // PV n-tiles
+  constexpr int DCH = D / 8;               // 16-byte chunks per row (16-bit elements)
+  const int G = p.num_heads / p.num_kv_heads;
+  const int head0 = kvh * G;
+  const int qr = lane >> 2, qc = lane & 3;
+  const bool real_row = qr < G;
+  const float c = p.scale_log2;
+  const int STAGES = p.stages, stage_bytes = 2 * p.tile_bytes;
+  // per-lane ldmatrix row offsets inside one [16 tok][PITCH] head tile
+  const int k_off = (((lane >> 4) & 1) * 8 + (lane & 7)) * PITCH + ((lane >> 3) & 1) * 8;
+  const int v_off = (((lane >> 3) & 1) * 8 + (lane & 7)) * PITCH + ((lane >> 4) & 1) * 8;
+
+  uint32_t it = 0;
+  bool first_seg = true;
+  int b = w.b_first, g = w.g_begin;
+  Seg s;
+  while (next_seg<BAL>(w, sm.prefix, b, g, s)) {
+    const int n_b = s.s1 - s.s0;
+    const int ctx = min(max(__ldg(&p.context_lens[s.b]), 0), n_b * kBlockSize);
+    uint32_t qa[KS][2];
+    {
+      const T* qrow = reinterpret_cast<const T*>(p.q) + (int64_t)s.b * p.q_sb + (int64_t)(head0 + qr) * p.q_sh;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        qa[ks][0] = real_row ? __ldg(reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 2 * qc)) : 0u;
+        qa[ks][1] = real_row ? __ldg(reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 8 + 2 * qc)) : 0u;
+      }
+    }
+    float m = -INFINITY, l = 0.f;
+    float o[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+
+    bool ok = true;
+    for (int lp = s.lp0; lp < s.lp1; ++lp, ++it) {
+      const int st = it % STAGES;
+      if (!mbar_wait_bounded(&sm.full_bar[st], (it / STAGES) & 1)) {
+        ok = false;
+        break;
+      }
+      const T* kt = reinterpret_cast<const T*>(sm.stages + st * stage_bytes) + kh * kBlockSize * PITCH;
+      T* vt = reinterpret_cast<T*>(sm.stages + st * stage_bytes + p.tile_bytes) + kh * kBlockSize * PITCH;
+      const int valid = ctx - lp * kBlockSize;
+
+      // ---- scores
+      float sa[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4(kt + k_off + 16 * ks, r0, r1, r2, r3);
+        mma16816<T>(sa[0], qa[ks][0], 0u, qa[ks][1], 0u, r0, r1);
+        mma16816<T>(sa[1], qa[ks][0], 0u, qa[ks][1], 0u, r2, r3);
+      }
+      // this lane's scores of row qr: tokens 2qc, 2qc+1, 8+2qc, 9+2qc
+      float sv[4] = {sa[0][0], sa[0][1], sa[1][0], sa[1][1]};
+      if (valid < kBlockSize) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if ((i >> 1) * 8 + 2 * qc + (i & 1) >= valid) sv[i] = -INFINITY;
+        // slots past the context may hold anything: zero their V rows (P is 0 there,
+        // but 0 * NaN would not be)
+        for (int i = lane; i < (kBlockSize - valid) * DCH; i += 32)
+          *reinterpret_cast<uint4*>(vt + (valid + i / DCH) * PITCH + (i % DCH) * 8) = make_uint4(0, 0, 0, 0);
+        // order these generic-proxy writes before the TMA that later refills the stage
+        fence_proxy_async_smem();
+        __syncwarp();
+      }
+      float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
+      mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 2));
+      const float m_new = fmaxf(m, mx);
+      if (__any_sync(kFull, m_new != m)) {  // rescale only when some row's max moved
+        const float alpha = exp2f((m - m_new) * c);
+        l *= alpha;
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+          o[n][0] *= alpha;
+          o[n][1] *= alpha;
+        }
+        m = m_new;
+      }
+      const float mc = m * c;
+      float pv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        pv[i] = exp2f(fmaf(sv[i], c, -mc));
+        l += pv[i];
+      }
+      const uint32_t pa0 = Elem<T>::pack2(pv[0], pv[1]);
+      const uint32_t pa2 = Elem<T>::pack2(pv[2], pv[3]);
+
+      // ---- PV
+#pragma unroll
+      for (int np = 0; np < NT / 2; ++np) {
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4_trans(vt + v_off + 16 * np, r0, r1, r2, r3);
+        mma16816<T>(o[2 * np], pa0, 0u, pa2, 0u, r0, r1);
+        mma16816<T>(o[2 * np + 1], pa0, 0u, pa2, 0u, r2, r3);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.empty_bar[st]);
+    }
+    if (!__all_sync(kFull, ok)) {
+      if (lane == 0) set_error(p.error, kErrTimeout);
+      return;
+    }
+
+    // ---- segment epilogue (row qr lives in lanes 4qr .. 4qr+3)
+    l += __shfl_xor_sync(kFull, l, 1);
+    l += __shfl_xor_sync(kFull, l, 2);
+    if (s.lp0 == 0 && s.lp1 == n_b) {
+      if (real_row) {
+        const float inv = 1.f / l;
+        uint32_t* dst = reinterpret_cast<uint32_t*>(reinterpret_cast<T*>(p.out) + (int64_t)s.b * p.o_sb +
+                                                    (int64_t)(head0 + qr) * p.o_sh + 2 * qc);
+#pragma unroll
+        for (int n = 0; n < NT; ++n) dst[4 * n] = Elem<T>::pack2(o[n][0] * inv, o[n][1] * inv);
+      }
+    } else {
+      const int64_t slot = partial_slot<BAL>(p, w, s.b, first_seg);
+      if (real_row) {
+        float2* dst = reinterpret_cast<float2*>(p.part_o + (slot * p.num_heads + head0 + qr) * D + 2 * qc);
+#pragma unroll
+        for (int n = 0; n < NT; ++n) dst[4 * n] = make_float2(o[n][0], o[n][1]);
+        if (qc == 0) p.part_ml[slot * p.num_heads + head0 + qr] = make_float2(m * c, l);
+      }
+      if constexpr (BAL) publish_and_merge<T, D>(p, w, s, (int64_t)s.b * p.num_kv_heads + kvh, head0, G, lane);
+    }
+    first_seg = false;
+  }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- kernels
+
+template <typename T, int D, int GW, bool BAL>
+__global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
+    paged_decode_fma_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
+                            const DecodeParams p) {
+  static_assert((kBlockSize / (32 / (D / Elem<T>::kPerChunk))) % 4 == 0, "token groups must be float4-sized");
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __shared__ int32_t warp_tot[32];
+  const Smem sm = carve_smem(smem_raw, p);
+  const int HG = p.heads_per_cta, WPK = p.warps_per_kv, NCW = HG * WPK;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.num_heads / p.num_kv_heads;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&sm.full_bar[s], 1);
+      mbar_init(&sm.empty_bar[s], NCW);
+    }
+    fence_mbar_init();
+  }
+  if (warp == NCW && lane == 0) {
+    tma_prefetch_desc(&tmap_k);
+    tma_prefetch_desc(&tmap_v);
+  }
+  const Work w = setup_work<T, D, BAL>(p, sm, warp_tot, blockIdx.y * HG * G, (blockIdx.y + 1) * HG * G);
+  if (w.g_begin >= w.g_end) return;
+  if (warp == NCW) {
+    produce<BAL>(p, w, sm, &tmap_k, &tmap_v, blockIdx.y * HG, lane);
+    return;
+  }
+  if (warp > NCW) return;
+  const int kh = warp / WPK;
+  consume_fma<T, D, GW, BAL>(p, w, sm, kh, blockIdx.y * HG + kh, warp % WPK, lane);
+}
+
+template <typename T, int D, bool BAL>
+__global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
+    paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
+                            const DecodeParams p) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __shared__ int32_t warp_tot[32];
+  const Smem sm = carve_smem(smem_raw, p);
+  const int HG = p.heads_per_cta, NCW = HG;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.num_heads / p.num_kv_heads;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&sm.full_bar[s], 1);
+      mbar_init(&sm.empty_bar[s], NCW);
+    }
+    fence_mbar_init();
+  }
+  if (warp == NCW && lane == 0) {
+    tma_prefetch_desc(&tmap_k);
+    tma_prefetch_desc(&tmap_v);
+  }
+  const Work w = setup_work<T, D, BAL>(p, sm, warp_tot, blockIdx.y * HG * G, (blockIdx.y + 1) * HG * G);
+  if (w.g_begin >= w.g_end) return;
+  if (warp == NCW) {
+    produce<BAL>(p, w, sm, &tmap_k, &tmap_v, blockIdx.y * HG, lane);
+    return;
+  }
+  if (warp > NCW) return;
+  consume_mma<T, D, BAL>(p, w, sm, warp, blockIdx.y * HG + warp, lane);
 }
 
 // Split schedule: merge the chunks of every sequence that has more than one.
@@ -543,23 +808,14 @@ __global__ void __launch_bounds__(128) lse_combine_kernel(const DecodeParams p) 
 
 // ---------------------------------------------------------------- host side
 
-int decode_smem_bytes(int dtype_bytes, int head_dim, int heads_per_cta, int warps_per_kv, int gw, int stages,
-                      int prefix_entries) {
-  const int tile = kBlockSize * heads_per_cta * head_dim * dtype_bytes;
-  const int ncw = heads_per_cta * warps_per_kv;
-  int bytes = stages * 2 * tile;
-  bytes += (ncw * gw * kBlockSize * 4 + 15) & ~15;
-  bytes += 2 * kMaxStages * 8;
-  bytes += prefix_entries * 4;
-  return bytes;
+int decode_smem_bytes(int tile_bytes, int pbuf_bytes, int stages, int prefix_entries) {
+  return stages * 2 * tile_bytes + pbuf_bytes + 2 * kMaxStages * 8 + prefix_entries * 4;
 }
 
-template <typename T, int D, int GW, bool BAL>
-static cudaError_t launch_one(const CUtensorMap& tk, const CUtensorMap& tv, const DecodeParams& p,
-                              const LaunchShape& s, cudaStream_t stream) {
-  auto kern = paged_decode_kernel<T, D, GW, BAL>;
+template <typename Kern>
+static cudaError_t launch_with_smem(Kern kern, int* granted, const CUtensorMap& tk, const CUtensorMap& tv,
+                                   const DecodeParams& p, const LaunchShape& s, cudaStream_t stream) {
   // raise the dynamic shared-memory limit once per device (and when a call needs more)
-  static int granted[64] = {0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -572,11 +828,29 @@ static cudaError_t launch_one(const CUtensorMap& tk, const CUtensorMap& tv, cons
   return cudaGetLastError();
 }
 
+template <typename T, int D, int GW, bool BAL>
+static cudaError_t launch_fma(const CUtensorMap& tk, const CUtensorMap& tv, const DecodeParams& p,
+                              const LaunchShape& s, cudaStream_t st) {
+  static int granted[64] = {0};
+  return launch_with_smem(paged_decode_fma_kernel<T, D, GW, BAL>, granted, tk, tv, p, s, st);
+}
+
+template <typename T, int D, bool BAL>
+static cudaError_t launch_mma(const CUtensorMap& tk, const CUtensorMap& tv, const DecodeParams& p,
+                              const LaunchShape& s, cudaStream_t st) {
+  static int granted[64] = {0};
+  return launch_with_smem(paged_decode_mma_kernel<T, D, BAL>, granted, tk, tv, p, s, st);
+}
+
 template <typename T, int D>
 static cudaError_t launch_d(int gw, bool bal, const CUtensorMap& tk, const CUtensorMap& tv, const DecodeParams& p,
                             const LaunchShape& s, cudaStream_t st) {
-  if (gw == 1) return bal ? launch_one<T, D, 1, true>(tk, tv, p, s, st) : launch_one<T, D, 1, false>(tk, tv, p, s, st);
-  return bal ? launch_one<T, D, 2, true>(tk, tv, p, s, st) : launch_one<T, D, 2, false>(tk, tv, p, s, st);
+  if constexpr (sizeof(T) == 2) {
+    return bal ? launch_mma<T, D, true>(tk, tv, p, s, st) : launch_mma<T, D, false>(tk, tv, p, s, st);
+  } else {
+    if (gw == 1) return bal ? launch_fma<T, D, 1, true>(tk, tv, p, s, st) : launch_fma<T, D, 1, false>(tk, tv, p, s, st);
+    return bal ? launch_fma<T, D, 2, true>(tk, tv, p, s, st) : launch_fma<T, D, 2, false>(tk, tv, p, s, st);
+  }
 }
 
 template <typename T>

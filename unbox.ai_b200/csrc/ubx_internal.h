@@ -11,13 +11,18 @@ constexpr int kBlockSize = 16;          // tokens per page (configs/infer/serve.
 constexpr int kMaxStages = 8;           // pipeline depth limit (mbarrier slots reserved)
 constexpr int kMaxConsumerWarps = 8;    // consumer warps per CTA
 constexpr int kMaxBatchSmem = 2048;     // balanced schedule keeps a (B+1) page prefix in smem
-constexpr int kMaxTileBytes = 32768;    // one K (or V) page tile of a head group
+constexpr int kMaxTileBytes = 36864;    // one K (or V) page tile of a head group
 constexpr int kSmemLimit = 226 * 1024;  // dynamic smem budget: 227 KB opt-in minus static smem and slack
 
 // Workspace layout prefix: [error word + reserved | merge counters | partials].
 constexpr size_t kWsHeaderBytes = 256;                      // error word at offset 0
 constexpr size_t kWsCounterEntries = 65536;                 // balanced-schedule merge counters
 constexpr size_t kWsCounterBytes = kWsCounterEntries * 4;   // must be zero before a call
+
+// Row pitch (elements) of a K/V page-tile row in shared memory on the 16-bit
+// tensor-core path: head_dim rounded up to an odd number of 16-byte chunks, so
+// the 8 rows one ldmatrix phase reads sit in 8 different bank groups.
+constexpr int mma_row_pitch(int head_dim) { return ((head_dim / 8) | 1) * 8; }
 
 struct DecodeParams {
   const void* q;
@@ -33,6 +38,8 @@ struct DecodeParams {
   int max_blocks;
   int64_t num_blocks;
   float scale_log2;      // softmax scale * log2(e): scores live in the exp2 domain
+  int tile_bytes;        // bytes of one K (or V) page tile in shared memory
+  int pbuf_bytes;        // bytes of the fp32 path's probability buffers
   int heads_per_cta;     // KV heads in one page tile (HG)
   int warps_per_kv;      // consumer warps sharing one KV head (WPK = G / GW)
   int stages;            // pipeline depth
@@ -56,8 +63,7 @@ struct LaunchShape {
 
 // Shared-memory bytes the decode kernel needs (stage ring + softmax buffers +
 // barriers + optional page prefix).
-int decode_smem_bytes(int dtype_bytes, int head_dim, int heads_per_cta, int warps_per_kv, int gw, int stages,
-                      int prefix_entries);
+int decode_smem_bytes(int tile_bytes, int pbuf_bytes, int stages, int prefix_entries);
 
 cudaError_t launch_paged_decode(int dtype, int head_dim, int gw, bool balanced, const CUtensorMap& tmap_k,
                                 const CUtensorMap& tmap_v, const DecodeParams& p, const LaunchShape& shape,
