@@ -47,7 +47,10 @@ def parse():
     ap.add_argument("--layers", type=int, default=24)
     ap.add_argument("--schedule", default="auto", choices=["auto", "balanced", "split"])
     ap.add_argument("--split-pages", type=int, default=0)
-    ap.add_argument("--graph", action="store_true", help="replay each decode step as one CUDA graph")
+    ap.add_argument("--no-graph", dest="graph", action="store_false",
+                    help="launch every op from Python instead of replaying the step as one CUDA graph")
+    ap.add_argument("--separate", action="store_true",
+                    help="KV append as its own launch before attention (default: fused into one launch)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     return ap.parse_args()
@@ -218,17 +221,26 @@ def main():
     outs = [torch.empty_like(dev["q"][l]) for l in range(L)]
     bt, cl, sm = dev["block_table"], dev["context_lens"], dev["slot_mapping"]
     kw = dict(schedule=args.schedule, split_pages=args.split_pages)
-    ws = pkg.workspace_for(device)
-    launches_per_layer = 2 + (1 if args.schedule == "split" else 0)
+    launches_per_layer = (2 if args.separate else 1) + (1 if args.schedule == "split" else 0)
+
+    def layer(l, q, k_new, v_new, block_table, context_lens, out, slots=None, timer=None):
+        """One layer-call: the new token's K/V append, then attention (engine.py:213-224)."""
+        if args.separate:
+            pkg.kv_append(k_new, v_new, dev["k_caches"][l], dev["v_caches"][l], slots)
+        if timer is not None:
+            timer[0].record()
+        if args.separate:
+            pkg.paged_attention(q, dev["k_caches"][l], dev["v_caches"][l], block_table, context_lens, out=out, **kw)
+        else:
+            pkg.paged_attention(q, dev["k_caches"][l], dev["v_caches"][l], block_table, context_lens, out=out,
+                                k_new=k_new, v_new=v_new, **kw)
+        if timer is not None:
+            timer[1].record()
 
     def step(timers=None):
         for l in range(L):
-            pkg.kv_append(dev["k_new"][l], dev["v_new"][l], dev["k_caches"][l], dev["v_caches"][l], sm)
-            if timers is not None:
-                timers[l][0].record()
-            pkg.paged_attention(dev["q"][l], dev["k_caches"][l], dev["v_caches"][l], bt, cl, out=outs[l], **kw)
-            if timers is not None:
-                timers[l][1].record()
+            layer(l, dev["q"][l], dev["k_new"][l], dev["v_new"][l], bt, cl, outs[l], sm,
+                  None if timers is None else timers[l])
 
     def barrier():
         if world > 1:
@@ -242,23 +254,26 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    def capture(fn):
+        """CUDA graph of fn (warmed up on a side stream first, as graph capture needs)."""
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        return g
+
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize()
     pkg.check_device_errors(device)
-
-    graph = None
-    if args.graph:
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s):
-            step()
-        torch.cuda.current_stream().wait_stream(s)
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            step()
-        for _ in range(3):
+    graph = capture(step) if args.graph else None
+    if graph is not None:
+        for _ in range(max(3, args.warmup)):
             graph.replay()
 
     # ---- device-resident timing (value)
@@ -279,11 +294,28 @@ def main():
     ms = ev0.elapsed_time(ev1)
     ms_max = max_over_ranks(ms)
     pkg.check_device_errors(device)
+
+    # ---- dominant kernel: average launch time on its own stream
     if graph is None:
         attn_ms = [a.elapsed_time(b) for row in timers for (a, b) in row]
-        attn_avg_ms = sum(attn_ms) / len(attn_ms)
+        kernel_avg_ms = sum(attn_ms) / len(attn_ms)
+    elif not args.separate and args.schedule != "split":
+        kernel_avg_ms = ms / (args.steps * L)   # the step is exactly L launches of the fused kernel
     else:
-        attn_avg_ms = None
+        def attn_only():
+            for l in range(L):
+                pkg.paged_attention(dev["q"][l], dev["k_caches"][l], dev["v_caches"][l], bt, cl, out=outs[l], **kw)
+        ga = capture(attn_only)
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a0.record()
+        for _ in range(args.steps):
+            ga.replay()
+        a1.record()
+        torch.cuda.synchronize()
+        kernel_avg_ms = a0.elapsed_time(a1) / (args.steps * L)
+        del ga
+    kernel_bytes = ab["attention"] if args.separate else ab["layer_call"]
 
     # ---- end to end through the public API with host buffers
     qh = torch.stack([x.cpu() for x in dev["q"]]).pin_memory()
@@ -304,21 +336,25 @@ def main():
         qd.copy_(qh, non_blocking=True)
         knd.copy_(knh, non_blocking=True)
         vnd.copy_(vnh, non_blocking=True)
-        torch.sub(cld, 1, out=posd)
-        pkg.slot_mapping(btd, posd, lay.block_size, out=smd)
+        if args.separate:
+            torch.sub(cld, 1, out=posd)
+            pkg.slot_mapping(btd, posd, lay.block_size, out=smd)
         for l in range(L):
-            pkg.kv_append(knd[l], vnd[l], dev["k_caches"][l], dev["v_caches"][l], smd)
-            pkg.paged_attention(qd[l], dev["k_caches"][l], dev["v_caches"][l], btd, cld, out=outd[l], **kw)
+            layer(l, qd[l], knd[l], vnd[l], btd, cld, outd[l], smd)
         outh.copy_(outd, non_blocking=True)
 
     for _ in range(3):
         e2e_step()
     torch.cuda.synchronize()
+    eg = capture(e2e_step) if args.graph else None
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        e2e_step()
+        if eg is not None:
+            eg.replay()
+        else:
+            e2e_step()
     e1.record()
     torch.cuda.synchronize()
     barrier()
@@ -326,6 +362,7 @@ def main():
     h2d = sum(t.numel() * t.element_size() for t in (bth, clh, qh, knh, vnh))
     d2h = outh.numel() * outh.element_size()
     assert torch.equal(outh[0].to(device), outs[0]), "end-to-end output differs from the device-resident step"
+    del eg
 
     total_bytes_step = ab["layer_call"] * L * world
     value = total_bytes_step * args.steps / (ms_max / 1e3) / 1e9
@@ -342,16 +379,17 @@ def main():
         "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms / args.steps, 4)},
         "clocks": clocks.summary(),
-        "graph": bool(graph is not None),
+        "graph": bool(graph is not None), "append": "separate launch" if args.separate else "fused",
     }
-    if attn_avg_ms is not None:
-        achieved = ab["attention"] / (attn_avg_ms / 1e3) / 1e9
-        traffic = profiled_traffic(args.workload)
-        line["roofline"] = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                            "frac": round(achieved / peak, 4), "traffic": traffic,
-                            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
-                            else "fallback 6650 GB/s", "kernel": "paged_decode_kernel",
-                            "algorithmic_bytes_per_launch": ab["attention"], "avg_launch_us": round(attn_avg_ms * 1e3, 2)}
+    achieved = kernel_bytes / (kernel_avg_ms / 1e3) / 1e9
+    traffic = profiled_traffic(args.workload)
+    line["roofline"] = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                        "frac": round(achieved / peak, 4), "traffic": traffic,
+                        "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                        else "fallback 6650 GB/s",
+                        "kernel": "paged_decode_mma_kernel" + ("" if args.separate else " (KV append fused)"),
+                        "algorithmic_bytes_per_launch": kernel_bytes, "avg_launch_us": round(kernel_avg_ms * 1e3, 2),
+                        "timing": "per-launch CUDA events" if graph is None else "graph replay / launches"}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         host = host_layer(dev, 0)
         calls, el, thr = cpu_oracle_run(lay, host, args.cpu_seconds)

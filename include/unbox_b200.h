@@ -8,8 +8,9 @@
  * (head_dim) dimension of every tensor is contiguous. Every call is
  * asynchronous on `stream` (a cudaStream_t passed as void*, NULL = legacy
  * default stream), allocates nothing, and never synchronises the host (except
- * ubx_read_device_error); a decode step made of ubx_slot_mapping, ubx_kv_append
- * and ubx_paged_decode_attention calls can be captured in a CUDA graph.
+ * ubx_read_device_error); a decode step made of ubx_slot_mapping, ubx_kv_append,
+ * ubx_paged_decode_attention and ubx_paged_decode_append_attention calls can be
+ * captured in a CUDA graph.
  *
  * Return value: UBX_OK or a UBX_ERR_* status for host-side validation and
  * launch failures (ubx_last_error() gives the message). Data-dependent problems
@@ -109,8 +110,9 @@ int ubx_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
  * scale = head_dim ** -0.5 (paged_decode_attention.py:134,169).
  *   q:            (batch, num_heads, head_dim), strides (q_s_b, q_s_h)
  *   k/v_cache:    (num_blocks, block_size, num_kv_heads, head_dim), strides
- *                 (c_s_block, c_s_tok, c_s_head); base 16-byte aligned and
- *                 strides multiples of 16 bytes (TMA)
+ *                 (c_s_block, c_s_tok, c_s_head) with c_s_head == head_dim
+ *                 (heads of a token row contiguous, the KVPool layout); base
+ *                 16-byte aligned, strides multiples of 16 bytes
  *   block_table:  (batch, max_blocks_per_seq) int32, row stride bt_s_row, -1 padded
  *   context_lens: (batch,) int32, includes the token just appended
  *   out:          (batch, num_heads, head_dim), strides (o_s_b, o_s_h), dtype of q
@@ -125,6 +127,28 @@ int ubx_paged_decode_attention(const void* q, int64_t q_s_b, int64_t q_s_h, cons
                                int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
                                int max_blocks_per_seq, float scale, int dtype, int schedule, int split_pages,
                                void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * KV append fused into paged decode attention: for every sequence b with
+ * context_lens[b] >= 1 the rows k_new[b], v_new[b] are first written to
+ * position context_lens[b] - 1 (page block_table[b, pos // bs], slot pos % bs),
+ * then out is computed over all context_lens[b] positions, as
+ * ubx_kv_append with slot_mapping = that slot followed by
+ * ubx_paged_decode_attention would do, in one launch.
+ * Replaces: the append loop and attention call of one layer of
+ * InferenceEngine.decode_step (unbox_platform/infer/engine.py:213-224), with
+ * the slot arithmetic of PagedKVCache.write_kv (kvcache.py:338-339).
+ *   k_new, v_new: (batch, num_kv_heads, head_dim), strides (new_s_tok, new_s_head)
+ * The other arguments are those of ubx_paged_decode_attention.
+ */
+int ubx_paged_decode_append_attention(const void* k_new, const void* v_new, int64_t new_s_tok, int64_t new_s_head,
+                                      const void* q, int64_t q_s_b, int64_t q_s_h, void* k_cache, void* v_cache,
+                                      int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head,
+                                      const int32_t* block_table, int64_t bt_s_row, const int32_t* context_lens,
+                                      void* out, int64_t o_s_b, int64_t o_s_h, int batch, int num_heads,
+                                      int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
+                                      int max_blocks_per_seq, float scale, int dtype, int schedule, int split_pages,
+                                      void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Allocation-free variant of ubx_paged_decode_attention. No counterpart in the

@@ -278,3 +278,45 @@ def test_full_size_sampled_rows_and_schedules(name, pkg, oracle):
     ref, st = oracle.paged_decode_attention(q[rows].cpu(), kch, vch, bt[rows].cpu(), cl[rows].cpu())
     assert st == 0
     close(a[rows], ref, spec["dtype"])
+
+
+@pytest.mark.parametrize("name", GOLDEN_NAMES)
+def test_fused_append_golden(name, pkg):
+    """Append fused into the attention launch: same cache bytes as the
+    reference's write_kv, same outputs as its paged attention."""
+    z, lay, t = load_golden(name)
+    d = to_dev(t)
+    out = pkg.paged_decode_append_attention(d["q"], d["k_new"], d["v_new"], d["k_cache"], d["v_cache"],
+                                            d["block_table"], d["context_lens"], lay.head_dim ** -0.5)
+    torch.cuda.synchronize()
+    pkg.check_device_errors()
+    assert sha(d["k_cache"].cpu()) == str(z["sha_k_after"])
+    assert sha(d["v_cache"].cpu()) == str(z["sha_v_after"])
+    close(out, z["out_ref"].astype(np.float64), str(z["dtype"]))
+
+
+@pytest.mark.parametrize("schedule", ["balanced", "split"])
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16", "float16"])
+def test_fused_append_equals_separate_launches(dtype, schedule, pkg):
+    wl = pkg.workloads
+    ctx = np.array([1, 16, 17, 0, 300, 1000, 33, 2], dtype=np.int32)
+    lay = wl.layout_uniform(31, 8, 1, 2, num_blocks=200)
+    perm = wl.portable_permutation(31, 2, 200)
+    bt = np.full((8, 64), -1, dtype=np.int32)
+    cur = 0
+    for b, c in enumerate(ctx):
+        n = (int(c) + 15) // 16
+        bt[b, :n] = perm[cur:cur + n]
+        cur += n
+    lay = wl.Layout(ctx, bt, 200)
+    t = wl.materialize_host(lay, 31, dtype=dtype)
+    a, f = to_dev(t), to_dev(t)
+    pkg.kv_append(a["k_new"], a["v_new"], a["k_cache"], a["v_cache"], a["slot_mapping"])
+    ref = pkg.paged_attention(a["q"], a["k_cache"], a["v_cache"], a["block_table"], a["context_lens"],
+                              schedule=schedule, split_pages=5)
+    out = pkg.paged_attention(f["q"], f["k_cache"], f["v_cache"], f["block_table"], f["context_lens"],
+                              schedule=schedule, split_pages=5, k_new=f["k_new"], v_new=f["v_new"])
+    torch.cuda.synchronize()
+    pkg.check_device_errors()
+    assert torch.equal(a["k_cache"], f["k_cache"]) and torch.equal(a["v_cache"], f["v_cache"])
+    assert torch.equal(ref, out)

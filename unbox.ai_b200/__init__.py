@@ -20,6 +20,9 @@ unbox_platform/infer/kvcache.py of the reference):
   -- the same op with an explicit softmax scale.
 * ``kv_append(k_new, v_new, k_cache, v_cache, slot_mapping)`` -- batched
   replacement for the per-sequence ``PagedKVCache.write_kv`` loop.
+* ``paged_decode_append_attention(q, k_new, v_new, k_cache, v_cache, block_table,
+  context_lens, scale)`` -- the append and the attention of one decode layer
+  in a single launch.
 * ``slot_mapping(block_table, positions, block_size)`` -- device-side slot
   computation (kvcache.py:338-339) for one decode step.
 """
@@ -32,7 +35,7 @@ __all__ = [
 
 
 _OPS = ("paged_decode_attention", "paged_attention", "paged_attention_split", "kv_append", "slot_mapping",
-        "DecodeWorkspace", "check_device_errors", "workspace_for")
+        "DecodeWorkspace", "check_device_errors", "workspace_for", "paged_decode_append_attention")
 
 
 def __getattr__(name):

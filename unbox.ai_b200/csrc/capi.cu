@@ -1,7 +1,5 @@
 // C ABI of unbox_b200: argument validation, launch planning, TMA descriptor
 // encoding and the extern "C" entry points declared in include/unbox_b200.h.
-#include <cudaTypedefs.h>
-
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
@@ -75,44 +73,8 @@ int num_sms_current_device(int* n) {
   return UBX_OK;
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
-// Tensor map over one per-layer K or V pool: dims (D, token, head, page) with
-// element strides (1, c_s_tok, c_s_head, c_s_block); box (D, 16, HG, 1).
-int encode_pool_map(CUtensorMap* map, const void* base, int dtype, int head_dim, int block_size, int kv_heads,
-                    int64_t num_blocks, int64_t s_tok, int64_t s_head, int64_t s_block, int heads_per_cta,
-                    int box_inner) {
-  auto fn = encode_fn();
-  if (!fn) return fail(UBX_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-  const int es = dtype_bytes(dtype);
-  CUtensorMapDataType dt = dtype == UBX_DTYPE_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
-                           : dtype == UBX_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  cuuint64_t dims[4] = {(cuuint64_t)head_dim, (cuuint64_t)block_size, (cuuint64_t)kv_heads, (cuuint64_t)num_blocks};
-  cuuint64_t strides[3] = {(cuuint64_t)(s_tok * es), (cuuint64_t)(s_head * es), (cuuint64_t)(s_block * es)};
-  // box_inner >= head_dim: the columns past head_dim are outside the tensor and
-  // TMA fills them with zeros (row padding in shared memory, no DRAM traffic)
-  cuuint32_t box[4] = {(cuuint32_t)box_inner, (cuuint32_t)block_size, (cuuint32_t)heads_per_cta, 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = fn(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(UBX_ERR_INVALID_ARGUMENT, "cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
-  return UBX_OK;
-}
-
 struct Plan {
-  int gw, wpk, hg, n_hg, stages, smem, pitch, tile, pbuf;
+  int gw, wpk, hg, n_hg, stages, smem, row, pitch, tile, pbuf;
   bool balanced;
   int split_pages, max_chunks;
   dim3 grid, block;
@@ -126,15 +88,16 @@ int make_plan(int batch, int num_heads, int num_kv_heads, int head_dim, int dtyp
   const bool mma = es == 2;  // 16-bit: tensor-core consumer, one warp per KV head
   pl->gw = mma ? G : (G < 2 ? G : 2);
   pl->wpk = mma ? 1 : G / pl->gw;
-  pl->pitch = mma ? mma_row_pitch(head_dim) : head_dim;
   pl->hg = 1;
   for (int hg = num_kv_heads; hg >= 1; --hg) {
     if (num_kv_heads % hg) continue;
     if (hg * pl->wpk > kMaxConsumerWarps) continue;
-    if (kBlockSize * hg * pl->pitch * es > kMaxTileBytes) continue;
+    if (kBlockSize * tile_row_pitch(hg * head_dim * es) > kMaxTileBytes) continue;
     pl->hg = hg;
     break;
   }
+  pl->row = pl->hg * head_dim * es;      // one bulk copy: a token row of the CTA's heads
+  pl->pitch = tile_row_pitch(pl->row);   // its shared-memory pitch
   pl->n_hg = num_kv_heads / pl->hg;
   const bool can_balance = batch <= kMaxBatchSmem && (int64_t)batch * num_kv_heads * pl->wpk <= (int64_t)kCounterEntries;
   if (schedule == UBX_SCHEDULE_BALANCED && !can_balance)
@@ -142,7 +105,7 @@ int make_plan(int batch, int num_heads, int num_kv_heads, int head_dim, int dtyp
   pl->balanced = schedule == UBX_SCHEDULE_BALANCED || (schedule == UBX_SCHEDULE_AUTO && can_balance);
   pl->split_pages = split_pages > 0 ? split_pages : kDefaultSplitPages;
   pl->max_chunks = (max_blocks + pl->split_pages - 1) / pl->split_pages;
-  pl->tile = kBlockSize * pl->hg * pl->pitch * es;
+  pl->tile = kBlockSize * pl->pitch;
   pl->pbuf = mma ? 0 : ((pl->hg * pl->wpk * pl->gw * kBlockSize * 4 + 15) & ~15);
   const int prefix = pl->balanced ? batch + 1 : 0;
   const int fixed = decode_smem_bytes(pl->tile, pl->pbuf, 0, prefix);
@@ -279,12 +242,22 @@ int ubx_read_device_error(const void* workspace, int32_t* value, int clear, void
   return UBX_OK;
 }
 
-int ubx_paged_decode_attention(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache, const void* v_cache,
-                               int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head, const int32_t* block_table,
-                               int64_t bt_s_row, const int32_t* context_lens, void* out, int64_t o_s_b, int64_t o_s_h,
-                               int batch, int num_heads, int num_kv_heads, int head_dim, int block_size,
-                               int64_t num_blocks, int max_blocks_per_seq, float scale, int dtype, int schedule,
-                               int split_pages, void* workspace, size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+struct AppendArgs {
+  const void* k_new;
+  const void* v_new;
+  int64_t s_tok, s_head;  // element strides of k_new / v_new
+};
+
+int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache, const void* v_cache,
+                int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head, const int32_t* block_table, int64_t bt_s_row,
+                const int32_t* context_lens, void* out, int64_t o_s_b, int64_t o_s_h, int batch, int num_heads,
+                int num_kv_heads, int head_dim, int block_size, int64_t num_blocks, int max_blocks_per_seq,
+                float scale, int dtype, int schedule, int split_pages, void* workspace, size_t workspace_bytes,
+                const AppendArgs* app, void* stream) {
   g_last_error.clear();
   int st = check_shape(num_heads, num_kv_heads, head_dim, block_size, dtype);
   if (st != UBX_OK) return st;
@@ -302,7 +275,16 @@ int ubx_paged_decode_attention(const void* q, int64_t q_s_b, int64_t q_s_h, cons
   if (!aligned16(q) || !aligned16(out) || !m16(q_s_b) || !m16(q_s_h) || !m16(o_s_b) || !m16(o_s_h))
     return fail(UBX_ERR_INVALID_ARGUMENT, "q/out rows must be 16-byte aligned");
   if (!aligned16(k_cache) || !aligned16(v_cache) || !m16(c_s_block) || !m16(c_s_tok) || !m16(c_s_head))
-    return fail(UBX_ERR_INVALID_ARGUMENT, "K/V cache base and strides must be multiples of 16 bytes (TMA)");
+    return fail(UBX_ERR_INVALID_ARGUMENT, "K/V cache base and strides must be multiples of 16 bytes");
+  if (c_s_head != head_dim)
+    return fail(UBX_ERR_UNSUPPORTED,
+                "KV heads must be contiguous within a token row (head stride %lld, head_dim %d): the KVPool layout",
+                (long long)c_s_head, head_dim);
+  if (app) {
+    if (!app->k_new || !app->v_new) return fail(UBX_ERR_INVALID_ARGUMENT, "null k_new / v_new");
+    if (!aligned16(app->k_new) || !aligned16(app->v_new) || !m16(app->s_tok) || !m16(app->s_head))
+      return fail(UBX_ERR_INVALID_ARGUMENT, "k_new / v_new rows must be 16-byte aligned");
+  }
   if (!(scale > 0.f) && !(scale < 0.f)) return fail(UBX_ERR_INVALID_ARGUMENT, "scale must be finite and non-zero");
   if (!workspace) return fail(UBX_ERR_WORKSPACE, "workspace is required");
 
@@ -315,14 +297,6 @@ int ubx_paged_decode_attention(const void* q, int64_t q_s_b, int64_t q_s_h, cons
   const WsLayout wl = ws_layout(pl.slots, num_heads, head_dim);
   if (workspace_bytes < wl.total)
     return fail(UBX_ERR_WORKSPACE, "workspace of %zu bytes, this call needs %zu", workspace_bytes, wl.total);
-
-  CUtensorMap tk, tv;
-  st = encode_pool_map(&tk, k_cache, dtype, head_dim, block_size, num_kv_heads, num_blocks, c_s_tok, c_s_head,
-                       c_s_block, pl.hg, pl.pitch);
-  if (st != UBX_OK) return st;
-  st = encode_pool_map(&tv, v_cache, dtype, head_dim, block_size, num_kv_heads, num_blocks, c_s_tok, c_s_head,
-                       c_s_block, pl.hg, pl.pitch);
-  if (st != UBX_OK) return st;
 
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   DecodeParams p;
@@ -342,6 +316,8 @@ int ubx_paged_decode_attention(const void* q, int64_t q_s_b, int64_t q_s_h, cons
   p.num_blocks = num_blocks;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.tile_bytes = pl.tile;
+  p.row_bytes = pl.row;
+  p.smem_row_bytes = pl.pitch;
   p.pbuf_bytes = pl.pbuf;
   p.heads_per_cta = pl.hg;
   p.warps_per_kv = pl.wpk;
@@ -352,16 +328,55 @@ int ubx_paged_decode_attention(const void* q, int64_t q_s_b, int64_t q_s_h, cons
   p.part_ml = reinterpret_cast<float2*>(ws + wl.ml_off);
   p.counters = reinterpret_cast<int32_t*>(ws + kHeaderBytes);
   p.error = reinterpret_cast<int32_t*>(ws);
+  p.k_cache = k_cache;
+  p.v_cache = v_cache;
+  p.c_sblk = c_s_block;
+  p.c_stok = c_s_tok;
+  p.c_sh = c_s_head;
+  p.k_new = app ? app->k_new : nullptr;
+  p.v_new = app ? app->v_new : nullptr;
+  p.n_stok = app ? app->s_tok : 0;
+  p.n_sh = app ? app->s_head : 0;
 
   LaunchShape shape{pl.grid, pl.block, pl.smem};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = launch_paged_decode(dtype, head_dim, pl.gw, pl.balanced, tk, tv, p, shape, s);
+  cudaError_t e = launch_paged_decode(dtype, head_dim, pl.gw, pl.balanced, p, shape, s);
   if (e != cudaSuccess) return cuda_fail(e, "paged_decode launch");
   if (!pl.balanced) {
     e = launch_lse_combine(dtype, head_dim, p, s);
     if (e != cudaSuccess) return cuda_fail(e, "lse_combine launch");
   }
   return UBX_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ubx_paged_decode_attention(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache, const void* v_cache,
+                               int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head, const int32_t* block_table,
+                               int64_t bt_s_row, const int32_t* context_lens, void* out, int64_t o_s_b, int64_t o_s_h,
+                               int batch, int num_heads, int num_kv_heads, int head_dim, int block_size,
+                               int64_t num_blocks, int max_blocks_per_seq, float scale, int dtype, int schedule,
+                               int split_pages, void* workspace, size_t workspace_bytes, void* stream) {
+  return decode_impl(q, q_s_b, q_s_h, k_cache, v_cache, c_s_block, c_s_tok, c_s_head, block_table, bt_s_row,
+                     context_lens, out, o_s_b, o_s_h, batch, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
+                     max_blocks_per_seq, scale, dtype, schedule, split_pages, workspace, workspace_bytes, nullptr,
+                     stream);
+}
+
+int ubx_paged_decode_append_attention(const void* k_new, const void* v_new, int64_t new_s_tok, int64_t new_s_head,
+                                      const void* q, int64_t q_s_b, int64_t q_s_h, void* k_cache, void* v_cache,
+                                      int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head,
+                                      const int32_t* block_table, int64_t bt_s_row, const int32_t* context_lens,
+                                      void* out, int64_t o_s_b, int64_t o_s_h, int batch, int num_heads,
+                                      int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
+                                      int max_blocks_per_seq, float scale, int dtype, int schedule, int split_pages,
+                                      void* workspace, size_t workspace_bytes, void* stream) {
+  const AppendArgs app{k_new, v_new, new_s_tok, new_s_head};
+  return decode_impl(q, q_s_b, q_s_h, k_cache, v_cache, c_s_block, c_s_tok, c_s_head, block_table, bt_s_row,
+                     context_lens, out, o_s_b, o_s_h, batch, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
+                     max_blocks_per_seq, scale, dtype, schedule, split_pages, workspace, workspace_bytes, &app, stream);
 }
 
 }  // extern "C"

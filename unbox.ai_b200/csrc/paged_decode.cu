@@ -7,21 +7,19 @@
 // slot j % 16, KV head h / (H / KVH).
 //
 // Structure (one CTA per SM, persistent):
-//   * A page of the pool holds 16 tokens x KVH heads x D elements, contiguous
-//     (the KVPool layout, kvcache.py:248-251). One 4-D TMA box
-//     (D, 16 tokens, HG heads, 1 page) moves the K tile of a head group and one
-//     more the V tile; the box is laid out [head][token][d] in shared memory so
-//     every (token, head) row is D elements at a D*sizeof(T) pitch.
+//   * In the KVPool layout (kvcache.py:248-251) one token row of a page holds
+//     all KV heads contiguously (KVH * D elements). The CTA's head group of a
+//     page is 16 such rows; each is moved with one bulk copy (cp.async.bulk on
+//     the TMA engine) into a shared-memory tile whose row pitch is padded to an
+//     odd number of 16-byte chunks, so ldmatrix reads are bank-conflict free.
 //   * Warp NCW is the producer: it walks the CTA's pages, reads the block table
-//     32 entries at a time and issues the two TMA loads per page into a ring of
-//     `stages` buffers guarded by full/empty mbarriers.
+//     32 entries at a time and has its 32 lanes issue the 32 row copies (16 K,
+//     16 V) of every page into a ring of `stages` buffers guarded by full/empty
+//     mbarriers.
 //   * bf16 / fp16: consumer warp w owns KV head w of the head group with all of
 //     its query heads as the rows of one tensor-core tile (mma m16n8k16 fed by
-//     ldmatrix from the TMA tiles); QK's accumulator fragments are reused as
+//     ldmatrix from the page tiles); QK's accumulator fragments are reused as
 //     the P operand of PV, online softmax runs on them with two shuffles per row.
-//     The TMA box is padded to an odd number of 16-byte chunks per row (the pad
-//     is filled by TMA's out-of-bounds zero fill, no extra DRAM reads) so that
-//     ldmatrix rows fall in distinct banks.
 //   * fp32: CUDA-core consumer, warp = (KV head, <= 2 query heads): QK with two
 //     lanes per token holding half of q in registers, PV with lane = (16-byte
 //     chunk of D, token group).
@@ -152,11 +150,58 @@ __device__ __forceinline__ void merge_parts(const DecodeParams& p, int b, int h,
   }
 }
 
+// Merge the `nparts` partial (acc, max, sum) triples of heads head0 .. head0+nh-1
+// of sequence b into normalised output rows. Lanes are (head, 16-byte output
+// chunk) pairs, and the loads of several parts are in flight together, so a
+// merge costs a few L2 round trips rather than one per part and head.
+template <typename T, int D, typename SlotFn>
+__device__ void merge_rows(const DecodeParams& p, int b, int head0, int nh, int nparts, SlotFn slot_of, int lane) {
+  constexpr int EPC = Elem<T>::kPerChunk;
+  constexpr int DCH = D / EPC;   // output chunks per row
+  constexpr int HPW = 32 / DCH;  // heads per pass of the warp
+  const int H = p.num_heads;
+  for (int hb = 0; hb < nh; hb += HPW) {
+    const int h = hb + lane / DCH, c = lane % DCH;
+    if (lane >= HPW * DCH || h >= nh) continue;  // no warp collectives below
+    const int head = head0 + h;
+    float M = -INFINITY;
+#pragma unroll 4
+    for (int i = 0; i < nparts; ++i) M = fmaxf(M, __ldcg(&p.part_ml[slot_of(i) * H + head]).x);
+    float L = 0.f, o[EPC];
+#pragma unroll
+    for (int e = 0; e < EPC; ++e) o[e] = 0.f;
+#pragma unroll 4
+    for (int i = 0; i < nparts; ++i) {
+      const int64_t slot = slot_of(i);
+      const float2 ml = __ldcg(&p.part_ml[slot * H + head]);
+      const float4* src = reinterpret_cast<const float4*>(p.part_o + (slot * H + head) * D + c * EPC);
+      float4 v[EPC / 4];
+#pragma unroll
+      for (int e4 = 0; e4 < EPC / 4; ++e4) v[e4] = __ldcg(src + e4);
+      const float wgt = exp2f(ml.x - M);
+      L = fmaf(ml.y, wgt, L);
+#pragma unroll
+      for (int e4 = 0; e4 < EPC / 4; ++e4) {
+        o[4 * e4 + 0] = fmaf(wgt, v[e4].x, o[4 * e4 + 0]);
+        o[4 * e4 + 1] = fmaf(wgt, v[e4].y, o[4 * e4 + 1]);
+        o[4 * e4 + 2] = fmaf(wgt, v[e4].z, o[4 * e4 + 2]);
+        o[4 * e4 + 3] = fmaf(wgt, v[e4].w, o[4 * e4 + 3]);
+      }
+    }
+    const float inv = 1.f / L;
+#pragma unroll
+    for (int e = 0; e < EPC; ++e) o[e] *= inv;
+    T* dst = reinterpret_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)head * p.o_sh + c * EPC;
+    *reinterpret_cast<uint4*>(dst) = Elem<T>::pack(o);
+  }
+}
+
 // One page of one KV head for the GW query heads of this warp.
-//   kt, vt: [16 tokens][D] tiles of this warp's KV head in shared memory
+//   kt, vt: this warp's KV head in the page tiles: 16 rows of D elements, row
+//           stride rs elements
 //   pw:     this warp's probability buffer [GW][16] (rotated per token group)
 template <typename T, int D, int GW, bool MASKED>
-__device__ __forceinline__ void page_update(const T* __restrict__ kt, const T* __restrict__ vt, int valid,
+__device__ __forceinline__ void page_update(const T* __restrict__ kt, const T* __restrict__ vt, int rs, int valid,
                                             const float (&qv)[GW][D / 2], float (&m)[GW], float (&l)[GW],
                                             float (&acc)[GW][Elem<T>::kPerChunk], float* pw, int lane) {
   constexpr int EPC = Elem<T>::kPerChunk;
@@ -167,7 +212,7 @@ __device__ __forceinline__ void page_update(const T* __restrict__ kt, const T* _
   const int t = lane >> 1, half = lane & 1;
 
   // ---- scores: lane pair (2t, 2t+1) covers token t, each lane half of D
-  const uint4* krow = reinterpret_cast<const uint4*>(kt) + t * DCH + half * CPL;
+  const uint4* krow = reinterpret_cast<const uint4*>(kt + t * rs) + half * CPL;
   float sa[GW], sb[GW];
 #pragma unroll
   for (int g = 0; g < GW; ++g) sa[g] = sb[g] = 0.f;
@@ -235,12 +280,11 @@ __device__ __forceinline__ void page_update(const T* __restrict__ kt, const T* _
         pp[g][4 * k4 + 3] = v.w;
       }
     }
-    const uint4* vcol = reinterpret_cast<const uint4*>(vt) + j;
 #pragma unroll
     for (int k = 0; k < TPG; ++k) {
       const int tt = gg * TPG + ((k + gg) % TPG);
       float vf[EPC];
-      Elem<T>::unpack(vcol[tt * DCH], vf);
+      Elem<T>::unpack(reinterpret_cast<const uint4*>(vt + tt * rs)[j], vf);
       if (MASKED && tt >= valid) {
 #pragma unroll
         for (int e = 0; e < EPC; ++e) vf[e] = 0.f;   // unused slots may hold anything
@@ -381,13 +425,44 @@ __device__ __forceinline__ bool next_seg(const Work& w, const int32_t* prefix, i
   return true;
 }
 
-// Producer warp: reads the block table 32 entries at a time and issues the two
-// TMA tile loads (K, V) of every page into the stage ring.
-template <bool BAL>
-__device__ void produce(const DecodeParams& p, const Work& w, const Smem& sm, const CUtensorMap* tk,
-                        const CUtensorMap* tv, int head_coord, int lane) {
+// Fused KV append (whole producer warp): write the new token of sequence b --
+// position context_lens[b] - 1, the engine's append at engine.py:213-215 --
+// into its slot of `page` for the heads this CTA streams, then fence so the
+// TMA load of the same page that follows sees the rows.
+template <typename T, int D>
+__device__ void append_rows(const DecodeParams& p, int b, int page, int head0, int nheads, int lane) {
+  constexpr int CPR = D * (int)sizeof(T) / 16;  // 16-byte chunks per row
+  const int ctx = __ldg(&p.context_lens[b]);
+  // no token to place, a clamped context (reported by pages_of) or a bad page
+  // (reported by the producer; the tile then reads as zeros)
+  if (ctx < 1 || (ctx - 1) / kBlockSize >= p.max_blocks || page < 0 || (int64_t)page >= p.num_blocks) return;
+  const int slot = (ctx - 1) % kBlockSize;
+  const int per_kv = nheads * CPR;
+  for (int i = lane; i < 2 * per_kv; i += 32) {
+    const int which = i / per_kv, r = i % per_kv, h = head0 + r / CPR, c = r % CPR;
+    const T* src = reinterpret_cast<const T*>(which ? p.v_new : p.k_new) + (int64_t)b * p.n_stok +
+                   (int64_t)h * p.n_sh + c * (16 / (int)sizeof(T));
+    T* dst = const_cast<T*>(reinterpret_cast<const T*>(which ? p.v_cache : p.k_cache)) + (int64_t)page * p.c_sblk +
+             (int64_t)slot * p.c_stok + (int64_t)h * p.c_sh + c * (16 / (int)sizeof(T));
+    *reinterpret_cast<uint4*>(dst) = __ldg(reinterpret_cast<const uint4*>(src));
+  }
+  fence_proxy_async_global();
+  __syncwarp();
+}
+
+// Producer warp: reads the block table 32 entries at a time; for every page
+// lane 0 claims a free stage and the 32 lanes each issue one row copy (lanes
+// 0-15 the K rows, 16-31 the V rows of the CTA's heads). With APPEND_HERE the
+// producer also performs the fused KV append (CUDA-core path; the tensor-core
+// consumers append themselves).
+template <typename T, int D, bool BAL, bool APPEND_HERE>
+__device__ void produce(const DecodeParams& p, const Work& w, const Smem& sm, int head0, int lane) {
   const int STAGES = p.stages;
-  const int stage_bytes = 2 * p.tile_bytes;
+  const int tile = p.tile_bytes, stage_bytes = 2 * tile;
+  const char* base = reinterpret_cast<const char*>(lane < 16 ? p.k_cache : p.v_cache) +
+                     (int64_t)head0 * p.c_sh * (int64_t)sizeof(T);
+  const int t = lane & 15;
+  const int dst_off = (lane >> 4) * tile + t * p.smem_row_bytes;
   uint32_t it = 0;
   bool ok = true;
   int b = w.b_first, g = w.g_begin;
@@ -400,22 +475,32 @@ __device__ void produce(const DecodeParams& p, const Work& w, const Smem& sm, co
       if (lane < cnt && (my_page < 0 || (int64_t)my_page >= p.num_blocks)) set_error(p.error, kErrBadPage);
       for (int i = 0; i < cnt; ++i, ++it) {
         const int page = __shfl_sync(kFull, my_page, i);
+        if (APPEND_HERE && p.k_new != nullptr && lp + i == s.s1 - s.s0 - 1)
+          append_rows<T, D>(p, s.b, page, head0, p.heads_per_cta, lane);
+        const bool in_pool = page >= 0 && (int64_t)page < p.num_blocks;
+        const int st = it % STAGES;
         int good = 1;
         if (lane == 0) {
-          const int st = it % STAGES;
-          if (!mbar_wait_bounded(&sm.empty_bar[st], ((it / STAGES) & 1) ^ 1)) {
+          if (!mbar_wait_bounded(&sm.empty_bar[st], ((it / STAGES) & 1) ^ 1))
             good = 0;
-          } else {
-            mbar_arrive_expect_tx(&sm.full_bar[st], stage_bytes);
-            uint8_t* dst = sm.stages + st * stage_bytes;
-            // an out-of-range page (reported above) reads as zeros: TMA fills outside the tensor
-            tma_load_4d(dst, tk, 0, 0, head_coord, page, &sm.full_bar[st]);
-            tma_load_4d(dst + p.tile_bytes, tv, 0, 0, head_coord, page, &sm.full_bar[st]);
-          }
+          else if (in_pool)
+            mbar_arrive_expect_tx(&sm.full_bar[st], 2 * kBlockSize * p.row_bytes);
         }
         if (!__shfl_sync(kFull, good, 0)) {
           ok = false;
           break;
+        }
+        uint8_t* dst = sm.stages + st * stage_bytes;
+        if (in_pool) {
+          bulk_copy_g2s(dst + dst_off, base + ((int64_t)page * p.c_sblk + (int64_t)t * p.c_stok) * (int64_t)sizeof(T),
+                        p.row_bytes, &sm.full_bar[st]);
+        } else {
+          // a page outside the pool (reported above) reads as zeros
+          for (int i = lane * 16; i < stage_bytes; i += 32 * 16)
+            *reinterpret_cast<uint4*>(dst + i) = make_uint4(0, 0, 0, 0);
+          fence_proxy_async_smem();  // before later bulk copies refill this stage
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.full_bar[st]);
         }
       }
     }
@@ -465,7 +550,7 @@ __device__ void publish_and_merge(const DecodeParams& p, const Work& w, const Se
       const int sw = (int)((int64_t)w.total * wi / w.w_eff);
       return 2 * (int64_t)wi + (sw < sb0 ? 1 : 0);
     };
-    for (int h = 0; h < nh; ++h) merge_parts<T, D>(p, s.b, head0 + h, nparts, slot_of, lane);
+    merge_rows<T, D>(p, s.b, head0, nh, nparts, slot_of, lane);
   }
 }
 
@@ -485,6 +570,7 @@ __device__ void consume_fma(const DecodeParams& p, const Work& w, const Smem& sm
   float* pw = sm.p_buf + warp * GW * kBlockSize;
   const int half = lane & 1;
   const int STAGES = p.stages, stage_bytes = 2 * p.tile_bytes;
+  const int rs = p.smem_row_bytes / (int)sizeof(T);  // tile row stride (elements)
 
   uint32_t it = 0;
   bool first_seg = true;
@@ -522,13 +608,13 @@ __device__ void consume_fma(const DecodeParams& p, const Work& w, const Smem& sm
         ok = false;
         break;
       }
-      const T* kt = reinterpret_cast<const T*>(sm.stages + st * stage_bytes) + kh * kBlockSize * D;
-      const T* vt = reinterpret_cast<const T*>(sm.stages + st * stage_bytes + p.tile_bytes) + kh * kBlockSize * D;
+      const T* kt = reinterpret_cast<const T*>(sm.stages + st * stage_bytes) + kh * D;
+      const T* vt = reinterpret_cast<const T*>(sm.stages + st * stage_bytes + p.tile_bytes) + kh * D;
       const int valid = ctx - lp * kBlockSize;
       if (valid >= kBlockSize)
-        page_update<T, D, GW, false>(kt, vt, valid, qv, m, l, acc, pw, lane);
+        page_update<T, D, GW, false>(kt, vt, rs, valid, qv, m, l, acc, pw, lane);
       else
-        page_update<T, D, GW, true>(kt, vt, valid, qv, m, l, acc, pw, lane);
+        page_update<T, D, GW, true>(kt, vt, rs, valid, qv, m, l, acc, pw, lane);
       if (lane == 0) mbar_arrive(&sm.empty_bar[st]);
     }
     if (!__all_sync(kFull, ok)) {
@@ -589,19 +675,18 @@ __device__ void consume_fma(const DecodeParams& p, const Work& w, const Smem& sm
 // probabilities never leave registers.
 template <typename T, int D, bool BAL>
 __device__ void consume_mma(const DecodeParams& p, const Work& w, const Smem& sm, int kh, int kvh, int lane) {
-  constexpr int PITCH = mma_row_pitch(D);  // elements per smem row (odd number of 16-byte chunks)
-  constexpr int KS = D / 16;               // QK k-steps
-  constexpr int NT = D / 8;                // PV n-tiles
-  constexpr int DCH = D / 8;               // 16-byte chunks per row (16-bit elements)
+  constexpr int KS = D / 16;                // QK k-steps
+  constexpr int NT = D / 8;                 // PV n-tiles
   const int G = p.num_heads / p.num_kv_heads;
   const int head0 = kvh * G;
   const int qr = lane >> 2, qc = lane & 3;
   const bool real_row = qr < G;
   const float c = p.scale_log2;
   const int STAGES = p.stages, stage_bytes = 2 * p.tile_bytes;
-  // per-lane ldmatrix row offsets inside one [16 tok][PITCH] head tile
-  const int k_off = (((lane >> 4) & 1) * 8 + (lane & 7)) * PITCH + ((lane >> 3) & 1) * 8;
-  const int v_off = (((lane >> 3) & 1) * 8 + (lane & 7)) * PITCH + ((lane >> 4) & 1) * 8;
+  const int rs = p.smem_row_bytes / (int)sizeof(T);  // tile row stride (elements)
+  // per-lane ldmatrix rows: K (x4: chunk pair x token halves), V (x4.trans: token halves x chunk pair)
+  const int k_row = (((lane >> 4) & 1) * 8 + (lane & 7)) * rs + ((lane >> 3) & 1) * 8;
+  const int v_row = (((lane >> 3) & 1) * 8 + (lane & 7)) * rs + ((lane >> 4) & 1) * 8;
 
   uint32_t it = 0;
   bool first_seg = true;
@@ -619,6 +704,24 @@ __device__ void consume_mma(const DecodeParams& p, const Work& w, const Smem& sm
         qa[ks][1] = real_row ? __ldg(reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 8 + 2 * qc)) : 0u;
       }
     }
+    // Fused KV append (this warp's KV head): the token at position ctx - 1 is
+    // stored to the pool now and patched into the shared-memory tile of the last
+    // page when that page arrives (so no cross-proxy ordering with its copy).
+    constexpr int RC = D / 8;  // 16-byte chunks of one head row
+    const int ctx_raw = __ldg(&p.context_lens[s.b]);
+    const bool append = p.k_new != nullptr && s.lp1 == n_b && ctx_raw >= 1 && (ctx_raw - 1) / kBlockSize < p.max_blocks;
+    const int a_slot = (ctx_raw - 1) & (kBlockSize - 1);
+    const int a_which = lane / RC, a_chunk = lane % RC;
+    uint4 a_row = make_uint4(0, 0, 0, 0);
+    if (append && lane < 2 * RC) {
+      a_row = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a_which ? p.v_new : p.k_new) +
+                                                   (int64_t)s.b * p.n_stok + (int64_t)kvh * p.n_sh) + a_chunk);
+      const int page = __ldg(p.block_table + (int64_t)s.b * p.bt_sb + n_b - 1);
+      if (page >= 0 && (int64_t)page < p.num_blocks)
+        *(reinterpret_cast<uint4*>(const_cast<T*>(reinterpret_cast<const T*>(a_which ? p.v_cache : p.k_cache)) +
+                                   (int64_t)page * p.c_sblk + (int64_t)a_slot * p.c_stok + (int64_t)kvh * p.c_sh) +
+          a_chunk) = a_row;
+    }
     float m = -INFINITY, l = 0.f;
     float o[NT][4];
 #pragma unroll
@@ -631,16 +734,28 @@ __device__ void consume_mma(const DecodeParams& p, const Work& w, const Smem& sm
         ok = false;
         break;
       }
-      const T* kt = reinterpret_cast<const T*>(sm.stages + st * stage_bytes) + kh * kBlockSize * PITCH;
-      T* vt = reinterpret_cast<T*>(sm.stages + st * stage_bytes + p.tile_bytes) + kh * kBlockSize * PITCH;
+      T* kt = reinterpret_cast<T*>(sm.stages + st * stage_bytes) + kh * D;
+      T* vt = reinterpret_cast<T*>(sm.stages + st * stage_bytes + p.tile_bytes) + kh * D;
       const int valid = ctx - lp * kBlockSize;
+      const bool patch = append && lp == n_b - 1;
+      if (patch || valid < kBlockSize) {
+        // slots past the context may hold anything: zero their V rows (P is 0
+        // there, but 0 * NaN would not be); then place the appended row
+        for (int i = lane; i < (kBlockSize - valid) * RC; i += 32)
+          *reinterpret_cast<uint4*>(vt + (valid + i / RC) * rs + (i % RC) * 8) = make_uint4(0, 0, 0, 0);
+        if (patch && lane < 2 * RC)
+          *reinterpret_cast<uint4*>((a_which ? vt : kt) + a_slot * rs + a_chunk * 8) = a_row;
+        // order these generic-proxy writes before the bulk copy that later refills the stage
+        fence_proxy_async_smem();
+        __syncwarp();
+      }
 
       // ---- scores
       float sa[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks) {
         uint32_t r0, r1, r2, r3;
-        ldsm_x4(kt + k_off + 16 * ks, r0, r1, r2, r3);
+        ldsm_x4(kt + k_row + 16 * ks, r0, r1, r2, r3);
         mma16816<T>(sa[0], qa[ks][0], 0u, qa[ks][1], 0u, r0, r1);
         mma16816<T>(sa[1], qa[ks][0], 0u, qa[ks][1], 0u, r2, r3);
       }
@@ -650,13 +765,6 @@ __device__ void consume_mma(const DecodeParams& p, const Work& w, const Smem& sm
 #pragma unroll
         for (int i = 0; i < 4; ++i)
           if ((i >> 1) * 8 + 2 * qc + (i & 1) >= valid) sv[i] = -INFINITY;
-        // slots past the context may hold anything: zero their V rows (P is 0 there,
-        // but 0 * NaN would not be)
-        for (int i = lane; i < (kBlockSize - valid) * DCH; i += 32)
-          *reinterpret_cast<uint4*>(vt + (valid + i / DCH) * PITCH + (i % DCH) * 8) = make_uint4(0, 0, 0, 0);
-        // order these generic-proxy writes before the TMA that later refills the stage
-        fence_proxy_async_smem();
-        __syncwarp();
       }
       float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
       mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 1));
@@ -686,7 +794,7 @@ __device__ void consume_mma(const DecodeParams& p, const Work& w, const Smem& sm
 #pragma unroll
       for (int np = 0; np < NT / 2; ++np) {
         uint32_t r0, r1, r2, r3;
-        ldsm_x4_trans(vt + v_off + 16 * np, r0, r1, r2, r3);
+        ldsm_x4_trans(vt + v_row + 16 * np, r0, r1, r2, r3);
         mma16816<T>(o[2 * np], pa0, 0u, pa2, 0u, r0, r1);
         mma16816<T>(o[2 * np + 1], pa0, 0u, pa2, 0u, r2, r3);
       }
@@ -729,8 +837,7 @@ __device__ void consume_mma(const DecodeParams& p, const Work& w, const Smem& sm
 
 template <typename T, int D, int GW, bool BAL>
 __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
-    paged_decode_fma_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
-                            const DecodeParams p) {
+    paged_decode_fma_kernel(const DecodeParams p) {
   static_assert((kBlockSize / (32 / (D / Elem<T>::kPerChunk))) % 4 == 0, "token groups must be float4-sized");
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ int32_t warp_tot[32];
@@ -745,14 +852,10 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
     }
     fence_mbar_init();
   }
-  if (warp == NCW && lane == 0) {
-    tma_prefetch_desc(&tmap_k);
-    tma_prefetch_desc(&tmap_v);
-  }
   const Work w = setup_work<T, D, BAL>(p, sm, warp_tot, blockIdx.y * HG * G, (blockIdx.y + 1) * HG * G);
   if (w.g_begin >= w.g_end) return;
   if (warp == NCW) {
-    produce<BAL>(p, w, sm, &tmap_k, &tmap_v, blockIdx.y * HG, lane);
+    produce<T, D, BAL, true>(p, w, sm, blockIdx.y * HG, lane);
     return;
   }
   if (warp > NCW) return;
@@ -762,8 +865,7 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
 
 template <typename T, int D, bool BAL>
 __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
-    paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
-                            const DecodeParams p) {
+    paged_decode_mma_kernel(const DecodeParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ int32_t warp_tot[32];
   const Smem sm = carve_smem(smem_raw, p);
@@ -777,14 +879,10 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
     }
     fence_mbar_init();
   }
-  if (warp == NCW && lane == 0) {
-    tma_prefetch_desc(&tmap_k);
-    tma_prefetch_desc(&tmap_v);
-  }
   const Work w = setup_work<T, D, BAL>(p, sm, warp_tot, blockIdx.y * HG * G, (blockIdx.y + 1) * HG * G);
   if (w.g_begin >= w.g_end) return;
   if (warp == NCW) {
-    produce<BAL>(p, w, sm, &tmap_k, &tmap_v, blockIdx.y * HG, lane);
+    produce<T, D, BAL, false>(p, w, sm, blockIdx.y * HG, lane);
     return;
   }
   if (warp > NCW) return;
@@ -813,8 +911,8 @@ int decode_smem_bytes(int tile_bytes, int pbuf_bytes, int stages, int prefix_ent
 }
 
 template <typename Kern>
-static cudaError_t launch_with_smem(Kern kern, int* granted, const CUtensorMap& tk, const CUtensorMap& tv,
-                                   const DecodeParams& p, const LaunchShape& s, cudaStream_t stream) {
+static cudaError_t launch_with_smem(Kern kern, int* granted, const DecodeParams& p, const LaunchShape& s,
+                                   cudaStream_t stream) {
   // raise the dynamic shared-memory limit once per device (and when a call needs more)
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -824,53 +922,49 @@ static cudaError_t launch_with_smem(Kern kern, int* granted, const CUtensorMap& 
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) granted[dev] = s.smem_bytes;
   }
-  kern<<<s.grid, s.block, s.smem_bytes, stream>>>(tk, tv, p);
+  kern<<<s.grid, s.block, s.smem_bytes, stream>>>(p);
   return cudaGetLastError();
 }
 
 template <typename T, int D, int GW, bool BAL>
-static cudaError_t launch_fma(const CUtensorMap& tk, const CUtensorMap& tv, const DecodeParams& p,
-                              const LaunchShape& s, cudaStream_t st) {
+static cudaError_t launch_fma(const DecodeParams& p, const LaunchShape& s, cudaStream_t st) {
   static int granted[64] = {0};
-  return launch_with_smem(paged_decode_fma_kernel<T, D, GW, BAL>, granted, tk, tv, p, s, st);
+  return launch_with_smem(paged_decode_fma_kernel<T, D, GW, BAL>, granted, p, s, st);
 }
 
 template <typename T, int D, bool BAL>
-static cudaError_t launch_mma(const CUtensorMap& tk, const CUtensorMap& tv, const DecodeParams& p,
-                              const LaunchShape& s, cudaStream_t st) {
+static cudaError_t launch_mma(const DecodeParams& p, const LaunchShape& s, cudaStream_t st) {
   static int granted[64] = {0};
-  return launch_with_smem(paged_decode_mma_kernel<T, D, BAL>, granted, tk, tv, p, s, st);
+  return launch_with_smem(paged_decode_mma_kernel<T, D, BAL>, granted, p, s, st);
 }
 
 template <typename T, int D>
-static cudaError_t launch_d(int gw, bool bal, const CUtensorMap& tk, const CUtensorMap& tv, const DecodeParams& p,
-                            const LaunchShape& s, cudaStream_t st) {
+static cudaError_t launch_d(int gw, bool bal, const DecodeParams& p, const LaunchShape& s, cudaStream_t st) {
   if constexpr (sizeof(T) == 2) {
-    return bal ? launch_mma<T, D, true>(tk, tv, p, s, st) : launch_mma<T, D, false>(tk, tv, p, s, st);
+    return bal ? launch_mma<T, D, true>(p, s, st) : launch_mma<T, D, false>(p, s, st);
   } else {
-    if (gw == 1) return bal ? launch_fma<T, D, 1, true>(tk, tv, p, s, st) : launch_fma<T, D, 1, false>(tk, tv, p, s, st);
-    return bal ? launch_fma<T, D, 2, true>(tk, tv, p, s, st) : launch_fma<T, D, 2, false>(tk, tv, p, s, st);
+    if (gw == 1) return bal ? launch_fma<T, D, 1, true>(p, s, st) : launch_fma<T, D, 1, false>(p, s, st);
+    return bal ? launch_fma<T, D, 2, true>(p, s, st) : launch_fma<T, D, 2, false>(p, s, st);
   }
 }
 
 template <typename T>
-static cudaError_t launch_t(int head_dim, int gw, bool bal, const CUtensorMap& tk, const CUtensorMap& tv,
-                            const DecodeParams& p, const LaunchShape& s, cudaStream_t st) {
+static cudaError_t launch_t(int head_dim, int gw, bool bal, const DecodeParams& p, const LaunchShape& s,
+                            cudaStream_t st) {
   switch (head_dim) {
-    case 64: return launch_d<T, 64>(gw, bal, tk, tv, p, s, st);
-    case 112: return launch_d<T, 112>(gw, bal, tk, tv, p, s, st);
-    case 128: return launch_d<T, 128>(gw, bal, tk, tv, p, s, st);
+    case 64: return launch_d<T, 64>(gw, bal, p, s, st);
+    case 112: return launch_d<T, 112>(gw, bal, p, s, st);
+    case 128: return launch_d<T, 128>(gw, bal, p, s, st);
     default: return cudaErrorInvalidValue;
   }
 }
 
-cudaError_t launch_paged_decode(int dtype, int head_dim, int gw, bool balanced, const CUtensorMap& tmap_k,
-                                const CUtensorMap& tmap_v, const DecodeParams& p, const LaunchShape& shape,
-                                cudaStream_t stream) {
+cudaError_t launch_paged_decode(int dtype, int head_dim, int gw, bool balanced, const DecodeParams& p,
+                                const LaunchShape& shape, cudaStream_t stream) {
   switch (dtype) {
-    case UBX_DTYPE_F32: return launch_t<float>(head_dim, gw, balanced, tmap_k, tmap_v, p, shape, stream);
-    case UBX_DTYPE_BF16: return launch_t<__nv_bfloat16>(head_dim, gw, balanced, tmap_k, tmap_v, p, shape, stream);
-    case UBX_DTYPE_F16: return launch_t<__half>(head_dim, gw, balanced, tmap_k, tmap_v, p, shape, stream);
+    case UBX_DTYPE_F32: return launch_t<float>(head_dim, gw, balanced, p, shape, stream);
+    case UBX_DTYPE_BF16: return launch_t<__nv_bfloat16>(head_dim, gw, balanced, p, shape, stream);
+    case UBX_DTYPE_F16: return launch_t<__half>(head_dim, gw, balanced, p, shape, stream);
     default: return cudaErrorInvalidValue;
   }
 }

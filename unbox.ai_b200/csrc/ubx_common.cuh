@@ -1,6 +1,6 @@
 // Device helpers shared by the unbox_b200 kernels (sm_100a).
 //
-// mbarrier + TMA (cp.async.bulk.tensor) primitives written as inline PTX, the
+// mbarrier + bulk-copy (cp.async.bulk, TMA engine) primitives written as inline PTX, the
 // 16-byte element converters used when K/V chunks are unpacked from shared
 // memory, and the device error word.
 #pragma once
@@ -82,20 +82,19 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// ---------------------------------------------------------------- TMA
-__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
-  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+// Same for global memory: generic writes before a later TMA read of them.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
-// 4-D tiled bulk tensor load global -> shared, completion counted in bytes on
-// `bar`. No multicast: every CTA reads its own tiles from this GPU's HBM.
-__device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* map, int c0, int c1, int c2,
-                                            int c3, uint64_t* bar) {
+// ---------------------------------------------------------------- TMA
+// Bulk copy (TMA engine, non-tensor) of `bytes` contiguous bytes global ->
+// shared, completion counted in bytes on `bar`. Both addresses 16-byte
+// aligned, bytes a multiple of 16. No multicast.
+__device__ __forceinline__ void bulk_copy_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4, %5}], [%6];"
-      ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
-        "r"(smem_u32(bar))
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(gmem_src)), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
 
@@ -106,7 +105,6 @@ struct Elem;
 template <>
 struct Elem<float> {
   static constexpr int kPerChunk = 4;   // elements per 16-byte chunk
-  static constexpr CUtensorMapDataType kTmaType = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   __device__ __forceinline__ static void unpack(const uint4& v, float (&f)[4]) {
     f[0] = __uint_as_float(v.x);
     f[1] = __uint_as_float(v.y);
@@ -122,7 +120,6 @@ struct Elem<float> {
 template <>
 struct Elem<__nv_bfloat16> {
   static constexpr int kPerChunk = 8;
-  static constexpr CUtensorMapDataType kTmaType = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   // bf16 is the upper half of an fp32: widening is a shift or a mask.
   __device__ __forceinline__ static void unpack(const uint4& v, float (&f)[8]) {
     f[0] = __uint_as_float(v.x << 16);
@@ -147,7 +144,6 @@ struct Elem<__nv_bfloat16> {
 template <>
 struct Elem<__half> {
   static constexpr int kPerChunk = 8;
-  static constexpr CUtensorMapDataType kTmaType = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   __device__ __forceinline__ static void unpack(const uint4& v, float (&f)[8]) {
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll

@@ -12,17 +12,18 @@ constexpr int kMaxStages = 8;           // pipeline depth limit (mbarrier slots 
 constexpr int kMaxConsumerWarps = 8;    // consumer warps per CTA
 constexpr int kMaxBatchSmem = 2048;     // balanced schedule keeps a (B+1) page prefix in smem
 constexpr int kMaxTileBytes = 36864;    // one K (or V) page tile of a head group
-constexpr int kSmemLimit = 226 * 1024;  // dynamic smem budget: 227 KB opt-in minus static smem and slack
+constexpr int kSmemLimit = 227 * 1024 - 512;  // dynamic smem budget: 227 KB opt-in minus static smem
 
 // Workspace layout prefix: [error word + reserved | merge counters | partials].
 constexpr size_t kWsHeaderBytes = 256;                      // error word at offset 0
 constexpr size_t kWsCounterEntries = 65536;                 // balanced-schedule merge counters
 constexpr size_t kWsCounterBytes = kWsCounterEntries * 4;   // must be zero before a call
 
-// Row pitch (elements) of a K/V page-tile row in shared memory on the 16-bit
-// tensor-core path: head_dim rounded up to an odd number of 16-byte chunks, so
-// the 8 rows one ldmatrix phase reads sit in 8 different bank groups.
-constexpr int mma_row_pitch(int head_dim) { return ((head_dim / 8) | 1) * 8; }
+// Shared-memory row pitch of a page tile: one token row of the CTA's heads
+// (heads * head_dim elements, contiguous in the KVPool layout) plus 16 bytes
+// when needed to make the pitch an odd number of 16-byte chunks, so that the 8
+// token rows one ldmatrix phase reads fall in 8 different bank groups.
+constexpr int tile_row_pitch(int row_bytes) { return ((row_bytes / 16) & 1) ? row_bytes : row_bytes + 16; }
 
 struct DecodeParams {
   const void* q;
@@ -38,7 +39,9 @@ struct DecodeParams {
   int max_blocks;
   int64_t num_blocks;
   float scale_log2;      // softmax scale * log2(e): scores live in the exp2 domain
-  int tile_bytes;        // bytes of one K (or V) page tile in shared memory
+  int tile_bytes;        // bytes of one K (or V) page tile in shared memory (16 rows)
+  int row_bytes;         // bytes of one token row of the CTA's heads (one bulk copy)
+  int smem_row_bytes;    // row pitch of a tile in shared memory
   int pbuf_bytes;        // bytes of the fp32 path's probability buffers
   int heads_per_cta;     // KV heads in one page tile (HG)
   int warps_per_kv;      // consumer warps sharing one KV head (WPK = G / GW)
@@ -49,6 +52,15 @@ struct DecodeParams {
   float2* part_ml;       // [slots][num_heads] (running max in log2 units, denominator)
   int32_t* counters;     // [batch][num_kv_heads * warps_per_kv] merge counters (balanced)
   int32_t* error;        // device error word
+  // raw pool views (fused append writes the new token's rows through them)
+  const void* k_cache;
+  const void* v_cache;
+  int64_t c_sblk, c_stok, c_sh;
+  // fused append (null when the call only attends): row t of k_new / v_new is
+  // the token at position context_lens[t] - 1
+  const void* k_new;
+  const void* v_new;
+  int64_t n_stok, n_sh;
 };
 
 // Message returned by ubx_last_error() on this host thread (set by any entry point).
@@ -65,9 +77,8 @@ struct LaunchShape {
 // barriers + optional page prefix).
 int decode_smem_bytes(int tile_bytes, int pbuf_bytes, int stages, int prefix_entries);
 
-cudaError_t launch_paged_decode(int dtype, int head_dim, int gw, bool balanced, const CUtensorMap& tmap_k,
-                                const CUtensorMap& tmap_v, const DecodeParams& p, const LaunchShape& shape,
-                                cudaStream_t stream);
+cudaError_t launch_paged_decode(int dtype, int head_dim, int gw, bool balanced, const DecodeParams& p,
+                                const LaunchShape& shape, cudaStream_t stream);
 
 cudaError_t launch_lse_combine(int dtype, int head_dim, const DecodeParams& p, cudaStream_t stream);
 

@@ -33,6 +33,9 @@ SIGNATURES = {
     "ubx_paged_decode_attention": (_i32, [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _i64,
                                           _i64, _i32, _i32, _i32, _i32, _i32, _i64, _i32, _f32, _i32, _i32, _i32,
                                           _vp, _sz, _vp]),
+    "ubx_paged_decode_append_attention": (_i32, [_vp, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64,
+                                                 _vp, _i64, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i64,
+                                                 _i32, _f32, _i32, _i32, _i32, _vp, _sz, _vp]),
     "ubx_read_device_error": (_i32, [_vp, ctypes.POINTER(ctypes.c_int32), _i32, _vp]),
     "ubx_paged_decode_attention_noalloc": (_i32, [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp,
                                                   _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i64, _i32, _f32, _i32,

@@ -132,10 +132,17 @@ def _int32(t: torch.Tensor, name: str) -> torch.Tensor:
 def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
                     context_lens: torch.Tensor, scale: Optional[float] = None, *, out: Optional[torch.Tensor] = None,
                     schedule: str = "auto", split_pages: int = 0,
-                    workspace: Optional[DecodeWorkspace] = None) -> torch.Tensor:
+                    workspace: Optional[DecodeWorkspace] = None, k_new: Optional[torch.Tensor] = None,
+                    v_new: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Paged GQA decode attention: out[b, h] = softmax(scale * q[b, h] K^T) V over
-    the first context_lens[b] positions of sequence b (see module docstring)."""
+    the first context_lens[b] positions of sequence b (see module docstring).
+
+    With ``k_new``/``v_new`` ((B, KVH, D) rows of the token being decoded) the
+    rows are first appended at position context_lens[b] - 1, in the same launch.
+    """
     dev = _require_cuda(q, k_cache, v_cache, block_table, context_lens)
+    if (k_new is None) != (v_new is None):
+        raise ValueError("pass both k_new and v_new, or neither")
     if q.dim() != 3 or k_cache.dim() != 4 or v_cache.shape != k_cache.shape:
         raise ValueError(f"expected q (B, H, D) and caches (NB, bs, KVH, D); got {tuple(q.shape)}, "
                          f"{tuple(k_cache.shape)}, {tuple(v_cache.shape)}")
@@ -168,14 +175,38 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
     ws = workspace or workspace_for(dev)
     buf = ws.ensure(B, H, D, max_blocks, split_pages)
     lib = _L.load()
-    st = lib.ubx_paged_decode_attention(
-        q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(),
-        k_cache.stride(0), k_cache.stride(1), k_cache.stride(2), block_table.data_ptr(), block_table.stride(0),
-        context_lens.data_ptr(), out.data_ptr(), out.stride(0), out.stride(1), B, H, KVH, D, bs, NB, max_blocks,
-        float(scale), _DTYPES[q.dtype], _SCHEDULES[schedule], int(split_pages), buf.data_ptr(), buf.numel(),
-        _stream(dev))
-    _L.check(st, "paged_decode_attention")
+    tail = (block_table.data_ptr(), block_table.stride(0), context_lens.data_ptr(), out.data_ptr(), out.stride(0),
+            out.stride(1), B, H, KVH, D, bs, NB, max_blocks, float(scale), _DTYPES[q.dtype], _SCHEDULES[schedule],
+            int(split_pages), buf.data_ptr(), buf.numel(), _stream(dev))
+    if k_new is None:
+        st = lib.ubx_paged_decode_attention(
+            q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(),
+            k_cache.stride(0), k_cache.stride(1), k_cache.stride(2), *tail)
+        _L.check(st, "paged_decode_attention")
+    else:
+        _require_cuda(q, k_new, v_new)
+        if k_new.shape != (B, KVH, D) or v_new.shape != k_new.shape:
+            raise ValueError(f"k_new / v_new must be ({B}, {KVH}, {D})")
+        if k_new.dtype != q.dtype or v_new.dtype != q.dtype:
+            raise TypeError("k_new / v_new must have the cache dtype")
+        if k_new.stride() != v_new.stride() or k_new.stride(-1) != 1:
+            raise ValueError("k_new and v_new need equal strides and a contiguous last dimension")
+        st = lib.ubx_paged_decode_append_attention(
+            k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0), k_new.stride(1),
+            q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(),
+            k_cache.stride(0), k_cache.stride(1), k_cache.stride(2), *tail)
+        _L.check(st, "paged_decode_append_attention")
     return out
+
+
+def paged_decode_append_attention(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, k_cache: torch.Tensor,
+                                  v_cache: torch.Tensor, block_table: torch.Tensor, context_lens: torch.Tensor,
+                                  scale: Optional[float] = None, *, out: Optional[torch.Tensor] = None,
+                                  schedule: str = "auto") -> torch.Tensor:
+    """One decode layer's KV append and attention in one launch: the engine's
+    append loop (engine.py:213-215) and attention call (:221-224)."""
+    return paged_attention(q, k_cache, v_cache, block_table, context_lens, scale, out=out, schedule=schedule,
+                           k_new=k_new, v_new=v_new)
 
 
 def paged_attention_split(q, k_cache, v_cache, block_table, context_lens, scale=None, split_pages: int = 32,

@@ -103,11 +103,15 @@ class Layout:
         return (self.context_lens.astype(np.int64) - 1).astype(np.int32)
 
     def slot_mapping(self) -> np.ndarray:
-        """slot = block_table[b, pos // bs] * bs + pos % bs (kvcache.py:338-339)."""
+        """slot = block_table[b, pos // bs] * bs + pos % bs (kvcache.py:338-339);
+        -1 (padding, nothing appended) for an empty context or a -1 page."""
         pos = self.positions().astype(np.int64)
-        b = np.arange(self.batch)
-        pages = self.block_table[b, pos // self.block_size].astype(np.int64)
-        return pages * self.block_size + pos % self.block_size
+        out = np.full(self.batch, -1, dtype=np.int64)
+        ok = pos >= 0
+        b = np.arange(self.batch)[ok]
+        pages = self.block_table[b, pos[ok] // self.block_size].astype(np.int64)
+        out[ok] = np.where(pages >= 0, pages * self.block_size + pos[ok] % self.block_size, -1)
+        return out
 
     def kv_tokens(self) -> int:
         """Σ ctx: token rows one attention call reads per KV head."""
