@@ -51,6 +51,8 @@ def parse():
                     help="launch every op from Python instead of replaying the step as one CUDA graph")
     ap.add_argument("--separate", action="store_true",
                     help="KV append as its own launch before attention (default: fused into one launch)")
+    ap.add_argument("--no-overlap", dest="overlap", action="store_false",
+                    help="no programmatic dependent launch between consecutive layer-calls")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     return ap.parse_args()
@@ -232,8 +234,10 @@ def main():
         if args.separate:
             pkg.paged_attention(q, dev["k_caches"][l], dev["v_caches"][l], block_table, context_lens, out=out, **kw)
         else:
+            # the previous kernel on the stream is another layer's attention (or a copy):
+            # it writes neither this layer's pool nor the block table / context lengths
             pkg.paged_attention(q, dev["k_caches"][l], dev["v_caches"][l], block_table, context_lens, out=out,
-                                k_new=k_new, v_new=v_new, **kw)
+                                k_new=k_new, v_new=v_new, overlap_previous=args.overlap, **kw)
         if timer is not None:
             timer[1].record()
 
@@ -380,6 +384,7 @@ def main():
                 "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms / args.steps, 4)},
         "clocks": clocks.summary(),
         "graph": bool(graph is not None), "append": "separate launch" if args.separate else "fused",
+        "overlap_previous": bool(args.overlap and not args.separate),
     }
     achieved = kernel_bytes / (kernel_avg_ms / 1e3) / 1e9
     traffic = profiled_traffic(args.workload)

@@ -53,6 +53,14 @@ extern "C" {
 #define UBX_SCHEDULE_BALANCED 1 /* persistent grid, equal pages per CTA, in-kernel LSE merge */
 #define UBX_SCHEDULE_SPLIT 2    /* fixed split-KV chunks per sequence + LSE combine kernel */
 
+/* call flags (ubx_paged_decode_append_attention) */
+#define UBX_FLAG_OVERLAP_PREVIOUS 1 /* launch with programmatic dependent launch: the kernel may start, and
+                                       stream pool pages, while the previous kernel on the stream is still
+                                       running. The caller promises that kernel writes neither the K/V pool,
+                                       block_table nor context_lens (true in a decode step, where it is the
+                                       previous layer's attention or this layer's QKV projection). q, k_new,
+                                       v_new, out and the workspace are only touched after it completed. */
+
 const char* ubx_status_string(int status);
 /* Message of the last failing call on this host thread ("" if none). */
 const char* ubx_last_error(void);
@@ -139,6 +147,7 @@ int ubx_paged_decode_attention(const void* q, int64_t q_s_b, int64_t q_s_h, cons
  * InferenceEngine.decode_step (unbox_platform/infer/engine.py:213-224), with
  * the slot arithmetic of PagedKVCache.write_kv (kvcache.py:338-339).
  *   k_new, v_new: (batch, num_kv_heads, head_dim), strides (new_s_tok, new_s_head)
+ *   flags:        0 or UBX_FLAG_OVERLAP_PREVIOUS
  * The other arguments are those of ubx_paged_decode_attention.
  */
 int ubx_paged_decode_append_attention(const void* k_new, const void* v_new, int64_t new_s_tok, int64_t new_s_head,
@@ -148,7 +157,7 @@ int ubx_paged_decode_append_attention(const void* k_new, const void* v_new, int6
                                       void* out, int64_t o_s_b, int64_t o_s_h, int batch, int num_heads,
                                       int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
                                       int max_blocks_per_seq, float scale, int dtype, int schedule, int split_pages,
-                                      void* workspace, size_t workspace_bytes, void* stream);
+                                      int flags, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Allocation-free variant of ubx_paged_decode_attention. No counterpart in the

@@ -320,3 +320,40 @@ def test_fused_append_equals_separate_launches(dtype, schedule, pkg):
     pkg.check_device_errors()
     assert torch.equal(a["k_cache"], f["k_cache"]) and torch.equal(a["v_cache"], f["v_cache"])
     assert torch.equal(ref, out)
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_overlap_previous_layers_match(graph, pkg):
+    """Programmatic overlap between consecutive layer calls changes nothing."""
+    wl = pkg.workloads
+    lay = wl.layout_uniform(32, 24, 1, 900)
+    L = 4
+    ref_dev = wl.materialize_device(lay, 3, "bfloat16", 0.5, L)
+    ovl_dev = wl.materialize_device(lay, 3, "bfloat16", 0.5, L)
+    outs_ref = [torch.empty_like(ref_dev["q"][l]) for l in range(L)]
+    outs_ovl = [torch.empty_like(ovl_dev["q"][l]) for l in range(L)]
+
+    def step(d, outs, overlap):
+        for l in range(L):
+            pkg.paged_attention(d["q"][l], d["k_caches"][l], d["v_caches"][l], d["block_table"], d["context_lens"],
+                                out=outs[l], k_new=d["k_new"][l], v_new=d["v_new"][l], overlap_previous=overlap)
+
+    step(ref_dev, outs_ref, False)
+    if graph:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            pkg.workspace_for(torch.device(DEV)).ensure(lay.batch, 16, 112, lay.max_blocks)
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step(ovl_dev, outs_ovl, True)
+        g.replay()
+    else:
+        step(ovl_dev, outs_ovl, True)
+    torch.cuda.synchronize()
+    pkg.check_device_errors()
+    for l in range(L):
+        assert torch.equal(outs_ref[l], outs_ovl[l])
+        assert torch.equal(ref_dev["k_caches"][l], ovl_dev["k_caches"][l])
+        assert torch.equal(ref_dev["v_caches"][l], ovl_dev["v_caches"][l])

@@ -256,8 +256,8 @@ int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache
                 int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head, const int32_t* block_table, int64_t bt_s_row,
                 const int32_t* context_lens, void* out, int64_t o_s_b, int64_t o_s_h, int batch, int num_heads,
                 int num_kv_heads, int head_dim, int block_size, int64_t num_blocks, int max_blocks_per_seq,
-                float scale, int dtype, int schedule, int split_pages, void* workspace, size_t workspace_bytes,
-                const AppendArgs* app, void* stream) {
+                float scale, int dtype, int schedule, int split_pages, int flags, void* workspace,
+                size_t workspace_bytes, const AppendArgs* app, void* stream) {
   g_last_error.clear();
   int st = check_shape(num_heads, num_kv_heads, head_dim, block_size, dtype);
   if (st != UBX_OK) return st;
@@ -286,6 +286,7 @@ int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache
       return fail(UBX_ERR_INVALID_ARGUMENT, "k_new / v_new rows must be 16-byte aligned");
   }
   if (!(scale > 0.f) && !(scale < 0.f)) return fail(UBX_ERR_INVALID_ARGUMENT, "scale must be finite and non-zero");
+  if (flags & ~UBX_FLAG_OVERLAP_PREVIOUS) return fail(UBX_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
   if (!workspace) return fail(UBX_ERR_WORKSPACE, "workspace is required");
 
   int sms = 0;
@@ -338,7 +339,7 @@ int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache
   p.n_stok = app ? app->s_tok : 0;
   p.n_sh = app ? app->s_head : 0;
 
-  LaunchShape shape{pl.grid, pl.block, pl.smem};
+  LaunchShape shape{pl.grid, pl.block, pl.smem, (flags & UBX_FLAG_OVERLAP_PREVIOUS) != 0};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = launch_paged_decode(dtype, head_dim, pl.gw, pl.balanced, p, shape, s);
   if (e != cudaSuccess) return cuda_fail(e, "paged_decode launch");
@@ -361,7 +362,7 @@ int ubx_paged_decode_attention(const void* q, int64_t q_s_b, int64_t q_s_h, cons
                                int split_pages, void* workspace, size_t workspace_bytes, void* stream) {
   return decode_impl(q, q_s_b, q_s_h, k_cache, v_cache, c_s_block, c_s_tok, c_s_head, block_table, bt_s_row,
                      context_lens, out, o_s_b, o_s_h, batch, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
-                     max_blocks_per_seq, scale, dtype, schedule, split_pages, workspace, workspace_bytes, nullptr,
+                     max_blocks_per_seq, scale, dtype, schedule, split_pages, 0, workspace, workspace_bytes, nullptr,
                      stream);
 }
 
@@ -372,11 +373,12 @@ int ubx_paged_decode_append_attention(const void* k_new, const void* v_new, int6
                                       void* out, int64_t o_s_b, int64_t o_s_h, int batch, int num_heads,
                                       int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
                                       int max_blocks_per_seq, float scale, int dtype, int schedule, int split_pages,
-                                      void* workspace, size_t workspace_bytes, void* stream) {
+                                      int flags, void* workspace, size_t workspace_bytes, void* stream) {
   const AppendArgs app{k_new, v_new, new_s_tok, new_s_head};
   return decode_impl(q, q_s_b, q_s_h, k_cache, v_cache, c_s_block, c_s_tok, c_s_head, block_table, bt_s_row,
                      context_lens, out, o_s_b, o_s_h, batch, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
-                     max_blocks_per_seq, scale, dtype, schedule, split_pages, workspace, workspace_bytes, &app, stream);
+                     max_blocks_per_seq, scale, dtype, schedule, split_pages, flags, workspace, workspace_bytes, &app,
+                     stream);
 }
 
 }  // extern "C"

@@ -369,10 +369,10 @@ __device__ __forceinline__ Smem carve_smem(uint8_t* smem, const DecodeParams& p)
 }
 
 // Pages this CTA streams: a contiguous range of the flattened (sequence, page)
-// list (balanced) or one chunk of one sequence (split). Rows with no context
-// are written as zeros here. Ends with a CTA barrier (publishes mbarrier init).
+// list (balanced) or one chunk of one sequence (split). Reads only
+// context_lens. Ends with a CTA barrier (publishes mbarrier init).
 template <typename T, int D, bool BAL>
-__device__ Work setup_work(const DecodeParams& p, const Smem& sm, int32_t* warp_tot, int head_lo, int head_hi) {
+__device__ Work setup_work(const DecodeParams& p, const Smem& sm, int32_t* warp_tot) {
   Work w{0, 0, 0, 1, 0, 0, 0};
   const int B = p.batch;
   if constexpr (BAL) {
@@ -389,19 +389,28 @@ __device__ Work setup_work(const DecodeParams& p, const Smem& sm, int32_t* warp_
       }
       w.b_first = lo;
     }
-    for (int b = blockIdx.x; b < B; b += gridDim.x)
-      if (sm.prefix[b + 1] == sm.prefix[b]) write_zero_row<T, D>(p, b, head_lo, head_hi, threadIdx.x, blockDim.x);
   } else {
     w.b_first = blockIdx.x / p.max_chunks;
     w.chunk = blockIdx.x % p.max_chunks;
     w.n_split = pages_of(p, w.b_first, w.chunk == 0 && blockIdx.y == 0);
     w.g_begin = w.chunk * p.split_pages;
     w.g_end = min(w.n_split, w.g_begin + p.split_pages);
-    if (w.n_split == 0 && w.chunk == 0)
-      write_zero_row<T, D>(p, w.b_first, head_lo, head_hi, threadIdx.x, blockDim.x);
     __syncthreads();
   }
   return w;
+}
+
+// Rows of sequences with nothing to attend to are written as zeros (the
+// reference raises there). Runs after the grid-dependency wait: it writes `out`.
+template <typename T, int D, bool BAL>
+__device__ void write_zero_rows(const DecodeParams& p, const Work& w, const int32_t* prefix, int head_lo,
+                                int head_hi, int tid, int nthreads) {
+  if constexpr (BAL) {
+    for (int b = blockIdx.x; b < p.batch; b += gridDim.x)
+      if (prefix[b + 1] == prefix[b]) write_zero_row<T, D>(p, b, head_lo, head_hi, tid, nthreads);
+  } else {
+    if (w.n_split == 0 && w.chunk == 0) write_zero_row<T, D>(p, w.b_first, head_lo, head_hi, tid, nthreads);
+  }
 }
 
 // Next (sequence, page range) segment of the CTA's work; b and g are the cursor.
@@ -846,15 +855,24 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.num_heads / p.num_kv_heads;
   if (threadIdx.x == 0) {
+    griddep_launch_dependents();  // the next grid may start on SMs this one frees
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&sm.full_bar[s], 1);
       mbar_init(&sm.empty_bar[s], NCW);
     }
     fence_mbar_init();
   }
-  const Work w = setup_work<T, D, BAL>(p, sm, warp_tot, blockIdx.y * HG * G, (blockIdx.y + 1) * HG * G);
-  if (w.g_begin >= w.g_end) return;
+  const Work w = setup_work<T, D, BAL>(p, sm, warp_tot);
+  const bool has_work = w.g_begin < w.g_end;
+  if (!has_work || warp < NCW) {
+    griddep_wait();  // everything below may touch memory the previous grid wrote
+    write_zero_rows<T, D, BAL>(p, w, sm.prefix, blockIdx.y * HG * G, (blockIdx.y + 1) * HG * G, threadIdx.x,
+                               has_work ? NCW * 32 : blockDim.x);
+  }
+  if (!has_work) return;
   if (warp == NCW) {
+    // the fused append in this producer reads k_new: wait for the previous grid too
+    griddep_wait();
     produce<T, D, BAL, true>(p, w, sm, blockIdx.y * HG, lane);
     return;
   }
@@ -873,15 +891,25 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.num_heads / p.num_kv_heads;
   if (threadIdx.x == 0) {
+    griddep_launch_dependents();  // the next grid may start on SMs this one frees
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&sm.full_bar[s], 1);
       mbar_init(&sm.empty_bar[s], NCW);
     }
     fence_mbar_init();
   }
-  const Work w = setup_work<T, D, BAL>(p, sm, warp_tot, blockIdx.y * HG * G, (blockIdx.y + 1) * HG * G);
-  if (w.g_begin >= w.g_end) return;
+  const Work w = setup_work<T, D, BAL>(p, sm, warp_tot);
+  const bool has_work = w.g_begin < w.g_end;
+  if (!has_work || warp < NCW) {
+    griddep_wait();  // everything below may touch memory the previous grid wrote
+    write_zero_rows<T, D, BAL>(p, w, sm.prefix, blockIdx.y * HG * G, (blockIdx.y + 1) * HG * G, threadIdx.x,
+                               has_work ? NCW * 32 : blockDim.x);
+  }
+  if (!has_work) return;
   if (warp == NCW) {
+    // Streams pool pages without waiting for the previous grid: a caller that
+    // launches with programmatic overlap promises that grid writes neither the
+    // pool, the block table nor context_lens.
     produce<T, D, BAL, false>(p, w, sm, blockIdx.y * HG, lane);
     return;
   }
@@ -913,6 +941,8 @@ int decode_smem_bytes(int tile_bytes, int pbuf_bytes, int stages, int prefix_ent
 template <typename Kern>
 static cudaError_t launch_with_smem(Kern kern, int* granted, const DecodeParams& p, const LaunchShape& s,
                                    cudaStream_t stream) {
+  // s.overlap: programmatic dependent launch (the kernel may start while the
+  // previous kernel on the stream drains; see paged_decode_mma_kernel)
   // raise the dynamic shared-memory limit once per device (and when a call needs more)
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -922,7 +952,18 @@ static cudaError_t launch_with_smem(Kern kern, int* granted, const DecodeParams&
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) granted[dev] = s.smem_bytes;
   }
-  kern<<<s.grid, s.block, s.smem_bytes, stream>>>(p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = s.grid;
+  cfg.blockDim = s.block;
+  cfg.dynamicSmemBytes = s.smem_bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = s.overlap ? 1 : 0;
+  e = cudaLaunchKernelEx(&cfg, kern, p);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

@@ -71,6 +71,7 @@ struct LaunchShape {
   dim3 grid;
   dim3 block;
   int smem_bytes;
+  bool overlap;  // programmatic dependent launch on the previous kernel of the stream
 };
 
 // Shared-memory bytes the decode kernel needs (stage ring + softmax buffers +

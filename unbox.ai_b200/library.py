@@ -15,6 +15,7 @@ LIB_PATH = os.path.join(HERE, "lib", "libunbox_b200.so")
 
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 SCHEDULE_AUTO, SCHEDULE_BALANCED, SCHEDULE_SPLIT = 0, 1, 2
+FLAG_OVERLAP_PREVIOUS = 1
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_WORKSPACE, ERR_CUDA = 0, 1, 2, 3, 4
 DEVERR = {1: "page id outside the pool", 2: "context longer than its block-table row",
           4: "negative context length", 8: "pipeline wait timed out", 16: "append slot outside the pool"}
@@ -35,7 +36,7 @@ SIGNATURES = {
                                           _vp, _sz, _vp]),
     "ubx_paged_decode_append_attention": (_i32, [_vp, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64,
                                                  _vp, _i64, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i64,
-                                                 _i32, _f32, _i32, _i32, _i32, _vp, _sz, _vp]),
+                                                 _i32, _f32, _i32, _i32, _i32, _i32, _vp, _sz, _vp]),
     "ubx_read_device_error": (_i32, [_vp, ctypes.POINTER(ctypes.c_int32), _i32, _vp]),
     "ubx_paged_decode_attention_noalloc": (_i32, [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp,
                                                   _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i64, _i32, _f32, _i32,

@@ -133,12 +133,17 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
                     context_lens: torch.Tensor, scale: Optional[float] = None, *, out: Optional[torch.Tensor] = None,
                     schedule: str = "auto", split_pages: int = 0,
                     workspace: Optional[DecodeWorkspace] = None, k_new: Optional[torch.Tensor] = None,
-                    v_new: Optional[torch.Tensor] = None) -> torch.Tensor:
+                    v_new: Optional[torch.Tensor] = None, overlap_previous: bool = False) -> torch.Tensor:
     """Paged GQA decode attention: out[b, h] = softmax(scale * q[b, h] K^T) V over
     the first context_lens[b] positions of sequence b (see module docstring).
 
     With ``k_new``/``v_new`` ((B, KVH, D) rows of the token being decoded) the
     rows are first appended at position context_lens[b] - 1, in the same launch.
+    ``overlap_previous`` (fused form only) launches with programmatic dependent
+    launch: pool pages start streaming while the previous kernel on the stream
+    drains. Only pass it when that kernel writes neither the pool, the block
+    table nor context_lens (the previous layer's attention or this layer's QKV
+    projection in a decode step).
     """
     dev = _require_cuda(q, k_cache, v_cache, block_table, context_lens)
     if (k_new is None) != (v_new is None):
@@ -179,6 +184,8 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
             out.stride(1), B, H, KVH, D, bs, NB, max_blocks, float(scale), _DTYPES[q.dtype], _SCHEDULES[schedule],
             int(split_pages), buf.data_ptr(), buf.numel(), _stream(dev))
     if k_new is None:
+        if overlap_previous:
+            raise ValueError("overlap_previous applies to the fused append + attention call")
         st = lib.ubx_paged_decode_attention(
             q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(),
             k_cache.stride(0), k_cache.stride(1), k_cache.stride(2), *tail)
@@ -194,7 +201,8 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
         st = lib.ubx_paged_decode_append_attention(
             k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0), k_new.stride(1),
             q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(),
-            k_cache.stride(0), k_cache.stride(1), k_cache.stride(2), *tail)
+            k_cache.stride(0), k_cache.stride(1), k_cache.stride(2), *tail[:-3],
+            _L.FLAG_OVERLAP_PREVIOUS if overlap_previous else 0, *tail[-3:])
         _L.check(st, "paged_decode_append_attention")
     return out
 
@@ -202,11 +210,11 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
 def paged_decode_append_attention(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, k_cache: torch.Tensor,
                                   v_cache: torch.Tensor, block_table: torch.Tensor, context_lens: torch.Tensor,
                                   scale: Optional[float] = None, *, out: Optional[torch.Tensor] = None,
-                                  schedule: str = "auto") -> torch.Tensor:
+                                  schedule: str = "auto", overlap_previous: bool = False) -> torch.Tensor:
     """One decode layer's KV append and attention in one launch: the engine's
     append loop (engine.py:213-215) and attention call (:221-224)."""
     return paged_attention(q, k_cache, v_cache, block_table, context_lens, scale, out=out, schedule=schedule,
-                           k_new=k_new, v_new=v_new)
+                           k_new=k_new, v_new=v_new, overlap_previous=overlap_previous)
 
 
 def paged_attention_split(q, k_cache, v_cache, block_table, context_lens, scale=None, split_pages: int = 32,
