@@ -1,10 +1,12 @@
 """Benchmark: paged GQA decode attention + KV append, 760M decode shape.
 
-One step = one decode step of the 760M model: for each of 24 layers, a KV
-append of the new token followed by paged attention over that layer's own
-cache (24 independent per-layer caches, ~7 GB, so L2 never holds a layer's K/V
-between uses). Workload: batch 64, context ~ U[512, 2048], GQA 16/8, head_dim
-112, page 16, bf16, values N(0,1)*0.5, randomly permuted pages.
+One step = one decode step of the 760M model: for each of 24 layers, the new
+token's K/V append and paged attention over that layer's own cache, fused in
+one launch (24 independent per-layer caches, ~7 GB, so L2 never holds a
+layer's K/V between uses). Default workload (decode_760m): batch 64, context
+~ U[512, 2048], GQA 16/8, head_dim 112, page 16, bf16, values N(0,1)*0.5,
+randomly permuted pages. The step is replayed as one CUDA graph, and
+consecutive layer-calls overlap through programmatic dependent launch.
 
 ``value`` is HBM GB/s of algorithmic bytes (K/V rows once per (sequence, KV
 head), q, out, block-table rows, context lengths, append rows) with all inputs
@@ -15,9 +17,11 @@ from pinned host memory and the outputs copied back inside the timed region.
 ``--impl reference`` times the CPU oracle (the reference algorithm restated in
 C, OpenMP over all host cores) on one layer-call of the same workload per step.
 
-Multi-GPU (torchrun): every rank runs its own batch of 64 sequences (requests
-partitioned across GPUs, no collective on the data path); value = all ranks'
-bytes / the slowest rank's time.
+Multi-GPU (torchrun): decode_760m runs one batch of 64 per GPU (weak scaling:
+requests partitioned across GPUs, no collective on the data path);
+``--workload box_scale`` splits one batch of 1024 requests over the GPUs
+(strong scaling, LPT placement, KV-head split of contexts over 2048 tokens).
+value = all ranks' bytes / the slowest rank's time.
 """
 from __future__ import annotations
 
@@ -28,8 +32,6 @@ import statistics
 import sys
 import threading
 import time
-
-import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
@@ -43,7 +45,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="decode_760m")
+    ap.add_argument("--workload", default="decode_760m",
+                    choices=["decode_760m", "correctness", "long_context", "radix_prefix", "box_scale"])
     ap.add_argument("--layers", type=int, default=24)
     ap.add_argument("--schedule", default="auto", choices=["auto", "balanced", "split"])
     ap.add_argument("--split-pages", type=int, default=0)
@@ -68,7 +71,7 @@ def peaks():
 
 
 def profiled_traffic(workload: str):
-    """DRAM bytes per attention launch from the committed ncu summary (or None)."""
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary (or None)."""
     path = os.path.join(ROOT, "profiles", f"paged_decode_{workload}.md")
     try:
         for line in open(path):
@@ -129,21 +132,23 @@ class ClockSampler:
                 "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
-def cpu_oracle_run(lay, host, seconds: float, nthreads: int = 0):
-    """Time the C oracle (append + attention, one layer) for about `seconds`."""
-    from oracle import oracle
-    oracle.build()
-    kc, vc = host["k_cache"], host["v_cache"]
-    calls, t0 = 0, time.perf_counter()
-    while True:
-        oracle.kv_append(host["k_new"], host["v_new"], kc, vc, host["slot_mapping"])
-        _, st = oracle.paged_decode_attention(host["q"], kc, vc, host["block_table"], host["context_lens"],
-                                              nthreads=nthreads)
-        calls += 1
-        el = time.perf_counter() - t0
-        if el >= seconds or calls >= 1000:
-            break
-    return calls, el, oracle.num_threads() if nthreads <= 0 else nthreads
+def build_parts(pkg, workload: str, rank: int, world: int):
+    """The (name, Layout) parts this rank attends over each layer, the scaling
+    mode, and the whole workload's layout."""
+    wl, sh = pkg.workloads, pkg.sharding
+    if workload == "box_scale":
+        glay = wl.named_layout("box_scale", seed=0)
+        shard = sh.plan_shards(glay.context_lens, world)[rank]
+        parts = []
+        if len(shard.whole):
+            parts.append(("whole", sh.local_layout(glay.context_lens, shard.whole, 1000 + rank, 16, 8)))
+        if shard.kv_head_count:
+            G = glay.num_heads // glay.num_kv_heads
+            parts.append(("kv_head_slice", sh.local_layout(glay.context_lens, shard.head_split, 2000 + rank,
+                                                           G * shard.kv_head_count, shard.kv_head_count)))
+        return parts, "strong", glay
+    lay = wl.named_layout(workload, seed=1000 + rank)
+    return [("batch", lay)], "weak", lay
 
 
 def host_layer(dev, layer):
@@ -151,6 +156,14 @@ def host_layer(dev, layer):
             "v_cache": dev["v_caches"][layer].cpu(), "k_new": dev["k_new"][layer].cpu(),
             "v_new": dev["v_new"][layer].cpu(), "block_table": dev["block_table"].cpu(),
             "context_lens": dev["context_lens"].cpu(), "slot_mapping": dev["slot_mapping"].cpu()}
+
+
+def cpu_layer_call(oracle, host):
+    """The oracle's KV append then attention: one layer-call of the reference algorithm."""
+    oracle.kv_append(host["k_new"], host["v_new"], host["k_cache"], host["v_cache"], host["slot_mapping"])
+    _, st = oracle.paged_decode_attention(host["q"], host["k_cache"], host["v_cache"], host["block_table"],
+                                          host["context_lens"])
+    return st
 
 
 def main():
@@ -166,25 +179,28 @@ def main():
     pkg = load_package()
     wl = pkg.workloads
     spec = wl.NAMED[args.workload]
-    lay = wl.named_layout(args.workload, seed=1000 + rank)
     ebytes = {"float32": 4, "bfloat16": 2, "float16": 2}[spec["dtype"]]
-    ab = wl.algorithmic_bytes(lay, ebytes)
     dtype_tag = {"float32": "f32", "bfloat16": "bf16", "float16": "f16"}[spec["dtype"]]
-    config = {"workload": args.workload, "batch_per_gpu": lay.batch, "ctx_mean": float(lay.context_lens.mean()),
-              "heads": [lay.num_heads, lay.num_kv_heads, lay.head_dim], "page": lay.block_size,
-              "layers": args.layers, "kv_bytes_per_layer": int(2 * lay.num_blocks * lay.block_size *
-                                                                lay.num_kv_heads * lay.head_dim * ebytes),
-              "l2": "inputs > L2: 24 rotating per-layer caches",
-              "parallelism": f"requests sharded, {world} GPU(s), no collective"}
+    parts, scaling, glay = build_parts(pkg, args.workload, rank, world)
+    abs_ = [wl.algorithmic_bytes(lay, ebytes) for _, lay in parts]
+    config = {"workload": args.workload, "batch": glay.batch if scaling == "strong" else glay.batch * world,
+              "batch_per_gpu": sum(l.batch for _, l in parts), "ctx_mean": float(glay.context_lens.mean()),
+              "heads": [glay.num_heads, glay.num_kv_heads, glay.head_dim], "page": glay.block_size,
+              "layers": args.layers, "kv_bytes_per_layer_per_gpu": int(sum(
+                  2 * l.num_blocks * l.block_size * l.num_kv_heads * l.head_dim * ebytes for _, l in parts)),
+              "l2": f"inputs > L2: {args.layers} rotating per-layer caches",
+              "parallelism": f"{world} GPU(s), requests" + (" and long-context KV heads" if scaling == "strong"
+                                                            else "") + " partitioned, no collective"}
 
     if args.impl == "reference":
         if rank != 0:
             return
-        dev = wl.materialize_device(lay, 7, spec["dtype"], spec["scale_values"], 1, device="cpu") \
-            if not torch.cuda.is_available() else None
-        if dev is None:
+        name, lay = parts[0]
+        on_gpu = torch.cuda.is_available()
+        if on_gpu:
             torch.cuda.set_device(local)
-            dev = wl.materialize_device(lay, 7, spec["dtype"], spec["scale_values"], 1)
+        dev = wl.materialize_device(lay, 7, spec["dtype"], spec["scale_values"], 1,
+                                    device="cuda" if on_gpu else "cpu")
         host = host_layer(dev, 0)
         del dev
         from oracle import oracle
@@ -192,19 +208,18 @@ def main():
         times = []
         for i in range(args.warmup + args.steps):
             t0 = time.perf_counter()
-            oracle.kv_append(host["k_new"], host["v_new"], host["k_cache"], host["v_cache"], host["slot_mapping"])
-            oracle.paged_decode_attention(host["q"], host["k_cache"], host["v_cache"], host["block_table"],
-                                          host["context_lens"])
+            cpu_layer_call(oracle, host)
             if i >= args.warmup:
                 times.append(time.perf_counter() - t0)
         tot = sum(times)
-        gbs = ab["layer_call"] * len(times) / tot / 1e9
+        gbs = abs_[0]["layer_call"] * len(times) / tot / 1e9
         cores = oracle.num_threads()
-        sample = f"one layer-call (append + attention) of the {lay.batch}-sequence batch per step, host cores"
+        sample = (f"one layer-call (append + attention) of the {lay.batch}-sequence '{name}' part per step, "
+                  f"C oracle, OpenMP on {cores} host threads")
         print(json.dumps({
             "metric": METRIC, "value": round(gbs, 4), "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * tot / len(times),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype_tag,
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": dtype_tag,
             "data": "synthetic", "config": config, "layer_calls_per_s": len(times) / tot,
             "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": "port",
                              "sample": sample},
@@ -219,47 +234,49 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
 
     L = args.layers
-    dev = wl.materialize_device(lay, 7 + rank, spec["dtype"], spec["scale_values"], L)
-    outs = [torch.empty_like(dev["q"][l]) for l in range(L)]
-    bt, cl, sm = dev["block_table"], dev["context_lens"], dev["slot_mapping"]
+    devs = [wl.materialize_device(lay, 7 + 31 * rank + i, spec["dtype"], spec["scale_values"], L)
+            for i, (_, lay) in enumerate(parts)]
+    outs = [[torch.empty_like(d["q"][l]) for l in range(L)] for d in devs]
     kw = dict(schedule=args.schedule, split_pages=args.split_pages)
-    launches_per_layer = (2 if args.separate else 1) + (1 if args.schedule == "split" else 0)
+    launches_per_call = (2 if args.separate else 1) + (1 if args.schedule == "split" else 0)
+    calls_per_step = L * len(parts)
 
-    def layer(l, q, k_new, v_new, block_table, context_lens, out, slots=None, timer=None):
+    def layer_call(d, l, q, k_new, v_new, block_table, context_lens, out, slots=None, timer=None):
         """One layer-call: the new token's K/V append, then attention (engine.py:213-224)."""
         if args.separate:
-            pkg.kv_append(k_new, v_new, dev["k_caches"][l], dev["v_caches"][l], slots)
+            pkg.kv_append(k_new, v_new, d["k_caches"][l], d["v_caches"][l], slots)
         if timer is not None:
             timer[0].record()
         if args.separate:
-            pkg.paged_attention(q, dev["k_caches"][l], dev["v_caches"][l], block_table, context_lens, out=out, **kw)
+            pkg.paged_attention(q, d["k_caches"][l], d["v_caches"][l], block_table, context_lens, out=out, **kw)
         else:
-            # the previous kernel on the stream is another layer's attention (or a copy):
-            # it writes neither this layer's pool nor the block table / context lengths
-            pkg.paged_attention(q, dev["k_caches"][l], dev["v_caches"][l], block_table, context_lens, out=out,
+            # the previous kernel on the stream is another layer-call's attention (or a
+            # copy): it writes neither this pool nor the block table / context lengths
+            pkg.paged_attention(q, d["k_caches"][l], d["v_caches"][l], block_table, context_lens, out=out,
                                 k_new=k_new, v_new=v_new, overlap_previous=args.overlap, **kw)
         if timer is not None:
             timer[1].record()
 
     def step(timers=None):
         for l in range(L):
-            layer(l, dev["q"][l], dev["k_new"][l], dev["v_new"][l], bt, cl, outs[l], sm,
-                  None if timers is None else timers[l])
+            for i, d in enumerate(devs):
+                layer_call(d, l, d["q"][l], d["k_new"][l], d["v_new"][l], d["block_table"], d["context_lens"],
+                           outs[i][l], d["slot_mapping"], None if timers is None else timers[l * len(devs) + i])
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
 
-    def max_over_ranks(x: float) -> float:
+    def reduce(x: float, op) -> float:
         if world == 1:
             return x
         t = torch.tensor([x], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=op)
         return float(t.item())
 
     def capture(fn):
-        """CUDA graph of fn (warmed up on a side stream first, as graph capture needs)."""
+        """CUDA graph of fn (run once on a side stream first, as graph capture needs)."""
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
@@ -282,8 +299,8 @@ def main():
 
     # ---- device-resident timing (value)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    timers = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
-              for _ in range(args.steps)]
+    timers = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(calls_per_step)] for _ in range(args.steps)]
     barrier()
     with ClockSampler(local) as clocks:
         ev0.record()
@@ -296,19 +313,23 @@ def main():
         torch.cuda.synchronize()
     barrier()
     ms = ev0.elapsed_time(ev1)
-    ms_max = max_over_ranks(ms)
+    ms_max = reduce(ms, dist.ReduceOp.MAX)
     pkg.check_device_errors(device)
 
     # ---- dominant kernel: average launch time on its own stream
+    bytes_attn = sum(a["attention"] for a in abs_)
+    bytes_call = sum(a["layer_call"] for a in abs_)
     if graph is None:
-        attn_ms = [a.elapsed_time(b) for row in timers for (a, b) in row]
-        kernel_avg_ms = sum(attn_ms) / len(attn_ms)
+        t_ms = [a.elapsed_time(b) for row in timers for (a, b) in row]
+        kernel_avg_ms = sum(t_ms) / len(t_ms)
     elif not args.separate and args.schedule != "split":
-        kernel_avg_ms = ms / (args.steps * L)   # the step is exactly L launches of the fused kernel
+        kernel_avg_ms = ms / (args.steps * calls_per_step)  # the step is exactly these launches
     else:
         def attn_only():
             for l in range(L):
-                pkg.paged_attention(dev["q"][l], dev["k_caches"][l], dev["v_caches"][l], bt, cl, out=outs[l], **kw)
+                for i, d in enumerate(devs):
+                    pkg.paged_attention(d["q"][l], d["k_caches"][l], d["v_caches"][l], d["block_table"],
+                                        d["context_lens"], out=outs[i][l], **kw)
         ga = capture(attn_only)
         a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
@@ -317,35 +338,36 @@ def main():
             ga.replay()
         a1.record()
         torch.cuda.synchronize()
-        kernel_avg_ms = a0.elapsed_time(a1) / (args.steps * L)
+        kernel_avg_ms = a0.elapsed_time(a1) / (args.steps * calls_per_step)
         del ga
-    kernel_bytes = ab["attention"] if args.separate else ab["layer_call"]
+    kernel_bytes = (bytes_attn if args.separate else bytes_call) / len(parts)
 
     # ---- end to end through the public API with host buffers
-    qh = torch.stack([x.cpu() for x in dev["q"]]).pin_memory()
-    knh = torch.stack([x.cpu() for x in dev["k_new"]]).pin_memory()
-    vnh = torch.stack([x.cpu() for x in dev["v_new"]]).pin_memory()
-    bth, clh = bt.cpu().pin_memory(), cl.cpu().pin_memory()
-    outh = torch.empty((L,) + tuple(outs[0].shape), dtype=outs[0].dtype).pin_memory()
-    qd, knd, vnd = torch.empty_like(qh, device=device), torch.empty_like(knh, device=device), \
-        torch.empty_like(vnh, device=device)
-    btd, cld = torch.empty_like(bth, device=device), torch.empty_like(clh, device=device)
-    posd = torch.empty_like(clh, device=device)
-    smd = torch.empty(lay.batch, dtype=torch.int64, device=device)
-    outd = torch.empty_like(outh, device=device)
+    hosts = []
+    for d in devs:
+        h = dict(q=torch.stack([x.cpu() for x in d["q"]]).pin_memory(),
+                 k_new=torch.stack([x.cpu() for x in d["k_new"]]).pin_memory(),
+                 v_new=torch.stack([x.cpu() for x in d["v_new"]]).pin_memory(),
+                 bt=d["block_table"].cpu().pin_memory(), cl=d["context_lens"].cpu().pin_memory())
+        h["out"] = torch.empty((L,) + tuple(d["q"][0].shape), dtype=d["q"][0].dtype).pin_memory()
+        dd = {k: torch.empty_like(v, device=device) for k, v in h.items()}
+        dd["pos"] = torch.empty_like(h["cl"], device=device)
+        dd["slots"] = torch.empty(h["cl"].shape[0], dtype=torch.int64, device=device)
+        hosts.append((h, dd))
 
     def e2e_step():
-        btd.copy_(bth, non_blocking=True)
-        cld.copy_(clh, non_blocking=True)
-        qd.copy_(qh, non_blocking=True)
-        knd.copy_(knh, non_blocking=True)
-        vnd.copy_(vnh, non_blocking=True)
-        if args.separate:
-            torch.sub(cld, 1, out=posd)
-            pkg.slot_mapping(btd, posd, lay.block_size, out=smd)
+        for h, dd in hosts:
+            for k in ("bt", "cl", "q", "k_new", "v_new"):
+                dd[k].copy_(h[k], non_blocking=True)
+            if args.separate:
+                torch.sub(dd["cl"], 1, out=dd["pos"])
+                pkg.slot_mapping(dd["bt"], dd["pos"], glay.block_size, out=dd["slots"])
         for l in range(L):
-            layer(l, qd[l], knd[l], vnd[l], btd, cld, outd[l], smd)
-        outh.copy_(outd, non_blocking=True)
+            for (h, dd), d in zip(hosts, devs):
+                layer_call(d, l, dd["q"][l], dd["k_new"][l], dd["v_new"][l], dd["bt"], dd["cl"], dd["out"][l],
+                           dd["slots"])
+        for h, dd in hosts:
+            h["out"].copy_(dd["out"], non_blocking=True)
 
     for _ in range(3):
         e2e_step()
@@ -362,44 +384,56 @@ def main():
     e1.record()
     torch.cuda.synchronize()
     barrier()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
-    h2d = sum(t.numel() * t.element_size() for t in (bth, clh, qh, knh, vnh))
-    d2h = outh.numel() * outh.element_size()
-    assert torch.equal(outh[0].to(device), outs[0]), "end-to-end output differs from the device-resident step"
+    e2e_ms = reduce(e0.elapsed_time(e1), dist.ReduceOp.MAX)
+    h2d = sum(h[k].numel() * h[k].element_size() for h, _ in hosts for k in ("bt", "cl", "q", "k_new", "v_new"))
+    d2h = sum(h["out"].numel() * h["out"].element_size() for h, _ in hosts)
+    for (h, _), o in zip(hosts, outs):
+        assert torch.equal(h["out"][0].to(device), o[0]), "end-to-end output differs from the device-resident step"
     del eg
 
-    total_bytes_step = ab["layer_call"] * L * world
-    value = total_bytes_step * args.steps / (ms_max / 1e3) / 1e9
-    e2e_val = total_bytes_step * args.steps / (e2e_ms / 1e3) / 1e9
+    step_bytes_all = reduce(float(bytes_call * L), dist.ReduceOp.SUM)
+    h2d_all, d2h_all = reduce(float(h2d), dist.ReduceOp.SUM), reduce(float(d2h), dist.ReduceOp.SUM)
+    calls_all = reduce(float(calls_per_step), dist.ReduceOp.SUM)
+    value = step_bytes_all * args.steps / (ms_max / 1e3) / 1e9
+    e2e_val = step_bytes_all * args.steps / (e2e_ms / 1e3) / 1e9
     peak, peak_kind = peaks()
 
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": dtype_tag, "data": "synthetic", "config": config,
-        "layer_calls_per_s": round(L * world * args.steps / (ms_max / 1e3), 1),
+        "scaling": scaling, "vs_baseline": None, "dtype": dtype_tag, "data": "synthetic", "config": config,
+        "layer_calls_per_s": round(calls_all * args.steps / (ms_max / 1e3), 1),
         "frac_of_hbm_peak": round(value / world / peak, 4),
-        "gpu_launches": args.steps * L * launches_per_layer,
-        "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
-                "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms / args.steps, 4)},
+        "gpu_launches": args.steps * calls_per_step * launches_per_call,
+        "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d_all),
+                "d2h_bytes_per_step": int(d2h_all), "ms_per_step": round(e2e_ms / args.steps, 4)},
         "clocks": clocks.summary(),
         "graph": bool(graph is not None), "append": "separate launch" if args.separate else "fused",
         "overlap_previous": bool(args.overlap and not args.separate),
     }
     achieved = kernel_bytes / (kernel_avg_ms / 1e3) / 1e9
-    traffic = profiled_traffic(args.workload)
     line["roofline"] = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                        "frac": round(achieved / peak, 4), "traffic": traffic,
+                        "frac": round(achieved / peak, 4), "traffic": profiled_traffic(args.workload),
                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                         else "fallback 6650 GB/s",
                         "kernel": "paged_decode_mma_kernel" + ("" if args.separate else " (KV append fused)"),
-                        "algorithmic_bytes_per_launch": kernel_bytes, "avg_launch_us": round(kernel_avg_ms * 1e3, 2),
+                        "algorithmic_bytes_per_launch": int(kernel_bytes),
+                        "avg_launch_us": round(kernel_avg_ms * 1e3, 2),
                         "timing": "per-launch CUDA events" if graph is None else "graph replay / launches"}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        host = host_layer(dev, 0)
-        calls, el, thr = cpu_oracle_run(lay, host, args.cpu_seconds)
-        cpu_gbs = ab["layer_call"] * calls / el / 1e9
-        line["cpu_baseline"] = {"value": round(cpu_gbs, 4), "unit": "GB/s", "cores": thr, "kind": "port",
+        from oracle import oracle
+        oracle.build()
+        host = host_layer(devs[0], 0)
+        calls, t0 = 0, time.perf_counter()
+        while True:
+            cpu_layer_call(oracle, host)
+            calls += 1
+            el = time.perf_counter() - t0
+            if el >= args.cpu_seconds or calls >= 1000:
+                break
+        cpu_gbs = abs_[0]["layer_call"] * calls / el / 1e9
+        line["cpu_baseline"] = {"value": round(cpu_gbs, 4), "unit": "GB/s", "cores": oracle.num_threads(),
+                                "kind": "port",
                                 "sample": f"{calls} layer-call(s) (append + attention) of layer 0 of this "
                                           f"workload, C oracle with OpenMP, {el:.1f} s"}
     if rank == 0:

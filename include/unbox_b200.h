@@ -99,7 +99,7 @@ int ubx_slot_mapping(const int32_t* block_table, int64_t bt_s_row, const int32_t
 /*
  * Bytes of device workspace the attention entry points need for these sizes on
  * the current device (partial results of split sequences, merge counters, the
- * error word). The workspace must be zeroed once with ubx_workspace_init before
+ * error word; sized for up to 4 CTAs per SM). The workspace must be zeroed once with ubx_workspace_init before
  * its first use; the kernels leave it ready for the next call.
  */
 int ubx_paged_decode_workspace_size(int batch, int num_heads, int head_dim, int max_blocks_per_seq,

@@ -74,7 +74,7 @@ int num_sms_current_device(int* n) {
 }
 
 struct Plan {
-  int gw, wpk, hg, n_hg, stages, smem, row, pitch, tile, pbuf;
+  int gw, wpk, hg, n_hg, stages, smem, row, pitch, tile, pbuf, ctas_per_sm;
   bool balanced;
   int split_pages, max_chunks;
   dim3 grid, block;
@@ -109,12 +109,21 @@ int make_plan(int batch, int num_heads, int num_kv_heads, int head_dim, int dtyp
   pl->pbuf = mma ? 0 : ((pl->hg * pl->wpk * pl->gw * kBlockSize * 4 + 15) & ~15);
   const int prefix = pl->balanced ? batch + 1 : 0;
   const int fixed = decode_smem_bytes(pl->tile, pl->pbuf, 0, prefix);
-  pl->stages = std::min(6, (kSmemLimit - fixed) / (2 * pl->tile));
+  // Small head groups leave a CTA with few consumer warps: put several CTAs on
+  // an SM (aiming at 8 consumer warps per SM) and share its shared memory.
+  const int ncw = pl->hg * pl->wpk;
+  int ctas = std::min(kMaxCtasPerSm, (kMaxConsumerWarps + ncw - 1) / ncw);
+  for (;; --ctas) {
+    const int budget = ctas == 1 ? kSmemLimit : kSmemPerSm / ctas - kSmemReservedPerCta;
+    pl->stages = std::min(6, (budget - fixed) / (2 * pl->tile));
+    if (pl->stages >= 2 || ctas == 1) break;
+  }
   if (pl->stages < 2) return fail(UBX_ERR_UNSUPPORTED, "shared memory too small for a 2-stage pipeline");
+  pl->ctas_per_sm = ctas;
   pl->smem = decode_smem_bytes(pl->tile, pl->pbuf, pl->stages, prefix);
   pl->block = dim3((pl->hg * pl->wpk + 1) * 32);
   if (pl->balanced) {
-    pl->grid = dim3(std::max(1, num_sms / pl->n_hg), pl->n_hg);
+    pl->grid = dim3(std::max(1, num_sms * ctas / pl->n_hg), pl->n_hg);
     pl->slots = 2 * (int64_t)pl->grid.x;
   } else {
     pl->grid = dim3((unsigned)((int64_t)batch * pl->max_chunks), pl->n_hg);
@@ -217,7 +226,7 @@ int ubx_paged_decode_workspace_size(int batch, int num_heads, int head_dim, int 
   if (st != UBX_OK) return st;
   const int sp = split_pages > 0 ? split_pages : kDefaultSplitPages;
   const int64_t chunks = (max_blocks_per_seq + sp - 1) / sp;
-  const int64_t slots = std::max<int64_t>(2 * (int64_t)sms, (int64_t)batch * chunks);
+  const int64_t slots = std::max<int64_t>(2 * (int64_t)sms * kMaxCtasPerSm, (int64_t)batch * chunks);
   *bytes = ws_layout(slots, num_heads, head_dim).total;
   return UBX_OK;
 }

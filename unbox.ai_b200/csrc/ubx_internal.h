@@ -13,6 +13,9 @@ constexpr int kMaxConsumerWarps = 8;    // consumer warps per CTA
 constexpr int kMaxBatchSmem = 2048;     // balanced schedule keeps a (B+1) page prefix in smem
 constexpr int kMaxTileBytes = 36864;    // one K (or V) page tile of a head group
 constexpr int kSmemLimit = 227 * 1024 - 512;  // dynamic smem budget: 227 KB opt-in minus static smem
+constexpr int kSmemPerSm = 228 * 1024;        // shared memory of one SM
+constexpr int kSmemReservedPerCta = 1024 + 512;  // per-CTA reservation + static smem
+constexpr int kMaxCtasPerSm = 4;              // CTAs of one balanced launch per SM (small head groups)
 
 // Workspace layout prefix: [error word + reserved | merge counters | partials].
 constexpr size_t kWsHeaderBytes = 256;                      // error word at offset 0
