@@ -35,6 +35,8 @@
 // No waits without bounds: every mbarrier wait gives up after ~2^31 clocks,
 // records UBX_DEVERR_TIMEOUT and unwinds; the producer then waits (bounded) for
 // its own loads in flight before the CTA exits.
+#include <type_traits>
+
 #include "ubx_common.cuh"
 #include "ubx_internal.h"
 
@@ -164,10 +166,9 @@ __device__ void merge_rows(const DecodeParams& p, int b, int head0, int nh, int 
     const int h = hb + lane / DCH, c = lane % DCH;
     if (lane >= HPW * DCH || h >= nh) continue;  // no warp collectives below
     const int head = head0 + h;
-    float M = -INFINITY;
-#pragma unroll 4
-    for (int i = 0; i < nparts; ++i) M = fmaxf(M, __ldcg(&p.part_ml[slot_of(i) * H + head]).x);
-    float L = 0.f, o[EPC];
+    // one pass with a running max: all of a part's loads are independent of the
+    // previous parts, so unrolled iterations keep several parts in flight
+    float M = -INFINITY, L = 0.f, o[EPC];
 #pragma unroll
     for (int e = 0; e < EPC; ++e) o[e] = 0.f;
 #pragma unroll 4
@@ -178,6 +179,13 @@ __device__ void merge_rows(const DecodeParams& p, int b, int head0, int nh, int 
       float4 v[EPC / 4];
 #pragma unroll
       for (int e4 = 0; e4 < EPC / 4; ++e4) v[e4] = __ldcg(src + e4);
+      if (ml.x > M) {
+        const float sc = exp2f(M - ml.x);  // M = -inf at first: sc = 0
+        L *= sc;
+#pragma unroll
+        for (int e = 0; e < EPC; ++e) o[e] *= sc;
+        M = ml.x;
+      }
       const float wgt = exp2f(ml.x - M);
       L = fmaf(ml.y, wgt, L);
 #pragma unroll
@@ -314,29 +322,29 @@ __device__ __forceinline__ void ldsm_x4_trans(const void* p, uint32_t& r0, uint3
                : "r"(smem_u32(p)));
 }
 
-// D(16x8, f32) += A(16x16) * B(16x8), A row-major, B column-major, 16-bit inputs.
+// D(16x8, f32) += A(16x16) * B(16x8) (A row-major, B column-major, 16-bit
+// inputs) for an A whose rows 8..15 are zero (the padding rows of a q-head
+// tile): only D rows 0..7 are kept (d[0], d[1] of this lane); rows 8..15 come
+// back as zeros into registers that die at once, so they hold no accumulator.
 template <typename T>
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1);
-
-template <>
-__device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                                        uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%0, %1, %2, %3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-template <>
-__device__ __forceinline__ void mma16816<__half>(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                                 uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%0, %1, %2, %3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+__device__ __forceinline__ void mma16816_top(float (&d)[2], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  float dead0, dead1;
+  const float zero = 0.f;
+  if constexpr (sizeof(T) == 2 && std::is_same<T, __nv_bfloat16>::value) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %10, %10};"
+        : "+f"(d[0]), "+f"(d[1]), "=f"(dead0), "=f"(dead1)
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1), "f"(zero));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %10, %10};"
+        : "+f"(d[0]), "+f"(d[1]), "=f"(dead0), "=f"(dead1)
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1), "f"(zero));
+  }
+  (void)dead0;
+  (void)dead1;
 }
 
 // ---------------------------------------------------------------- shared CTA plumbing
@@ -357,6 +365,7 @@ struct Smem {
   int32_t* prefix;
 };
 
+// Layout: [stages][p_buf][full x kMaxStages][empty x kMaxStages][prefix]
 __device__ __forceinline__ Smem carve_smem(uint8_t* smem, const DecodeParams& p) {
   Smem s;
   const int stage_bytes = 2 * p.tile_bytes;
@@ -457,6 +466,14 @@ __device__ void append_rows(const DecodeParams& p, int b, int page, int head0, i
   }
   fence_proxy_async_global();
   __syncwarp();
+}
+
+// True when the segment ends its sequence and the fused append has a token to
+// place (a clamped context has none: pages_of reported it).
+__device__ __forceinline__ bool segment_appends(const DecodeParams& p, const Seg& s) {
+  if (p.k_new == nullptr || s.lp1 != s.s1 - s.s0) return false;
+  const int ctx = __ldg(&p.context_lens[s.b]);
+  return ctx >= 1 && (ctx - 1) / kBlockSize < p.max_blocks;
 }
 
 // Producer warp: reads the block table 32 entries at a time; for every page
@@ -697,14 +714,31 @@ __device__ void consume_mma(const DecodeParams& p, const Work& w, const Smem& sm
   const int k_row = (((lane >> 4) & 1) * 8 + (lane & 7)) * rs + ((lane >> 3) & 1) * 8;
   const int v_row = (((lane >> 3) & 1) * 8 + (lane & 7)) * rs + ((lane >> 4) & 1) * 8;
 
+  // Fused KV append (this warp's KV head): the token at position ctx - 1 is
+  // stored to the pool and patched into the shared-memory tile of the last page
+  // when that page arrives (so no cross-proxy ordering with its copy).
+  constexpr int RC = D / 8;  // 16-byte chunks of one head row
+  const int a_which = lane / RC, a_chunk = lane % RC;
+  auto store_appended = [&](const Seg& s, int a_slot, const uint4& a_row) {
+    const int page = __ldg(p.block_table + (int64_t)s.b * p.bt_sb + (s.s1 - s.s0) - 1);
+    if (page >= 0 && (int64_t)page < p.num_blocks)
+      *(reinterpret_cast<uint4*>(const_cast<T*>(reinterpret_cast<const T*>(a_which ? p.v_cache : p.k_cache)) +
+                                 (int64_t)page * p.c_sblk + (int64_t)a_slot * p.c_stok + (int64_t)kvh * p.c_sh) +
+        a_chunk) = a_row;
+  };
+
   uint32_t it = 0;
   bool first_seg = true;
   int b = w.b_first, g = w.g_begin;
   Seg s;
   while (next_seg<BAL>(w, sm.prefix, b, g, s)) {
     const int n_b = s.s1 - s.s0;
-    const int ctx = min(max(__ldg(&p.context_lens[s.b]), 0), n_b * kBlockSize);
+    const int ctx_raw = __ldg(&p.context_lens[s.b]);
+    const int ctx = min(max(ctx_raw, 0), n_b * kBlockSize);
+    const bool append = segment_appends(p, s);
+    const int a_slot = (ctx_raw - 1) & (kBlockSize - 1);
     uint32_t qa[KS][2];
+    uint4 a_row = make_uint4(0, 0, 0, 0);
     {
       const T* qrow = reinterpret_cast<const T*>(p.q) + (int64_t)s.b * p.q_sb + (int64_t)(head0 + qr) * p.q_sh;
 #pragma unroll
@@ -712,29 +746,16 @@ __device__ void consume_mma(const DecodeParams& p, const Work& w, const Smem& sm
         qa[ks][0] = real_row ? __ldg(reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 2 * qc)) : 0u;
         qa[ks][1] = real_row ? __ldg(reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 8 + 2 * qc)) : 0u;
       }
-    }
-    // Fused KV append (this warp's KV head): the token at position ctx - 1 is
-    // stored to the pool now and patched into the shared-memory tile of the last
-    // page when that page arrives (so no cross-proxy ordering with its copy).
-    constexpr int RC = D / 8;  // 16-byte chunks of one head row
-    const int ctx_raw = __ldg(&p.context_lens[s.b]);
-    const bool append = p.k_new != nullptr && s.lp1 == n_b && ctx_raw >= 1 && (ctx_raw - 1) / kBlockSize < p.max_blocks;
-    const int a_slot = (ctx_raw - 1) & (kBlockSize - 1);
-    const int a_which = lane / RC, a_chunk = lane % RC;
-    uint4 a_row = make_uint4(0, 0, 0, 0);
-    if (append && lane < 2 * RC) {
-      a_row = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a_which ? p.v_new : p.k_new) +
-                                                   (int64_t)s.b * p.n_stok + (int64_t)kvh * p.n_sh) + a_chunk);
-      const int page = __ldg(p.block_table + (int64_t)s.b * p.bt_sb + n_b - 1);
-      if (page >= 0 && (int64_t)page < p.num_blocks)
-        *(reinterpret_cast<uint4*>(const_cast<T*>(reinterpret_cast<const T*>(a_which ? p.v_cache : p.k_cache)) +
-                                   (int64_t)page * p.c_sblk + (int64_t)a_slot * p.c_stok + (int64_t)kvh * p.c_sh) +
-          a_chunk) = a_row;
+      if (append && lane < 2 * RC) {
+        a_row = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a_which ? p.v_new : p.k_new) +
+                                                     (int64_t)s.b * p.n_stok + (int64_t)kvh * p.n_sh) + a_chunk);
+        store_appended(s, a_slot, a_row);
+      }
     }
     float m = -INFINITY, l = 0.f;
-    float o[NT][4];
+    float o[NT][2];  // rows 0..7 of the O tile (q heads); rows 8..15 are padding
 #pragma unroll
-    for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = 0.f;
 
     bool ok = true;
     for (int lp = s.lp0; lp < s.lp1; ++lp, ++it) {
@@ -760,13 +781,13 @@ __device__ void consume_mma(const DecodeParams& p, const Work& w, const Smem& sm
       }
 
       // ---- scores
-      float sa[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      float sa[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks) {
         uint32_t r0, r1, r2, r3;
         ldsm_x4(kt + k_row + 16 * ks, r0, r1, r2, r3);
-        mma16816<T>(sa[0], qa[ks][0], 0u, qa[ks][1], 0u, r0, r1);
-        mma16816<T>(sa[1], qa[ks][0], 0u, qa[ks][1], 0u, r2, r3);
+        mma16816_top<T>(sa[0], qa[ks][0], qa[ks][1], r0, r1);
+        mma16816_top<T>(sa[1], qa[ks][0], qa[ks][1], r2, r3);
       }
       // this lane's scores of row qr: tokens 2qc, 2qc+1, 8+2qc, 9+2qc
       float sv[4] = {sa[0][0], sa[0][1], sa[1][0], sa[1][1]};
@@ -804,8 +825,8 @@ __device__ void consume_mma(const DecodeParams& p, const Work& w, const Smem& sm
       for (int np = 0; np < NT / 2; ++np) {
         uint32_t r0, r1, r2, r3;
         ldsm_x4_trans(vt + v_row + 16 * np, r0, r1, r2, r3);
-        mma16816<T>(o[2 * np], pa0, 0u, pa2, 0u, r0, r1);
-        mma16816<T>(o[2 * np + 1], pa0, 0u, pa2, 0u, r2, r3);
+        mma16816_top<T>(o[2 * np], pa0, pa2, r0, r1);
+        mma16816_top<T>(o[2 * np + 1], pa0, pa2, r2, r3);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.empty_bar[st]);
