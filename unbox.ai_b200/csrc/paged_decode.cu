@@ -357,6 +357,27 @@ struct Seg {
   int b, s0, s1, lp0, lp1;
 };
 
+// Position in the stage ring: the stage index and the phase parity its
+// barriers are in (kept incrementally: no integer division per page).
+struct RingPos {
+  int st;
+  uint32_t ph;
+  __device__ __forceinline__ void next(int stages) {
+    if (++st == stages) {
+      st = 0;
+      ph ^= 1u;
+    }
+  }
+  __device__ __forceinline__ void prev(int stages) {
+    if (st == 0) {
+      st = stages - 1;
+      ph ^= 1u;
+    } else {
+      --st;
+    }
+  }
+};
+
 struct Smem {
   uint8_t* stages;
   float* p_buf;
@@ -490,6 +511,7 @@ __device__ void produce(const DecodeParams& p, const Work& w, const Smem& sm, in
   const int t = lane & 15;
   const int dst_off = (lane >> 4) * tile + t * p.smem_row_bytes;
   uint32_t it = 0;
+  RingPos pos{0, 0};
   bool ok = true;
   int b = w.b_first, g = w.g_begin;
   Seg s;
@@ -499,15 +521,15 @@ __device__ void produce(const DecodeParams& p, const Work& w, const Smem& sm, in
       const int cnt = min(32, s.lp1 - lp);
       const int my_page = lane < cnt ? __ldg(row + lp + lane) : 0;
       if (lane < cnt && (my_page < 0 || (int64_t)my_page >= p.num_blocks)) set_error(p.error, kErrBadPage);
-      for (int i = 0; i < cnt; ++i, ++it) {
+      for (int i = 0; i < cnt; ++i, ++it, pos.next(STAGES)) {
         const int page = __shfl_sync(kFull, my_page, i);
         if (APPEND_HERE && p.k_new != nullptr && lp + i == s.s1 - s.s0 - 1)
           append_rows<T, D>(p, s.b, page, head0, p.heads_per_cta, lane);
         const bool in_pool = page >= 0 && (int64_t)page < p.num_blocks;
-        const int st = it % STAGES;
+        const int st = pos.st;
         int good = 1;
         if (lane == 0) {
-          if (!mbar_wait_bounded(&sm.empty_bar[st], ((it / STAGES) & 1) ^ 1))
+          if (!mbar_wait_bounded(&sm.empty_bar[st], pos.ph ^ 1u))
             good = 0;
           else if (in_pool)
             mbar_arrive_expect_tx(&sm.full_bar[st], 2 * kBlockSize * p.row_bytes);
@@ -535,9 +557,10 @@ __device__ void produce(const DecodeParams& p, const Work& w, const Smem& sm, in
   // the CTA must not retire with bulk copies still writing its shared memory
   if (lane == 0) {
     const uint32_t n = it < (uint32_t)STAGES ? it : (uint32_t)STAGES;
+    RingPos back = pos;
     for (uint32_t k = 1; k <= n; ++k) {
-      const uint32_t i = it - k;
-      if (!mbar_wait_bounded(&sm.full_bar[i % STAGES], (i / STAGES) & 1)) set_error(p.error, kErrTimeout);
+      back.prev(STAGES);
+      if (!mbar_wait_bounded(&sm.full_bar[back.st], back.ph)) set_error(p.error, kErrTimeout);
     }
   }
 }
@@ -598,7 +621,7 @@ __device__ void consume_fma(const DecodeParams& p, const Work& w, const Smem& sm
   const int STAGES = p.stages, stage_bytes = 2 * p.tile_bytes;
   const int rs = p.smem_row_bytes / (int)sizeof(T);  // tile row stride (elements)
 
-  uint32_t it = 0;
+  RingPos pos{0, 0};
   bool first_seg = true;
   int b = w.b_first, g = w.g_begin;
   Seg s;
@@ -628,9 +651,9 @@ __device__ void consume_fma(const DecodeParams& p, const Work& w, const Smem& sm
       for (int e = 0; e < EPC; ++e) acc[gq][e] = 0.f;
     }
     bool ok = true;
-    for (int lp = s.lp0; lp < s.lp1; ++lp, ++it) {
-      const int st = it % STAGES;
-      if (!mbar_wait_bounded(&sm.full_bar[st], (it / STAGES) & 1)) {
+    for (int lp = s.lp0; lp < s.lp1; ++lp, pos.next(STAGES)) {
+      const int st = pos.st;
+      if (!mbar_wait_bounded(&sm.full_bar[st], pos.ph)) {
         ok = false;
         break;
       }
@@ -727,7 +750,7 @@ __device__ void consume_mma(const DecodeParams& p, const Work& w, const Smem& sm
         a_chunk) = a_row;
   };
 
-  uint32_t it = 0;
+  RingPos pos{0, 0};
   bool first_seg = true;
   int b = w.b_first, g = w.g_begin;
   Seg s;
@@ -758,9 +781,9 @@ __device__ void consume_mma(const DecodeParams& p, const Work& w, const Smem& sm
     for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = 0.f;
 
     bool ok = true;
-    for (int lp = s.lp0; lp < s.lp1; ++lp, ++it) {
-      const int st = it % STAGES;
-      if (!mbar_wait_bounded(&sm.full_bar[st], (it / STAGES) & 1)) {
+    for (int lp = s.lp0; lp < s.lp1; ++lp, pos.next(STAGES)) {
+      const int st = pos.st;
+      if (!mbar_wait_bounded(&sm.full_bar[st], pos.ph)) {
         ok = false;
         break;
       }
