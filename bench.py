@@ -56,6 +56,9 @@ def parse():
                     help="KV append as its own launch before attention (default: fused into one launch)")
     ap.add_argument("--no-overlap", dest="overlap", action="store_false",
                     help="no programmatic dependent launch between consecutive layer-calls")
+    ap.add_argument("--prep", action="store_true",
+                    help="layer-call = q/k RMSNorm + rotary embedding + KV append + attention in one launch "
+                         "(the attention block between the QKV projection and o_proj)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     return ap.parse_args()
@@ -159,7 +162,14 @@ def host_layer(dev, layer):
 
 
 def cpu_layer_call(oracle, host):
-    """The oracle's KV append then attention: one layer-call of the reference algorithm."""
+    """The oracle's KV append then attention: one layer-call of the reference algorithm
+    (with ``prep`` in host: the q/k RMSNorm and rotary embedding first)."""
+    if "prep" in host:
+        import torch
+        pr = host["prep"]
+        q, k, _ = oracle.qk_norm_rope(host["q"], host["k_new"], pr["q_w"], pr["k_w"], pr["rope"],
+                                      host["context_lens"].numpy() - 1, 1e-6)
+        host = dict(host, q=torch.from_numpy(q).to(host["q"].dtype), k_new=torch.from_numpy(k).to(host["q"].dtype))
     oracle.kv_append(host["k_new"], host["v_new"], host["k_cache"], host["v_cache"], host["slot_mapping"])
     _, st = oracle.paged_decode_attention(host["q"], host["k_cache"], host["v_cache"], host["block_table"],
                                           host["context_lens"])
@@ -186,7 +196,10 @@ def main():
     config = {"workload": args.workload, "batch": glay.batch if scaling == "strong" else glay.batch * world,
               "batch_per_gpu": sum(l.batch for _, l in parts), "ctx_mean": float(glay.context_lens.mean()),
               "heads": [glay.num_heads, glay.num_kv_heads, glay.head_dim], "page": glay.block_size,
-              "layers": args.layers, "kv_bytes_per_layer_per_gpu": int(sum(
+              "layers": args.layers,
+              "layer_call": ("q/k RMSNorm + rotary + KV append + attention" if args.prep
+                             else "KV append + attention"),
+              "kv_bytes_per_layer_per_gpu": int(sum(
                   2 * l.num_blocks * l.block_size * l.num_kv_heads * l.head_dim * ebytes for _, l in parts)),
               "l2": f"inputs > L2: {args.layers} rotating per-layer caches",
               "parallelism": f"{world} GPU(s), requests" + (" and long-context KV heads" if scaling == "strong"
@@ -237,6 +250,20 @@ def main():
     devs = [wl.materialize_device(lay, 7 + 31 * rank + i, spec["dtype"], spec["scale_values"], L)
             for i, (_, lay) in enumerate(parts)]
     outs = [[torch.empty_like(d["q"][l]) for l in range(L)] for d in devs]
+    if args.prep and args.separate:
+        raise SystemExit("--prep runs the fused launch; it does not combine with --separate")
+    rope = None
+    if args.prep:
+        # per-layer q_norm / k_norm weights near 1 and the model's rotary table
+        # (max_seq_len * 2 rows, as the model registers it)
+        D = glay.head_dim
+        g = torch.Generator(device=device)
+        g.manual_seed(11 + rank)
+        for d in devs:
+            td = d["q"][0].dtype
+            d["q_w"] = [(1 + 0.1 * torch.randn(D, generator=g, device=device)).to(td) for _ in range(L)]
+            d["k_w"] = [(1 + 0.1 * torch.randn(D, generator=g, device=device)).to(td) for _ in range(L)]
+        rope = pkg.rope_table(D, 2 * 2048, 500000.0, device=device)
     kw = dict(schedule=args.schedule, split_pages=args.split_pages)
     launches_per_call = (2 if args.separate else 1) + (1 if args.schedule == "split" else 0)
     calls_per_step = L * len(parts)
@@ -249,6 +276,10 @@ def main():
             timer[0].record()
         if args.separate:
             pkg.paged_attention(q, d["k_caches"][l], d["v_caches"][l], block_table, context_lens, out=out, **kw)
+        elif args.prep:
+            pkg.paged_decode_prep_attention(q, k_new, v_new, d["q_w"][l], d["k_w"][l], rope, d["k_caches"][l],
+                                            d["v_caches"][l], block_table, context_lens, 1e-6, out=out,
+                                            schedule=args.schedule, overlap_previous=args.overlap)
         else:
             # the previous kernel on the stream is another layer-call's attention (or a
             # copy): it writes neither this pool nor the block table / context lengths
@@ -319,10 +350,12 @@ def main():
     # ---- dominant kernel: average launch time on its own stream
     bytes_attn = sum(a["attention"] for a in abs_)
     bytes_call = sum(a["layer_call"] for a in abs_)
+    if args.prep:  # + the two norm weights and each sequence's rotary table row
+        bytes_call += sum(2 * l.head_dim * ebytes + l.batch * l.head_dim * 4 for _, l in parts)
     if graph is None:
         t_ms = [a.elapsed_time(b) for row in timers for (a, b) in row]
         kernel_avg_ms = sum(t_ms) / len(t_ms)
-    elif not args.separate and args.schedule != "split":
+    elif args.prep or (not args.separate and args.schedule != "split"):
         kernel_avg_ms = ms / (args.steps * calls_per_step)  # the step is exactly these launches
     else:
         def attn_only():
@@ -409,6 +442,7 @@ def main():
                 "d2h_bytes_per_step": int(d2h_all), "ms_per_step": round(e2e_ms / args.steps, 4)},
         "clocks": clocks.summary(),
         "graph": bool(graph is not None), "append": "separate launch" if args.separate else "fused",
+        "prep": "q/k RMSNorm + rotary fused" if args.prep else None,
         "overlap_previous": bool(args.overlap and not args.separate),
     }
     achieved = kernel_bytes / (kernel_avg_ms / 1e3) / 1e9
@@ -416,7 +450,9 @@ def main():
                         "frac": round(achieved / peak, 4), "traffic": profiled_traffic(args.workload),
                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                         else "fallback 6650 GB/s",
-                        "kernel": "paged_decode_mma_kernel" + ("" if args.separate else " (KV append fused)"),
+                        "kernel": "paged_decode_mma_kernel" + ("" if args.separate else
+                                                               " (q/k RMSNorm, rotary, KV append fused)" if args.prep
+                                                               else " (KV append fused)"),
                         "algorithmic_bytes_per_launch": int(kernel_bytes),
                         "avg_launch_us": round(kernel_avg_ms * 1e3, 2),
                         "timing": "per-launch CUDA events" if graph is None else "graph replay / launches"}
@@ -424,6 +460,8 @@ def main():
         from oracle import oracle
         oracle.build()
         host = host_layer(devs[0], 0)
+        if args.prep:
+            host["prep"] = {"q_w": devs[0]["q_w"][0].cpu(), "k_w": devs[0]["k_w"][0].cpu(), "rope": rope.cpu()}
         calls, t0 = 0, time.perf_counter()
         while True:
             cpu_layer_call(oracle, host)
@@ -434,7 +472,8 @@ def main():
         cpu_gbs = abs_[0]["layer_call"] * calls / el / 1e9
         line["cpu_baseline"] = {"value": round(cpu_gbs, 4), "unit": "GB/s", "cores": oracle.num_threads(),
                                 "kind": "port",
-                                "sample": f"{calls} layer-call(s) (append + attention) of layer 0 of this "
+                                "sample": f"{calls} layer-call(s) ({'norm + rotary + ' if args.prep else ''}"
+                                          f"append + attention) of layer 0 of this "
                                           f"workload, C oracle with OpenMP, {el:.1f} s"}
     if rank == 0:
         print(json.dumps(line))

@@ -47,6 +47,7 @@ extern "C" {
 #define UBX_DEVERR_NEG_CTX 4       /* negative context_len: treated as 0 */
 #define UBX_DEVERR_TIMEOUT 8       /* a pipeline wait exceeded its bound; output undefined */
 #define UBX_DEVERR_BAD_SLOT 16     /* kv_append slot >= num_blocks * block_size: row skipped */
+#define UBX_DEVERR_BAD_POSITION 32 /* rotary position outside [0, rope_positions): row left unrotated */
 
 /* work schedules of the attention kernel */
 #define UBX_SCHEDULE_AUTO 0     /* library picks */
@@ -158,6 +159,66 @@ int ubx_paged_decode_append_attention(const void* k_new, const void* v_new, int6
                                       int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
                                       int max_blocks_per_seq, float scale, int dtype, int schedule, int split_pages,
                                       int flags, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Pre-attention step of a decode step or a prefill chunk, one launch: for every
+ * token t (position positions[t]) and head, RMSNorm of the q and k head rows,
+ * then the rotary embedding at that position; q_out receives the rotated q rows,
+ * k_out (optional) the rotated k rows, and when k_cache is given the rotated k
+ * row and the unchanged v row are stored at slot_mapping[t] (negative slot:
+ * padding, not stored).
+ *   RMSNorm (unbox_platform/model/model.py:25-27): y = x * rsqrt(mean(x^2) + eps) * w
+ *   rotary  (model.py:36-48): (y[2j] + i y[2j+1]) * (cos + i sin) of rope row pos, pair j
+ * with the rounding of the reference's tensor ops in the model dtype (every op
+ * rounds its fp32 result to the dtype; fp32 tensors are not rounded).
+ * Replaces: q_norm/k_norm, the per-sequence apply_rotary_emb loop and the write_kv
+ * loop of InferenceEngine.decode_step (unbox_platform/infer/engine.py:201-215) and
+ * of prefill_step (engine.py:121-128).
+ *   q_in:  (num_tokens, num_heads, head_dim), strides (q_s_tok, q_s_head)
+ *   k_in, v_in: (num_tokens, num_kv_heads, head_dim), strides (k_s_tok, k_s_head), (v_s_tok, v_s_head)
+ *   q_weight, k_weight: (head_dim,) RMSNorm weights in the model dtype
+ *   rope:  (rope_positions, head_dim / 2, 2) fp32 (cos, sin) pairs, row stride rope_s_pos
+ *          (torch.view_as_real of the model's complex freqs_cis, model.py:30-34)
+ *   positions: (num_tokens,) int32
+ *   q_out: (num_tokens, num_heads, head_dim); k_out: (num_tokens, num_kv_heads, head_dim) or NULL
+ *   k_cache/v_cache/slot_mapping: as ubx_kv_append, or all NULL for no append
+ *   error_word: device int32 for UBX_DEVERR_BAD_POSITION / UBX_DEVERR_BAD_SLOT, may be NULL
+ * head_dim even, <= 256; element pairs must be 2-element aligned (pointers and strides).
+ */
+int ubx_qk_norm_rope_append(const void* q_in, int64_t q_s_tok, int64_t q_s_head, const void* k_in, int64_t k_s_tok,
+                            int64_t k_s_head, const void* v_in, int64_t v_s_tok, int64_t v_s_head,
+                            const void* q_weight, const void* k_weight, float eps, const float* rope,
+                            int64_t rope_s_pos, int rope_positions, const int32_t* positions, void* q_out,
+                            int64_t qo_s_tok, int64_t qo_s_head, void* k_out, int64_t ko_s_tok, int64_t ko_s_head,
+                            void* k_cache, void* v_cache, int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head,
+                            const int64_t* slot_mapping, int64_t num_blocks, int block_size, int64_t num_tokens,
+                            int num_heads, int num_kv_heads, int head_dim, int dtype, int32_t* error_word,
+                            void* stream);
+
+/*
+ * One launch per layer for the whole attention block of a decode step between the
+ * QKV projection and o_proj: RMSNorm + rotary embedding of q and of the new k
+ * row at position context_lens[b] - 1 (as ubx_qk_norm_rope_append), the KV append
+ * of that k row and of v_new, and paged decode attention over all
+ * context_lens[b] positions (as ubx_paged_decode_append_attention).
+ * Replaces: engine.py:201-224 of InferenceEngine.decode_step.
+ *   q_raw:  (batch, num_heads, head_dim) q projection, strides (q_s_b, q_s_h)
+ *   k_raw, v_new: (batch, num_kv_heads, head_dim) k and v projections, strides (new_s_tok, new_s_head)
+ *   q_weight, k_weight, eps, rope, rope_s_pos, rope_positions: as ubx_qk_norm_rope_append
+ * The other arguments are those of ubx_paged_decode_append_attention. Built for
+ * bf16 and f16 (fp32: UBX_ERR_UNSUPPORTED, run ubx_qk_norm_rope_append and then
+ * ubx_paged_decode_attention).
+ */
+int ubx_paged_decode_prep_attention(const void* q_raw, int64_t q_s_b, int64_t q_s_h, const void* k_raw,
+                                    const void* v_new, int64_t new_s_tok, int64_t new_s_head, const void* q_weight,
+                                    const void* k_weight, float eps, const float* rope, int64_t rope_s_pos,
+                                    int rope_positions, void* k_cache, void* v_cache, int64_t c_s_block,
+                                    int64_t c_s_tok, int64_t c_s_head, const int32_t* block_table, int64_t bt_s_row,
+                                    const int32_t* context_lens, void* out, int64_t o_s_b, int64_t o_s_h, int batch,
+                                    int num_heads, int num_kv_heads, int head_dim, int block_size,
+                                    int64_t num_blocks, int max_blocks_per_seq, float scale, int dtype, int schedule,
+                                    int split_pages, int flags, void* workspace, size_t workspace_bytes,
+                                    void* stream);
 
 /*
  * Allocation-free variant of ubx_paged_decode_attention. No counterpart in the

@@ -9,6 +9,9 @@ Each wrapper names the reference function it restates:
   paged_decode_attention  -> unbox_platform/infer/kernels/paged_decode_attention.py:157-191
   kv_append               -> unbox_platform/infer/kvcache.py:253-262 and :330-340
   slot_mapping            -> unbox_platform/infer/kvcache.py:338-339
+  rms_norm / rotary / qk_norm_rope -> unbox_platform/model/model.py:19-48 as the
+                             engine applies them (engine.py:201-210, :121-123);
+                             numpy, elementwise, no C library needed
 """
 from __future__ import annotations
 
@@ -147,3 +150,72 @@ def slot_mapping(block_table, positions, block_size: int):
     st = lib().oracle_slot_mapping(bt.ctypes.data, bt.shape[1], pos.ctypes.data, out.ctypes.data,
                                    pos.shape[0], bt.shape[1], block_size)
     return out, st
+
+
+# ---------------------------------------------------------------------------
+# pre-attention (numpy): RMSNorm + rotary embedding with the dtype's rounding
+# ---------------------------------------------------------------------------
+
+def _as_f32(x):
+    """float32 copy of a CPU torch tensor / numpy array and its dtype code."""
+    code = _dtype_code(x)
+    a = _np(x)
+    if code == BF16:
+        a = (np.asarray(a, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+    return np.array(a, dtype=np.float32), code
+
+
+def round_to(a: np.ndarray, code: int) -> np.ndarray:
+    """Round float32 values to the dtype (nearest-even) and back to float32: what
+    a torch op on a 16-bit tensor does with its fp32 result."""
+    a = np.asarray(a, dtype=np.float32)
+    if code == F32:
+        return a
+    if code == F16:
+        return a.astype(np.float16).astype(np.float32)
+    u = a.view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)
+
+
+def rms_norm(x: np.ndarray, w: np.ndarray, eps: float, code: int) -> np.ndarray:
+    """RMSNorm.forward (model.py:25-27) over the last axis:
+    x * rsqrt(mean(x^2) + eps) * w, rounding after every tensor op (the mean as
+    the fp32 sum times 1/D, rounded once)."""
+    x = np.asarray(x, dtype=np.float32)
+    sq = round_to(x * x, code)
+    mean = round_to(sq.sum(axis=-1, keepdims=True, dtype=np.float32) * np.float32(1.0 / x.shape[-1]), code)
+    r = round_to(np.float32(1.0) / np.sqrt(round_to(mean + np.float32(eps), code)), code)
+    return round_to(round_to(x * r, code) * np.asarray(w, dtype=np.float32), code)
+
+
+def rotary(y: np.ndarray, cos_sin: np.ndarray, code: int) -> np.ndarray:
+    """apply_rotary_emb's rotate (model.py:41-46): pairs (2j, 2j+1) of the last
+    axis as complex numbers times (cos + i sin), in fp32, rounded to the dtype.
+    ``cos_sin`` broadcasts against y[..., ::2] with a trailing (cos, sin) axis."""
+    a, b = y[..., 0::2], y[..., 1::2]
+    c, s = cos_sin[..., 0], cos_sin[..., 1]
+    out = np.empty_like(y)
+    out[..., 0::2] = a * c - b * s
+    out[..., 1::2] = a * s + b * c
+    return round_to(out, code)
+
+
+def qk_norm_rope(q, k, q_weight, k_weight, rope, positions, eps: float = 1e-6):
+    """q (T, H, D), k (T, KVH, D): RMSNorm with q_weight / k_weight, then the rotary
+    embedding at positions[t] (rows of ``rope``, (P, D/2, 2) fp32). A position
+    outside [0, P) leaves its rows unrotated and is reported.
+    Returns (q_out, k_out) float32 holding dtype values, and the bad-position mask."""
+    qf, code = _as_f32(q)
+    kf, _ = _as_f32(k)
+    qw, _ = _as_f32(q_weight)
+    kw, _ = _as_f32(k_weight)
+    tab = np.asarray(_np(rope), dtype=np.float32)
+    pos = np.asarray(_np(positions)).astype(np.int64)
+    bad = (pos < 0) | (pos >= tab.shape[0])
+    cs = tab[np.where(bad, 0, pos)].copy()  # (T, D/2, 2)
+    cs[bad] = (1.0, 0.0)
+    cs = cs[:, None, :, :]                   # broadcast over heads
+    q_out = rotary(rms_norm(qf, qw, eps, code), cs, code)
+    k_out = rotary(rms_norm(kf, kw, eps, code), cs, code)
+    return q_out, k_out, bad

@@ -41,7 +41,9 @@ def sha(t) -> str:
     return hashlib.sha256(x.numpy().tobytes()).hexdigest()
 
 
-GOLDEN_NAMES = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
+_ALL_GOLDEN = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
+GOLDEN_NAMES = [n for n in _ALL_GOLDEN if not n.startswith("prep_")]   # append + attention cases
+PREP_GOLDEN_NAMES = [n for n in _ALL_GOLDEN if n.startswith("prep_")]  # norm + rotary (+ append, attention)
 
 
 def load_golden(name: str):
@@ -58,6 +60,33 @@ def load_golden(name: str):
         assert sha(t[k]) == str(z["sha_" + k]), f"{name}: regenerated {k} differs from the fixture's inputs"
     assert np.array_equal(t["slot_mapping"].numpy(), z["slot_mapping"])
     return z, lay, t
+
+
+def load_prep_golden(name: str):
+    """Pre-attention fixture: the record, the regenerated inputs (checked by
+    SHA-256), the pool before the write, the layout and a rotary table of
+    ``rope_positions`` rows holding the reference's rows at the used positions
+    (the other rows are zero and never read)."""
+    import torch
+    z = dict(np.load(os.path.join(GOLDEN_DIR, name + ".npz")))
+    wl = PKG.workloads
+    H, KVH, D = int(z["num_heads"]), int(z["num_kv_heads"]), int(z["head_dim"])
+    T, dtype, seed = int(z["num_tokens"]), str(z["dtype"]), int(z["seed"])
+    if str(z["kind"]) == "decode":
+        lay = wl.Layout(z["context_lens"], z["block_table"], int(z["num_blocks"]), H, KVH, D, int(z["block_size"]))
+    else:
+        start = int(z["start_pos"])
+        lay = wl.Layout(np.array([start + T], dtype=np.int32), z["block_table_row"][None, :].copy(),
+                        int(z["num_blocks"]), H, KVH, D, int(z["block_size"]))
+    caches = wl.materialize_host(lay, seed, dtype=dtype)
+    x = wl.materialize_prep_host(seed, T, H, KVH, D, dtype=dtype)
+    for k in ("q_raw", "k_raw", "v_new", "q_weight", "k_weight"):
+        assert sha(x[k]) == str(z["sha_" + k]), f"{name}: regenerated {k} differs from the fixture's inputs"
+    for k in ("k_cache", "v_cache"):
+        assert sha(caches[k]) == str(z["sha_" + k]), f"{name}: regenerated {k} differs"
+    rope = np.zeros((int(z["rope_positions"]), D // 2, 2), dtype=np.float32)
+    rope[z["positions"]] = z["rope_rows"]
+    return z, lay, x, caches, torch.from_numpy(rope)
 
 
 @pytest.fixture(scope="session")

@@ -35,6 +35,24 @@ def test_library_exports_every_declared_symbol(pkg):
         assert re.search(rf"\bT {s}\b", nm), s
 
 
+def declared_arities():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    out = {}
+    for m in re.finditer(r"\b(ubx_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", src):
+        args = m.group(2).strip()
+        out[m.group(1)] = 0 if args in ("", "void") else args.count(",") + 1
+    return out
+
+
+def test_ctypes_signatures_match_header_arity(pkg):
+    """Every ctypes stub passes exactly as many arguments as the C declaration takes."""
+    ar = declared_arities()
+    assert set(ar) == set(declared_symbols())
+    for name, n in ar.items():
+        assert len(pkg.library.SIGNATURES[name][1]) == n, (name, n, len(pkg.library.SIGNATURES[name][1]))
+
+
 def test_host_only_entry_points(pkg):
     lib = pkg.library.load()
     assert lib.ubx_version() >= 100

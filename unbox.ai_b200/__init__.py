@@ -25,17 +25,30 @@ unbox_platform/infer/kvcache.py of the reference):
   in a single launch.
 * ``slot_mapping(block_table, positions, block_size)`` -- device-side slot
   computation (kvcache.py:338-339) for one decode step.
+* ``qk_norm_rope(q, k, q_weight, k_weight, rope, positions, eps, ...)`` -- the
+  q/k RMSNorm and rotary embedding of T tokens (model.py:19-48 as used at
+  engine.py:201-210), optionally with the KV append, in one launch.
+* ``paged_decode_prep_attention(q_raw, k_raw, v_new, q_weight, k_weight, rope,
+  k_cache, v_cache, block_table, context_lens, eps)`` -- norm, rotary, append
+  and attention of one decode layer (engine.py:201-224) in one launch.
+* ``prefill_kv_write`` / ``prefill_prep`` -- a prefill chunk's KV write
+  (engine.py:126-128), alone or with its norm and rotary steps (:121-128).
+* ``rope_table(head_dim, num_positions, theta)`` -- the (cos, sin) table of
+  precompute_freqs_cis (model.py:30-34).
 """
 from . import workloads  # noqa: F401  (pure Python, no CUDA needed)
 
 __all__ = [
     "paged_decode_attention", "paged_attention", "paged_attention_split", "kv_append",
-    "slot_mapping", "DecodeWorkspace", "workloads", "library", "sharding",
+    "slot_mapping", "DecodeWorkspace", "workloads", "library", "sharding", "qk_norm_rope",
+    "paged_decode_prep_attention", "prefill_kv_write", "prefill_prep", "prefill_slots", "rope_table",
 ]
 
 
 _OPS = ("paged_decode_attention", "paged_attention", "paged_attention_split", "kv_append", "slot_mapping",
-        "DecodeWorkspace", "check_device_errors", "workspace_for", "paged_decode_append_attention")
+        "DecodeWorkspace", "check_device_errors", "workspace_for", "paged_decode_append_attention",
+        "qk_norm_rope", "paged_decode_prep_attention", "prefill_kv_write", "prefill_prep", "prefill_slots",
+        "rope_table")
 
 
 def __getattr__(name):

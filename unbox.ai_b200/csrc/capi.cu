@@ -216,6 +216,84 @@ int ubx_slot_mapping(const int32_t* block_table, int64_t bt_s_row, const int32_t
   return UBX_OK;
 }
 
+int ubx_qk_norm_rope_append(const void* q_in, int64_t q_s_tok, int64_t q_s_head, const void* k_in, int64_t k_s_tok,
+                            int64_t k_s_head, const void* v_in, int64_t v_s_tok, int64_t v_s_head,
+                            const void* q_weight, const void* k_weight, float eps, const float* rope,
+                            int64_t rope_s_pos, int rope_positions, const int32_t* positions, void* q_out,
+                            int64_t qo_s_tok, int64_t qo_s_head, void* k_out, int64_t ko_s_tok, int64_t ko_s_head,
+                            void* k_cache, void* v_cache, int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head,
+                            const int64_t* slot_mapping, int64_t num_blocks, int block_size, int64_t num_tokens,
+                            int num_heads, int num_kv_heads, int head_dim, int dtype, int32_t* error_word,
+                            void* stream) {
+  g_last_error.clear();
+  if (dtype != UBX_DTYPE_F32 && dtype != UBX_DTYPE_BF16 && dtype != UBX_DTYPE_F16)
+    return fail(UBX_ERR_INVALID_ARGUMENT, "unknown dtype code %d", dtype);
+  if (num_tokens < 0 || num_heads <= 0 || num_kv_heads <= 0)
+    return fail(UBX_ERR_INVALID_ARGUMENT, "bad token or head count");
+  if (head_dim < 2 || head_dim > 256 || (head_dim & 1))
+    return fail(UBX_ERR_UNSUPPORTED, "head_dim %d not built (even, <= 256)", head_dim);
+  if (num_tokens == 0) return UBX_OK;
+  if (!q_in || !k_in || !q_weight || !k_weight || !rope || !positions || !q_out)
+    return fail(UBX_ERR_INVALID_ARGUMENT, "null pointer");
+  if (rope_positions <= 0 || rope_s_pos < head_dim || (rope_s_pos & 1) || (reinterpret_cast<uintptr_t>(rope) & 7))
+    return fail(UBX_ERR_INVALID_ARGUMENT, "rope table: %d rows, row stride %lld floats (even, >= %d), 8-byte aligned",
+                rope_positions, (long long)rope_s_pos, head_dim);
+  if (!(eps >= 0.f) || eps > 1e30f) return fail(UBX_ERR_INVALID_ARGUMENT, "eps must be finite, >= 0");
+  const bool append = k_cache != nullptr;
+  if (append && (!v_cache || !v_in || !slot_mapping || num_blocks <= 0 || block_size <= 0))
+    return fail(UBX_ERR_INVALID_ARGUMENT, "append needs v_in, v_cache, slot_mapping and a positive pool size");
+  const int es = dtype_bytes(dtype);
+  const uintptr_t pa = 2u * (uintptr_t)es;  // element-pair alignment
+  auto ap = [&](const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) % pa) == 0; };
+  auto ev = [](int64_t st) { return (st & 1) == 0; };
+  if (!ap(q_in) || !ap(k_in) || !ap(v_in) || !ap(q_weight) || !ap(k_weight) || !ap(q_out) || !ap(k_out) ||
+      !ap(k_cache) || !ap(v_cache))
+    return fail(UBX_ERR_INVALID_ARGUMENT, "rows must be aligned to element pairs (%d bytes)", (int)pa);
+  if (!ev(q_s_tok) || !ev(q_s_head) || !ev(k_s_tok) || !ev(k_s_head) || !ev(qo_s_tok) || !ev(qo_s_head) ||
+      (k_out && (!ev(ko_s_tok) || !ev(ko_s_head))) ||
+      (append && (!ev(v_s_tok) || !ev(v_s_head) || !ev(c_s_block) || !ev(c_s_tok) || !ev(c_s_head))))
+    return fail(UBX_ERR_INVALID_ARGUMENT, "strides must be even (element pairs)");
+  PrepParams p;
+  p.q_in = q_in;
+  p.k_in = k_in;
+  p.v_in = v_in;
+  p.q_st = q_s_tok;
+  p.q_sh = q_s_head;
+  p.k_st = k_s_tok;
+  p.k_sh = k_s_head;
+  p.v_st = v_s_tok;
+  p.v_sh = v_s_head;
+  p.q_w = q_weight;
+  p.k_w = k_weight;
+  p.eps = eps;
+  p.rope = rope;
+  p.rope_sp = rope_s_pos;
+  p.rope_n = rope_positions;
+  p.positions = positions;
+  p.q_out = q_out;
+  p.qo_st = qo_s_tok;
+  p.qo_sh = qo_s_head;
+  p.k_out = k_out;
+  p.ko_st = ko_s_tok;
+  p.ko_sh = ko_s_head;
+  p.k_cache = append ? k_cache : nullptr;
+  p.v_cache = append ? v_cache : nullptr;
+  p.c_sblk = c_s_block;
+  p.c_stok = c_s_tok;
+  p.c_sh = c_s_head;
+  p.slots = slot_mapping;
+  p.num_blocks = num_blocks;
+  p.block_size = block_size;
+  p.num_tokens = num_tokens;
+  p.num_heads = num_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.head_dim = head_dim;
+  p.error = error_word;
+  cudaError_t e = launch_qk_norm_rope(dtype, p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "qk_norm_rope launch");
+  return UBX_OK;
+}
+
 int ubx_paged_decode_workspace_size(int batch, int num_heads, int head_dim, int max_blocks_per_seq, int split_pages,
                                     size_t* bytes) {
   g_last_error.clear();
@@ -261,12 +339,21 @@ struct AppendArgs {
   int64_t s_tok, s_head;  // element strides of k_new / v_new
 };
 
+struct PrepArgs {
+  const void* q_w;
+  const void* k_w;
+  float eps;
+  const float* rope;
+  int64_t rope_sp;
+  int rope_n;
+};
+
 int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache, const void* v_cache,
                 int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head, const int32_t* block_table, int64_t bt_s_row,
                 const int32_t* context_lens, void* out, int64_t o_s_b, int64_t o_s_h, int batch, int num_heads,
                 int num_kv_heads, int head_dim, int block_size, int64_t num_blocks, int max_blocks_per_seq,
                 float scale, int dtype, int schedule, int split_pages, int flags, void* workspace,
-                size_t workspace_bytes, const AppendArgs* app, void* stream) {
+                size_t workspace_bytes, const AppendArgs* app, const PrepArgs* prep, void* stream) {
   g_last_error.clear();
   int st = check_shape(num_heads, num_kv_heads, head_dim, block_size, dtype);
   if (st != UBX_OK) return st;
@@ -293,6 +380,18 @@ int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache
     if (!app->k_new || !app->v_new) return fail(UBX_ERR_INVALID_ARGUMENT, "null k_new / v_new");
     if (!aligned16(app->k_new) || !aligned16(app->v_new) || !m16(app->s_tok) || !m16(app->s_head))
       return fail(UBX_ERR_INVALID_ARGUMENT, "k_new / v_new rows must be 16-byte aligned");
+  }
+  if (prep) {
+    if (es != 2)
+      return fail(UBX_ERR_UNSUPPORTED, "fused pre-attention is built for bf16/f16 (fp32: ubx_qk_norm_rope_append, "
+                                       "then ubx_paged_decode_attention)");
+    if (!prep->q_w || !prep->k_w || !prep->rope) return fail(UBX_ERR_INVALID_ARGUMENT, "null norm weight or rope table");
+    if (!aligned16(prep->q_w) || !aligned16(prep->k_w) || !aligned16(prep->rope) || (prep->rope_sp & 3))
+      return fail(UBX_ERR_INVALID_ARGUMENT, "norm weights and rope rows must be 16-byte aligned");
+    if (prep->rope_n <= 0 || prep->rope_sp < head_dim)
+      return fail(UBX_ERR_INVALID_ARGUMENT, "rope table of %d rows with row stride %lld floats (need >= %d)",
+                  prep->rope_n, (long long)prep->rope_sp, head_dim);
+    if (!(prep->eps >= 0.f) || prep->eps > 1e30f) return fail(UBX_ERR_INVALID_ARGUMENT, "eps must be finite, >= 0");
   }
   if (!(scale > 0.f) && !(scale < 0.f)) return fail(UBX_ERR_INVALID_ARGUMENT, "scale must be finite and non-zero");
   if (flags & ~UBX_FLAG_OVERLAP_PREVIOUS) return fail(UBX_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
@@ -347,6 +446,12 @@ int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache
   p.v_new = app ? app->v_new : nullptr;
   p.n_stok = app ? app->s_tok : 0;
   p.n_sh = app ? app->s_head : 0;
+  p.q_w = prep ? prep->q_w : nullptr;
+  p.k_w = prep ? prep->k_w : nullptr;
+  p.eps = prep ? prep->eps : 0.f;
+  p.rope = prep ? prep->rope : nullptr;
+  p.rope_sp = prep ? prep->rope_sp : 0;
+  p.rope_n = prep ? prep->rope_n : 0;
 
   LaunchShape shape{pl.grid, pl.block, pl.smem, (flags & UBX_FLAG_OVERLAP_PREVIOUS) != 0};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -372,7 +477,7 @@ int ubx_paged_decode_attention(const void* q, int64_t q_s_b, int64_t q_s_h, cons
   return decode_impl(q, q_s_b, q_s_h, k_cache, v_cache, c_s_block, c_s_tok, c_s_head, block_table, bt_s_row,
                      context_lens, out, o_s_b, o_s_h, batch, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
                      max_blocks_per_seq, scale, dtype, schedule, split_pages, 0, workspace, workspace_bytes, nullptr,
-                     stream);
+                     nullptr, stream);
 }
 
 int ubx_paged_decode_append_attention(const void* k_new, const void* v_new, int64_t new_s_tok, int64_t new_s_head,
@@ -387,7 +492,25 @@ int ubx_paged_decode_append_attention(const void* k_new, const void* v_new, int6
   return decode_impl(q, q_s_b, q_s_h, k_cache, v_cache, c_s_block, c_s_tok, c_s_head, block_table, bt_s_row,
                      context_lens, out, o_s_b, o_s_h, batch, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
                      max_blocks_per_seq, scale, dtype, schedule, split_pages, flags, workspace, workspace_bytes, &app,
-                     stream);
+                     nullptr, stream);
+}
+
+int ubx_paged_decode_prep_attention(const void* q_raw, int64_t q_s_b, int64_t q_s_h, const void* k_raw,
+                                    const void* v_new, int64_t new_s_tok, int64_t new_s_head, const void* q_weight,
+                                    const void* k_weight, float eps, const float* rope, int64_t rope_s_pos,
+                                    int rope_positions, void* k_cache, void* v_cache, int64_t c_s_block,
+                                    int64_t c_s_tok, int64_t c_s_head, const int32_t* block_table, int64_t bt_s_row,
+                                    const int32_t* context_lens, void* out, int64_t o_s_b, int64_t o_s_h, int batch,
+                                    int num_heads, int num_kv_heads, int head_dim, int block_size,
+                                    int64_t num_blocks, int max_blocks_per_seq, float scale, int dtype, int schedule,
+                                    int split_pages, int flags, void* workspace, size_t workspace_bytes,
+                                    void* stream) {
+  const AppendArgs app{k_raw, v_new, new_s_tok, new_s_head};
+  const PrepArgs prep{q_weight, k_weight, eps, rope, rope_s_pos, rope_positions};
+  return decode_impl(q_raw, q_s_b, q_s_h, k_cache, v_cache, c_s_block, c_s_tok, c_s_head, block_table, bt_s_row,
+                     context_lens, out, o_s_b, o_s_h, batch, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
+                     max_blocks_per_seq, scale, dtype, schedule, split_pages, flags, workspace, workspace_bytes, &app,
+                     &prep, stream);
 }
 
 }  // extern "C"

@@ -39,6 +39,7 @@
 
 #include "ubx_common.cuh"
 #include "ubx_internal.h"
+#include "ubx_prep.cuh"
 
 namespace ubx {
 
@@ -716,6 +717,75 @@ __device__ void consume_fma(const DecodeParams& p, const Work& w, const Smem& sm
   }
 }
 
+// Fused pre-attention at a segment start (tensor-core path): RMSNorm and the
+// rotary embedding at position `pos`, applied to this warp's q rows, held in MMA
+// A-fragment layout (lane (qr, qc) holds, per k-step ks, the element pairs at
+// columns 16ks + 2qc and 16ks + 8 + 2qc of row qr; the 4 lanes of a quad hold a
+// whole row), and to the appended K row (lane c < D/8 holds elements 8c..8c+7).
+// Same steps and rounding as qk_norm_rope_kernel (model.py:25-27, :36-48).
+template <typename T, int D>
+__device__ __forceinline__ void prep_rows(const DecodeParams& p, int pos, bool real_row, int qc, int lane, bool append,
+                                          uint32_t (&qa)[D / 16][2], uint4& a_row) {
+  constexpr int KS = D / 16, RC = D / 8;
+  const float inv_d = 1.f / (float)D;
+  const bool pos_ok = pos >= 0 && pos < p.rope_n;
+  if (!pos_ok && lane == 0) set_error(p.error, kErrBadPosition);
+  const float2* rope_row = reinterpret_cast<const float2*>(p.rope + (int64_t)(pos_ok ? pos : 0) * p.rope_sp);
+  {
+    float ss = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float2 x = unpack_word<T>(qa[ks][h]);
+        ss += rounded_square<T>(x.x) + rounded_square<T>(x.y);
+      }
+    ss += __shfl_xor_sync(kFull, ss, 1);
+    ss += __shfl_xor_sync(kFull, ss, 2);
+    const float rf = rms_factor<T>(ss, inv_d, p.eps);
+    const uint32_t* w = static_cast<const uint32_t*>(p.q_w);
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int j = 8 * ks + 4 * h + qc;  // element pair index of column 16ks + 8h + 2qc
+        const float2 x = unpack_word<T>(qa[ks][h]);
+        const float2 wv = unpack_word<T>(__ldg(w + j));
+        const float2 cs = pos_ok ? __ldg(rope_row + j) : make_float2(1.f, 0.f);
+        const float2 o = rotate_pair(rms_apply<T>(x.x, rf, wv.x), rms_apply<T>(x.y, rf, wv.y), cs.x, cs.y);
+        qa[ks][h] = real_row ? Elem<T>::pack2(o.x, o.y) : 0u;
+      }
+  }
+  if (append) {  // warp-uniform
+    float f[8];
+    Elem<T>::unpack(a_row, f);
+    const bool k_lane = lane < RC;
+    float ss = 0.f;
+    if (k_lane) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += rounded_square<T>(f[i]);
+    }
+    ss = warp_sum(ss);
+    if (k_lane) {
+      const float rf = rms_factor<T>(ss, inv_d, p.eps);
+      float wf[8];
+      Elem<T>::unpack(__ldg(static_cast<const uint4*>(p.k_w) + lane), wf);
+      const float4* rp = reinterpret_cast<const float4*>(rope_row + 4 * lane);
+      const float4 r01 = pos_ok ? __ldg(rp) : make_float4(1.f, 0.f, 1.f, 0.f);
+      const float4 r23 = pos_ok ? __ldg(rp + 1) : make_float4(1.f, 0.f, 1.f, 0.f);
+      const float cs[8] = {r01.x, r01.y, r01.z, r01.w, r23.x, r23.y, r23.z, r23.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 o = rotate_pair(rms_apply<T>(f[2 * i], rf, wf[2 * i]), rms_apply<T>(f[2 * i + 1], rf, wf[2 * i + 1]),
+                                     cs[2 * i], cs[2 * i + 1]);
+        f[2 * i] = o.x;
+        f[2 * i + 1] = o.y;
+      }
+      a_row = Elem<T>::pack(f);
+    }
+  }
+}
+
 // Tensor-core consumer (bf16 / fp16): warp = one KV head with all G <= 8 of its
 // query heads as the rows of a 16-row MMA tile (rows >= G are zero).
 //   QK:  S^T[16 q x 16 tok] = Q[16 x D] K^T   (m16n8k16, K rows via ldmatrix)
@@ -769,11 +839,11 @@ __device__ void consume_mma(const DecodeParams& p, const Work& w, const Smem& sm
         qa[ks][0] = real_row ? __ldg(reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 2 * qc)) : 0u;
         qa[ks][1] = real_row ? __ldg(reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 8 + 2 * qc)) : 0u;
       }
-      if (append && lane < 2 * RC) {
+      if (append && lane < 2 * RC)
         a_row = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a_which ? p.v_new : p.k_new) +
                                                      (int64_t)s.b * p.n_stok + (int64_t)kvh * p.n_sh) + a_chunk);
-        store_appended(s, a_slot, a_row);
-      }
+      if (p.rope) prep_rows<T, D>(p, ctx_raw - 1, real_row, qc, lane, append, qa, a_row);
+      if (append && lane < 2 * RC) store_appended(s, a_slot, a_row);
     }
     float m = -INFINITY, l = 0.f;
     float o[NT][2];  // rows 0..7 of the O tile (q heads); rows 8..15 are padding

@@ -1,0 +1,150 @@
+// Pre-attention step as one launch (sm_100a): per-head RMSNorm of q and k, the
+// rotary embedding at each token's position, and the KV append of the rotated k
+// and the raw v rows.
+//
+// Replaces, for the T tokens of a decode step (one per sequence) or of a prefill
+// chunk, the reference's
+//   xq = q_norm(xq); xk = k_norm(xk)                 engine.py:201-202 / :121-122
+//   per-sequence apply_rotary_emb at pos (.item())   engine.py:204-210 / :123
+//   per-token write_kv(layer, seq, pos, xk, xv)      engine.py:213-215 / :126-128
+// (RMSNorm: unbox_platform/model/model.py:19-27; rotary: model.py:30-48; the
+// write: kvcache.py:330-340). One warp handles one (token, head) row; the warps
+// of K heads also store the token's K and V rows into the pool.
+#include "ubx_common.cuh"
+#include "ubx_internal.h"
+#include "ubx_prep.cuh"
+
+namespace ubx {
+
+namespace {
+
+constexpr int kPrepWarps = 8;
+constexpr int kMaxPairsPerLane = 4;  // head_dim <= 256
+
+template <typename T>
+__device__ __forceinline__ float2 load_pair(const T* p);
+template <>
+__device__ __forceinline__ float2 load_pair<float>(const float* p) {
+  return __ldg(reinterpret_cast<const float2*>(p));
+}
+template <>
+__device__ __forceinline__ float2 load_pair<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return unpack_word<__nv_bfloat16>(__ldg(reinterpret_cast<const uint32_t*>(p)));
+}
+template <>
+__device__ __forceinline__ float2 load_pair<__half>(const __half* p) {
+  return unpack_word<__half>(__ldg(reinterpret_cast<const uint32_t*>(p)));
+}
+
+template <typename T>
+__device__ __forceinline__ void store_pair(T* p, float2 v);
+template <>
+__device__ __forceinline__ void store_pair<float>(float* p, float2 v) {
+  *reinterpret_cast<float2*>(p) = v;
+}
+template <>
+__device__ __forceinline__ void store_pair<__nv_bfloat16>(__nv_bfloat16* p, float2 v) {
+  *reinterpret_cast<uint32_t*>(p) = Elem<__nv_bfloat16>::pack2(v.x, v.y);
+}
+template <>
+__device__ __forceinline__ void store_pair<__half>(__half* p, float2 v) {
+  *reinterpret_cast<uint32_t*>(p) = Elem<__half>::pack2(v.x, v.y);
+}
+
+// Raw copy of one element pair (the V row goes to the pool unchanged).
+template <typename T>
+__device__ __forceinline__ void copy_pair(T* dst, const T* src) {
+  if constexpr (sizeof(T) == 4)
+    *reinterpret_cast<uint2*>(dst) = __ldg(reinterpret_cast<const uint2*>(src));
+  else
+    *reinterpret_cast<uint32_t*>(dst) = __ldg(reinterpret_cast<const uint32_t*>(src));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kPrepWarps * 32) qk_norm_rope_kernel(const PrepParams p) {
+  const int lane = threadIdx.x & 31;
+  const int rows_per_token = p.num_heads + p.num_kv_heads;
+  const int64_t rows = p.num_tokens * rows_per_token;
+  const int np = p.head_dim / 2;
+  const float inv_d = 1.f / (float)p.head_dim;
+  const int64_t limit = p.num_blocks * p.block_size;
+  for (int64_t r = (int64_t)blockIdx.x * kPrepWarps + (threadIdx.x >> 5); r < rows;
+       r += (int64_t)gridDim.x * kPrepWarps) {
+    const int64_t t = r / rows_per_token;
+    const int h = (int)(r % rows_per_token);
+    const bool is_q = h < p.num_heads;
+    const int hk = h - p.num_heads;
+    const T* x = is_q ? static_cast<const T*>(p.q_in) + t * p.q_st + (int64_t)h * p.q_sh
+                      : static_cast<const T*>(p.k_in) + t * p.k_st + (int64_t)hk * p.k_sh;
+    const T* w = static_cast<const T*>(is_q ? p.q_w : p.k_w);
+    const int pos = __ldg(&p.positions[t]);
+    const bool pos_ok = pos >= 0 && pos < p.rope_n;
+    if (!pos_ok && lane == 0 && h == 0) set_error(p.error, kErrBadPosition);
+
+    float2 v[kMaxPairsPerLane];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxPairsPerLane; ++i) {
+      const int j = lane + 32 * i;
+      v[i] = j < np ? load_pair<T>(x + 2 * j) : make_float2(0.f, 0.f);
+      ss += rounded_square<T>(v[i].x) + rounded_square<T>(v[i].y);
+    }
+    const float rf = rms_factor<T>(warp_sum(ss), inv_d, p.eps);
+
+    // destinations of this row
+    T* dst = nullptr;
+    T* dst_cache = nullptr;
+    T* dst_v = nullptr;
+    const T* src_v = nullptr;
+    if (is_q) {
+      dst = static_cast<T*>(p.q_out) + t * p.qo_st + (int64_t)h * p.qo_sh;
+    } else {
+      if (p.k_out) dst = static_cast<T*>(p.k_out) + t * p.ko_st + (int64_t)hk * p.ko_sh;
+      if (p.k_cache) {
+        const int64_t slot = __ldg(&p.slots[t]);
+        if (slot >= limit) {
+          if (lane == 0 && hk == 0) set_error(p.error, kErrBadSlot);
+        } else if (slot >= 0) {
+          const int64_t off = (slot / p.block_size) * p.c_sblk + (slot % p.block_size) * p.c_stok + (int64_t)hk * p.c_sh;
+          dst_cache = static_cast<T*>(p.k_cache) + off;
+          dst_v = static_cast<T*>(p.v_cache) + off;
+          src_v = static_cast<const T*>(p.v_in) + t * p.v_st + (int64_t)hk * p.v_sh;
+        }
+      }
+    }
+    const float* rope_row = p.rope + (int64_t)(pos_ok ? pos : 0) * p.rope_sp;
+#pragma unroll
+    for (int i = 0; i < kMaxPairsPerLane; ++i) {
+      const int j = lane + 32 * i;
+      if (j >= np) break;
+      const float2 wv = load_pair<T>(w + 2 * j);
+      const float y0 = rms_apply<T>(v[i].x, rf, wv.x), y1 = rms_apply<T>(v[i].y, rf, wv.y);
+      const float2 cs = pos_ok ? __ldg(reinterpret_cast<const float2*>(rope_row) + j) : make_float2(1.f, 0.f);
+      const float2 o = rotate_pair(y0, y1, cs.x, cs.y);
+      const float2 out = make_float2(round_to<T>(o.x), round_to<T>(o.y));
+      if (dst) store_pair<T>(dst + 2 * j, out);
+      if (dst_cache) {
+        store_pair<T>(dst_cache + 2 * j, out);
+        copy_pair<T>(dst_v + 2 * j, src_v + 2 * j);
+      }
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_qk_norm_rope(int dtype, const PrepParams& p, cudaStream_t stream) {
+  const int64_t rows = p.num_tokens * (p.num_heads + p.num_kv_heads);
+  if (rows == 0) return cudaSuccess;
+  const int64_t want = (rows + kPrepWarps - 1) / kPrepWarps;
+  const int blocks = (int)(want < 148 * 32 ? want : 148 * 32);
+  switch (dtype) {
+    case 0: qk_norm_rope_kernel<float><<<blocks, kPrepWarps * 32, 0, stream>>>(p); break;
+    case 1: qk_norm_rope_kernel<__nv_bfloat16><<<blocks, kPrepWarps * 32, 0, stream>>>(p); break;
+    case 2: qk_norm_rope_kernel<__half><<<blocks, kPrepWarps * 32, 0, stream>>>(p); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace ubx

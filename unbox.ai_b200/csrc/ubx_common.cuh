@@ -24,6 +24,7 @@ enum : int32_t {
   kErrNegCtx = UBX_DEVERR_NEG_CTX,            // negative context length
   kErrTimeout = UBX_DEVERR_TIMEOUT,           // a pipeline wait exceeded its bound
   kErrBadSlot = UBX_DEVERR_BAD_SLOT,          // append slot >= num_blocks * block_size
+  kErrBadPosition = UBX_DEVERR_BAD_POSITION,  // rotary position outside the table
 };
 
 __device__ __forceinline__ void set_error(int32_t* err, int32_t bit) {

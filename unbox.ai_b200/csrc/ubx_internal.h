@@ -64,6 +64,43 @@ struct DecodeParams {
   const void* k_new;
   const void* v_new;
   int64_t n_stok, n_sh;
+  // fused pre-attention (null rope: q and k_new are used as given): RMSNorm with
+  // q_w / k_w and the rotary embedding at position context_lens[b] - 1 are
+  // applied to q and to the appended k row
+  const void* q_w;
+  const void* k_w;
+  float eps;
+  const float* rope;   // (rope_n, head_dim / 2) float2 (cos, sin)
+  int64_t rope_sp;     // float stride between rope rows
+  int rope_n;
+};
+
+// Standalone pre-attention step (qk_norm_rope.cu); strides in elements.
+struct PrepParams {
+  const void* q_in;
+  const void* k_in;
+  const void* v_in;
+  int64_t q_st, q_sh, k_st, k_sh, v_st, v_sh;
+  const void* q_w;
+  const void* k_w;
+  float eps;
+  const float* rope;
+  int64_t rope_sp;
+  int rope_n;
+  const int32_t* positions;
+  void* q_out;
+  int64_t qo_st, qo_sh;
+  void* k_out;  // may be null
+  int64_t ko_st, ko_sh;
+  void* k_cache;  // null: no append
+  void* v_cache;
+  int64_t c_sblk, c_stok, c_sh;
+  const int64_t* slots;
+  int64_t num_blocks;
+  int block_size;
+  int64_t num_tokens;
+  int num_heads, num_kv_heads, head_dim;
+  int32_t* error;
 };
 
 // Message returned by ubx_last_error() on this host thread (set by any entry point).
@@ -91,6 +128,8 @@ cudaError_t launch_kv_append(const void* k_new, const void* v_new, int64_t n_sto
                              const int64_t* slots, int64_t num_tokens, int num_kv_heads, int row_bytes,
                              int block_size, int64_t num_blocks, int vec_bytes, int32_t* error_word,
                              cudaStream_t stream);
+
+cudaError_t launch_qk_norm_rope(int dtype, const PrepParams& p, cudaStream_t stream);
 
 cudaError_t launch_slot_mapping(const int32_t* block_table, int64_t bt_s_row, const int32_t* positions,
                                 int64_t* slot_mapping, int batch, int max_blocks, int block_size,

@@ -283,3 +283,221 @@ def slot_mapping(block_table: torch.Tensor, positions: torch.Tensor, block_size:
     _L.check(lib.ubx_slot_mapping(block_table.data_ptr(), block_table.stride(0), positions.data_ptr(),
                                   out.data_ptr(), B, block_table.shape[1], block_size, _stream(dev)), "slot_mapping")
     return out
+
+
+# ---------------------------------------------------------------------------
+# pre-attention: q/k RMSNorm + rotary embedding (+ KV append)
+# ---------------------------------------------------------------------------
+
+def rope_table(head_dim: int, num_positions: int, theta: float = 500000.0, device=None) -> torch.Tensor:
+    """(num_positions, head_dim // 2, 2) fp32 (cos, sin) table: torch.view_as_real of
+    the model's complex ``freqs_cis`` (precompute_freqs_cis, model.py:30-34; the
+    engine slices it at the token positions, engine.py:108 / :206). Built on the
+    CPU, like the model's buffer, then moved to ``device``."""
+    freqs = 1.0 / (theta ** (torch.arange(0, head_dim, 2).float() / head_dim))
+    ang = torch.outer(torch.arange(num_positions), freqs)
+    tab = torch.view_as_real(torch.polar(torch.ones_like(ang), ang)).contiguous()
+    return tab if device is None else tab.to(device)
+
+
+def _rope_args(rope: torch.Tensor, head_dim: int):
+    if rope.dtype == torch.complex64:
+        rope = torch.view_as_real(rope)
+    if rope.dtype != torch.float32 or rope.dim() != 3 or rope.shape[1:] != (head_dim // 2, 2):
+        raise ValueError(f"rope must be (P, {head_dim // 2}, 2) float32 (cos, sin) or (P, {head_dim // 2}) complex64")
+    if rope.stride(2) != 1 or rope.stride(1) != 2:
+        raise ValueError("rope rows must be contiguous")
+    return rope, rope.stride(0), rope.shape[0]
+
+
+def _norm_weight(w: torch.Tensor, dtype, head_dim: int, name: str) -> torch.Tensor:
+    if w.shape != (head_dim,) or w.dtype != dtype or not w.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous ({head_dim},) tensor in {dtype}")
+    return w
+
+
+def qk_norm_rope(q: torch.Tensor, k: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor,
+                 rope: torch.Tensor, positions: torch.Tensor, eps: float = 1e-6, *,
+                 v: Optional[torch.Tensor] = None, k_cache: Optional[torch.Tensor] = None,
+                 v_cache: Optional[torch.Tensor] = None, slot_mapping: Optional[torch.Tensor] = None,
+                 q_out: Optional[torch.Tensor] = None, k_out: Optional[torch.Tensor] = None,
+                 return_k: bool = True):
+    """RMSNorm (model.py:25-27) and rotary embedding (model.py:36-48) of the q and k
+    head rows of T tokens at ``positions``, as the engine's q_norm / k_norm /
+    apply_rotary_emb steps (engine.py:201-210 decode, :121-123 prefill), in one
+    launch. With ``k_cache``/``v_cache``/``slot_mapping`` (and ``v``) the rotated k
+    row and the raw v row of every token are also stored at its slot (the write_kv
+    loop, engine.py:213-215 / :126-128).
+
+    q: (T, H, D); k, v: (T, KVH, D); weights (D,) in the model dtype; rope as
+    ``rope_table``. Returns (q_out, k_out) -- k_out is None with ``return_k=False``.
+    """
+    dev = _require_cuda(q, k, q_weight, k_weight, rope, positions)
+    if q.dim() != 3 or k.dim() != 3 or q.shape[0] != k.shape[0] or q.shape[2] != k.shape[2]:
+        raise ValueError(f"expected q (T, H, D) and k (T, KVH, D); got {tuple(q.shape)}, {tuple(k.shape)}")
+    if q.dtype not in _DTYPES or k.dtype != q.dtype:
+        raise TypeError(f"q and k must share one of {list(_DTYPES)}")
+    T, H, D = q.shape
+    KVH = k.shape[1]
+    if q.stride(-1) != 1 or k.stride(-1) != 1:
+        raise ValueError("the head_dim dimension must be contiguous")
+    q_weight = _norm_weight(q_weight, q.dtype, D, "q_weight")
+    k_weight = _norm_weight(k_weight, q.dtype, D, "k_weight")
+    rope, rope_sp, rope_n = _rope_args(rope, D)
+    positions = _int32(positions, "positions").contiguous()
+    if positions.shape != (T,):
+        raise ValueError(f"positions must be ({T},)")
+    if q_out is None:
+        q_out = torch.empty((T, H, D), dtype=q.dtype, device=dev)
+    if return_k and k_out is None:
+        k_out = torch.empty((T, KVH, D), dtype=q.dtype, device=dev)
+    for name, t, shp in (("q_out", q_out, (T, H, D)), ("k_out", k_out, (T, KVH, D))):
+        if t is not None and (t.shape != shp or t.dtype != q.dtype or t.stride(-1) != 1):
+            raise ValueError(f"{name} must be {shp} in {q.dtype} with a contiguous last dimension")
+    append = k_cache is not None
+    cache_args = (None, None, 0, 0, 0, None, 0, 0)
+    if append:
+        if v is None or v_cache is None or slot_mapping is None:
+            raise ValueError("the append needs v, k_cache, v_cache and slot_mapping")
+        _require_cuda(q, v, k_cache, v_cache, slot_mapping)
+        if v.shape != k.shape or v.dtype != q.dtype or v.stride(-1) != 1:
+            raise ValueError("v must match k")
+        if k_cache.dim() != 4 or v_cache.shape != k_cache.shape or k_cache.shape[2:] != (KVH, D):
+            raise ValueError(f"caches must be (NB, bs, {KVH}, {D})")
+        if k_cache.dtype != q.dtype or v_cache.dtype != q.dtype or k_cache.stride() != v_cache.stride():
+            raise ValueError("caches must share q's dtype and have equal strides")
+        if slot_mapping.dtype != torch.int64:
+            slot_mapping = slot_mapping.to(torch.int64)
+        slot_mapping = slot_mapping.contiguous()
+        if slot_mapping.shape != (T,):
+            raise ValueError(f"slot_mapping must be ({T},)")
+        NB, bs = k_cache.shape[0], k_cache.shape[1]
+        cache_args = (k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0), k_cache.stride(1),
+                      k_cache.stride(2), slot_mapping.data_ptr(), NB, bs)
+    if T == 0:
+        return q_out, k_out
+    ws = workspace_for(dev)
+    lib = _L.load()
+    st = lib.ubx_qk_norm_rope_append(
+        q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0), k.stride(1),
+        v.data_ptr() if append else None, v.stride(0) if append else 0, v.stride(1) if append else 0,
+        q_weight.data_ptr(), k_weight.data_ptr(), float(eps), rope.data_ptr(), rope_sp, rope_n,
+        positions.data_ptr(), q_out.data_ptr(), q_out.stride(0), q_out.stride(1),
+        k_out.data_ptr() if k_out is not None else None, k_out.stride(0) if k_out is not None else 0,
+        k_out.stride(1) if k_out is not None else 0, *cache_args, T, H, KVH, D, _DTYPES[q.dtype],
+        ws.error_word_ptr(), _stream(dev))
+    _L.check(st, "qk_norm_rope_append")
+    return q_out, k_out
+
+
+def paged_decode_prep_attention(q_raw: torch.Tensor, k_raw: torch.Tensor, v_new: torch.Tensor,
+                                q_weight: torch.Tensor, k_weight: torch.Tensor, rope: torch.Tensor,
+                                k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
+                                context_lens: torch.Tensor, eps: float = 1e-6, scale: Optional[float] = None, *,
+                                out: Optional[torch.Tensor] = None, schedule: str = "auto",
+                                overlap_previous: bool = False) -> torch.Tensor:
+    """The attention block of one decode layer between the QKV projection and o_proj
+    (engine.py:201-224): q/k RMSNorm, rotary embedding at position
+    context_lens[b] - 1, the KV append and paged attention, in one launch for
+    bf16/f16. fp32 runs ``qk_norm_rope`` (with the append) and then
+    ``paged_attention``: two launches.
+
+    q_raw: (B, H, D) q projection; k_raw, v_new: (B, KVH, D) k and v projections.
+    """
+    dev = _require_cuda(q_raw, k_raw, v_new, q_weight, k_weight, rope, k_cache, v_cache, block_table, context_lens)
+    if q_raw.dim() != 3:
+        raise ValueError("q_raw must be (B, H, D)")
+    B, H, D = q_raw.shape
+    if q_raw.dtype == torch.float32:
+        ctx = _int32(context_lens, "context_lens")
+        positions = ctx - 1
+        slots = slot_mapping(block_table, positions, k_cache.shape[1])
+        q_rot, _ = qk_norm_rope(q_raw, k_raw, q_weight, k_weight, rope, positions, eps, v=v_new, k_cache=k_cache,
+                                v_cache=v_cache, slot_mapping=slots, return_k=False)
+        return paged_attention(q_rot, k_cache, v_cache, block_table, ctx, scale, out=out, schedule=schedule)
+    if q_raw.dtype not in _DTYPES:
+        raise TypeError(f"unsupported dtype {q_raw.dtype}")
+    if k_raw.shape != v_new.shape or k_raw.dim() != 3 or k_raw.shape[0] != B or k_raw.shape[2] != D:
+        raise ValueError(f"k_raw / v_new must be (B, KVH, {D})")
+    if k_raw.dtype != q_raw.dtype or v_new.dtype != q_raw.dtype:
+        raise TypeError("k_raw / v_new must have q_raw's dtype")
+    if k_raw.stride() != v_new.stride() or k_raw.stride(-1) != 1 or q_raw.stride(-1) != 1:
+        raise ValueError("k_raw and v_new need equal strides; every last dimension must be contiguous")
+    if k_cache.dim() != 4 or v_cache.shape != k_cache.shape or k_cache.stride() != v_cache.stride():
+        raise ValueError("caches must be (NB, bs, KVH, D) with equal strides")
+    if k_cache.dtype != q_raw.dtype or v_cache.dtype != q_raw.dtype:
+        raise TypeError("caches must have q_raw's dtype")
+    NB, bs, KVH, D2 = k_cache.shape
+    if D2 != D or k_raw.shape[1] != KVH:
+        raise ValueError("head shape mismatch between projections and caches")
+    q_weight = _norm_weight(q_weight, q_raw.dtype, D, "q_weight")
+    k_weight = _norm_weight(k_weight, q_raw.dtype, D, "k_weight")
+    rope, rope_sp, rope_n = _rope_args(rope, D)
+    block_table = _int32(block_table, "block_table")
+    context_lens = _int32(context_lens, "context_lens")
+    if block_table.dim() != 2 or block_table.shape[0] != B or block_table.stride(-1) != 1:
+        raise ValueError("block_table must be (B, max_blocks) with contiguous rows")
+    if context_lens.shape != (B,) or not context_lens.is_contiguous():
+        raise ValueError(f"context_lens must be a contiguous ({B},) tensor")
+    if out is None:
+        out = torch.empty((B, H, D), dtype=q_raw.dtype, device=dev)
+    elif out.shape != (B, H, D) or out.dtype != q_raw.dtype or out.stride(-1) != 1:
+        raise ValueError("out must be (B, H, D) in q's dtype with a contiguous last dimension")
+    if B == 0:
+        return out
+    if scale is None:
+        scale = D ** -0.5
+    max_blocks = block_table.shape[1]
+    buf = workspace_for(dev).ensure(B, H, D, max_blocks, 0)
+    lib = _L.load()
+    st = lib.ubx_paged_decode_prep_attention(
+        q_raw.data_ptr(), q_raw.stride(0), q_raw.stride(1), k_raw.data_ptr(), v_new.data_ptr(), k_raw.stride(0),
+        k_raw.stride(1), q_weight.data_ptr(), k_weight.data_ptr(), float(eps), rope.data_ptr(), rope_sp, rope_n,
+        k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0), k_cache.stride(1), k_cache.stride(2),
+        block_table.data_ptr(), block_table.stride(0), context_lens.data_ptr(), out.data_ptr(), out.stride(0),
+        out.stride(1), B, H, KVH, D, bs, NB, max_blocks, float(scale), _DTYPES[q_raw.dtype], _SCHEDULES[schedule],
+        0, _L.FLAG_OVERLAP_PREVIOUS if overlap_previous else 0, buf.data_ptr(), buf.numel(), _stream(dev))
+    _L.check(st, "paged_decode_prep_attention")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# prefill: the chunk's KV rows written in one launch
+# ---------------------------------------------------------------------------
+
+def prefill_slots(block_table_row: torch.Tensor, start_pos: int, num_tokens: int, block_size: int) -> torch.Tensor:
+    """Slots of positions start_pos .. start_pos + num_tokens - 1 of one sequence
+    (kvcache.py:338-339 for every token of a prefill chunk)."""
+    dev = _require_cuda(block_table_row)
+    row = _int32(block_table_row, "block_table_row").contiguous()
+    if row.dim() != 1:
+        raise ValueError("block_table_row must be 1-D")
+    positions = torch.arange(start_pos, start_pos + num_tokens, dtype=torch.int32, device=dev)
+    return slot_mapping(row.unsqueeze(0).expand(num_tokens, -1), positions, block_size)
+
+
+def prefill_kv_write(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                     block_table_row: torch.Tensor, start_pos: int) -> torch.Tensor:
+    """Write the K/V rows of a prefill chunk (T tokens of one sequence starting at
+    ``start_pos``) into the pool: the per-token write_kv loop of prefill_step
+    (engine.py:126-128) as one slot computation and one append launch. Returns the
+    slots (T,) int64."""
+    if k.dim() != 3:
+        raise ValueError("k must be (T, KVH, D)")
+    slots = prefill_slots(block_table_row, start_pos, k.shape[0], k_cache.shape[1])
+    kv_append(k, v, k_cache, v_cache, slots)
+    return slots
+
+
+def prefill_prep(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor,
+                 rope: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table_row: torch.Tensor,
+                 start_pos: int, eps: float = 1e-6):
+    """A prefill chunk's q_norm / k_norm / rotary embedding at positions
+    start_pos.. and its KV write (engine.py:121-128) in one launch (plus the slot
+    computation). Returns (q_rot, k_rot) for the chunk's own attention."""
+    T = q.shape[0]
+    dev = _require_cuda(q)
+    positions = torch.arange(start_pos, start_pos + T, dtype=torch.int32, device=dev)
+    slots = prefill_slots(block_table_row, start_pos, T, k_cache.shape[1])
+    return qk_norm_rope(q, k, q_weight, k_weight, rope, positions, eps, v=v, k_cache=k_cache, v_cache=v_cache,
+                        slot_mapping=slots)

@@ -235,6 +235,27 @@ def materialize_host(lay: Layout, seed: int, dtype: str = "float32", value_scale
     )
 
 
+def materialize_prep_host(seed: int, num_tokens: int, num_heads: int, num_kv_heads: int, head_dim: int,
+                          dtype: str = "bfloat16", value_scale: float = 1.0):
+    """Inputs of the pre-attention step from the portable generator: the q, k and v
+    projections of ``num_tokens`` tokens and the q_norm / k_norm weights
+    (1 + 0.1 N(0, 1), trained RMSNorm weights sit near 1).
+
+    Returns dict(q_raw (T, H, D), k_raw (T, KVH, D), v_new (T, KVH, D), q_weight (D,), k_weight (D,)).
+    """
+    import torch
+    td = _torch_dtype(dtype)
+
+    def gen(stream, shape, scale=value_scale, offset=0.0):
+        n = int(np.prod(shape))
+        a = (portable_normal(seed, stream, n) * scale + offset).astype(np.float32).reshape(shape)
+        return torch.from_numpy(a).to(td)
+
+    T, H, KVH, D = num_tokens, num_heads, num_kv_heads, head_dim
+    return dict(q_raw=gen(20, (T, H, D)), k_raw=gen(21, (T, KVH, D)), v_new=gen(22, (T, KVH, D)),
+                q_weight=gen(23, (D,), 0.1, 1.0), k_weight=gen(24, (D,), 0.1, 1.0))
+
+
 def materialize_device(lay: Layout, seed: int, dtype: str, value_scale: float, num_layers: int,
                        device="cuda"):
     """Device tensors for a multi-layer decode step drawn with torch's generator.
