@@ -56,6 +56,8 @@ def parse():
                     help="KV append as its own launch before attention (default: fused into one launch)")
     ap.add_argument("--no-overlap", dest="overlap", action="store_false",
                     help="no programmatic dependent launch between consecutive layer-calls")
+    ap.add_argument("--op", choices=["decode", "handoff"], default="decode",
+                    help="decode: the decode layer-call (default); handoff: KV page hand-off between workers")
     ap.add_argument("--prep", action="store_true",
                     help="layer-call = q/k RMSNorm + rotary embedding + KV append + attention in one launch "
                          "(the attention block between the QKV projection and o_proj)")
@@ -176,8 +178,186 @@ def cpu_layer_call(oracle, host):
     return st
 
 
+HANDOFF_METRIC = "KV hand-off GB/s of page payload (prefill pool -> decode pool)"
+
+
+def bench_handoff(args):
+    """One step = hand one finished 2048-token prompt of the 760M model (24 layers,
+    128 pages of 16 x 8 x 112 bf16, K and V: 176 MB) from a prefill worker's pool
+    to a decode worker's pool, at other page ids (worker.py:175-183 -> :217-223).
+    N=1: both pools on one GPU, one page-copy kernel (HBM read + write).
+    N>=2: ranks pair up (2k -> 2k+1), the decode worker's pool is mapped into the
+    prefill worker over CUDA IPC and written over NVLink by one kernel.
+    e2e: the reference's host path through this package's drop-ins,
+    serialize_blocks -> host bytes -> deserialize_blocks."""
+    import torch
+    import torch.distributed as dist
+    from __graft_entry__ import load_package
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    pkg = load_package()
+    ho = pkg.handoff
+    L, KVH, D, bs, npg, NB = 24, 8, 112, 16, 128, 1536
+    payload = L * 2 * npg * bs * KVH * D * 2
+    config = {"workload": "handoff_760m_prompt2048", "layers": L, "pages": npg, "page_bytes": bs * KVH * D * 2,
+              "pool_pages": NB, "dtype": "bf16",
+              "l2": "inputs > L2: 176 MB payload per step, 8 rotating page sets",
+              "parallelism": "single GPU" if world == 1 else f"{world // 2} prefill->decode pair(s) over NVLink"}
+
+    def pool(seed):
+        g = torch.Generator(device="cuda")
+        g.manual_seed(seed)
+        t = torch.empty((L, 2, NB, bs, KVH, D), dtype=torch.bfloat16, device="cuda")
+        for l in range(L):
+            t[l].copy_(torch.randn((2, NB, bs, KVH, D), generator=g, device="cuda"))
+        return t
+
+    def page_sets(seed):
+        g = torch.Generator(device="cuda")
+        g.manual_seed(seed)
+        return [torch.randperm(NB, generator=g, device="cuda")[:npg].to(torch.int32) for _ in range(8)]
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        from oracle import oracle
+        src = torch.randn((L, 2, 256, bs, KVH, D)).to(torch.bfloat16)
+        dst = torch.zeros_like(src)
+        sp = list(range(0, 256, 2))
+        dp = list(range(1, 256, 2))
+        times = []
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            oracle.scatter_pages(oracle.gather_pages(src, sp), dst, dp)
+            if i >= args.warmup:
+                times.append(time.perf_counter() - t0)
+        v = payload * len(times) / sum(times) / 1e9
+        print(json.dumps({
+            "metric": HANDOFF_METRIC, "value": round(v, 3), "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(times) / len(times),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": config,
+            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+                             "sample": "one prompt's pages per step: numpy gather + scatter (the reference's "
+                                       "serialize_blocks / deserialize_blocks without the socket)"},
+            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    sender = world == 1 or (rank % 2 == 0 and rank + 1 < world)
+    receiver = world > 1 and rank % 2 == 1
+    src = pool(100 + rank) if sender else None
+    dst = pool(200 + rank) if (receiver or world == 1) else None
+    sps, dps = page_sets(300 + rank), page_sets(400 + rank)
+    mapping = None
+    if world > 1:
+        tokens = [None] * world
+        dist.all_gather_object(tokens, ho.ipc_export(dst) if receiver else None)
+        if sender:
+            mapping = ho.ipc_import(tokens[rank + 1], device)
+
+    def step(k):
+        if not sender:
+            return
+        if mapping is None:
+            ho.transfer_pages(src, sps[k % 8], dst, dps[k % 8])
+        else:
+            ho.transfer_pages_to_ipc(src, sps[k % 8], mapping, (L, 2, NB, bs, KVH, D), dps[k % 8])
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+
+    for k in range(max(3, args.warmup)):
+        step(k)
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        ev0.record()
+        for k in range(args.steps):
+            step(k)
+        ev1.record()
+        torch.cuda.synchronize()
+    barrier()
+    ms = ev0.elapsed_time(ev1) if sender else 0.0
+    ms_max, pairs = ms, 1
+    if world > 1:
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max, pairs = float(t.item()), world // 2
+    value = pairs * payload * args.steps / (ms_max / 1e3) / 1e9
+    pkg.check_device_errors(device)
+
+    # e2e: the reference's host path (device gather -> host bytes -> device scatter)
+    e2e = None
+    if world == 1:
+        sp_l = [sps[0].tolist(), sps[1].tolist()]
+        dp_l = [dps[0].tolist(), dps[1].tolist()]
+        for k in range(2):
+            ho.deserialize_blocks(dst, ho.serialize_blocks(src, sp_l[k]), dp_l[k])
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        n_e2e = max(3, args.steps // 4)
+        for k in range(n_e2e):
+            ho.deserialize_blocks(dst, ho.serialize_blocks(src, sp_l[k % 2]), dp_l[k % 2])
+        e1.record()
+        torch.cuda.synchronize()
+        e_ms = e0.elapsed_time(e1) / n_e2e
+        e2e = {"value": round(payload / (e_ms / 1e3) / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": payload + 64,
+               "d2h_bytes_per_step": payload + 64, "ms_per_step": round(e_ms, 4),
+               "path": "serialize_blocks -> host bytes -> deserialize_blocks (checksum verified)"}
+    if world > 1:
+        if mapping is not None:
+            mapping.close()
+        dist.barrier()
+
+    peak, kind = peaks()
+    per_step_ms = ms_max / args.steps
+    line = {"metric": HANDOFF_METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step_ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": config, "gpu_launches": args.steps * (1 if sender else 0),
+            "clocks": clocks.summary(), "e2e": e2e}
+    if world == 1:
+        ach = 2 * payload / (per_step_ms / 1e3) / 1e9
+        line["roofline"] = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                            "frac": round(ach / peak, 4), "traffic": None, "kernel": "kv_pages_copy_kernel",
+                            "algorithmic_bytes_per_launch": 2 * payload, "avg_launch_us": round(per_step_ms * 1e3, 2),
+                            "peak_source": f"{kind} (MEASURED_PEAKS.json hbm_gbs, read + write bytes)"}
+    else:
+        ach = payload / (per_step_ms / 1e3) / 1e9
+        line["roofline"] = {"bound": "nvlink", "achieved": round(ach, 1), "peak": 770.0, "unit": "GB/s",
+                            "frac": round(ach / 770.0, 4), "traffic": None, "kernel": "kv_pages_copy_kernel",
+                            "algorithmic_bytes_per_launch": payload, "avg_launch_us": round(per_step_ms * 1e3, 2),
+                            "peak_source": "measured peer copy per direction on this pool (770 GB/s)"}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle
+        hs = src[:, :, :256].cpu()
+        hd = torch.zeros_like(hs)
+        t0, n = time.perf_counter(), 0
+        while time.perf_counter() - t0 < min(args.cpu_seconds, 5.0) or n == 0:
+            oracle.scatter_pages(oracle.gather_pages(hs, list(range(0, 256, 2))), hd, list(range(1, 256, 2)))
+            n += 1
+        el = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": round(payload * n / el / 1e9, 3), "unit": "GB/s", "cores": 1,
+                                "kind": "port", "sample": f"{n} prompt(s): numpy gather + scatter of 128 pages x 24 "
+                                                          f"layers, {el:.1f} s"}
+    if rank == 0:
+        print(json.dumps(line))
+
+
 def main():
     args = parse()
+    if args.op == "handoff":
+        return bench_handoff(args)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -221,6 +221,85 @@ int ubx_paged_decode_prep_attention(const void* q_raw, int64_t q_s_b, int64_t q_
                                     void* stream);
 
 /*
+ * KV hand-off between a prefill worker and a decode worker.
+ * Replaces: KVPool.serialize_blocks / deserialize_blocks
+ * (unbox_platform/infer/kvcache.py:268-277), used at worker.py:175-183 (prefill
+ * side) and :217-223 (decode side), which copy the pages through host memory,
+ * serialise only fp32 pools (bf16 raises in numpy) and decode every payload as
+ * float32. Here pages move on the device, the wire message carries a fixed
+ * 64-byte header with the payload's dtype and geometry, and a pool-to-pool copy
+ * can write straight into another GPU's pool over NVLink.
+ *
+ * Wire message = ubx_kv_wire_header followed by the payload: the pages in the
+ * reference's byte order, (num_layers, 2 [K, V], num_pages, block_size,
+ * num_kv_heads, head_dim) in the pool dtype. All fields little-endian.
+ */
+#define UBX_KV_WIRE_MAGIC "UBXKVPG1"
+#define UBX_KV_WIRE_VERSION 1
+typedef struct ubx_kv_wire_header {
+  char magic[8];          /* UBX_KV_WIRE_MAGIC, not NUL-terminated */
+  uint32_t version;       /* UBX_KV_WIRE_VERSION */
+  uint32_t header_bytes;  /* 64 */
+  uint32_t dtype;         /* UBX_DTYPE_* of the payload */
+  uint32_t num_layers;
+  uint32_t num_kv_heads;
+  uint32_t head_dim;
+  uint32_t block_size;
+  uint32_t num_pages;
+  uint64_t payload_bytes; /* num_layers * 2 * num_pages * block_size * num_kv_heads * head_dim * element bytes */
+  uint64_t checksum;      /* sum over the payload's 32-bit words p[i] of p[i] * (2i + 1), mod 2^64 */
+  uint8_t reserved[8];    /* zero */
+} ubx_kv_wire_header;
+
+/* Fill a header (host memory). */
+int ubx_kv_wire_header_init(ubx_kv_wire_header* header, int dtype, int num_layers, int num_kv_heads, int head_dim,
+                            int block_size, int num_pages, uint64_t checksum);
+/*
+ * Check a received header (host memory) against the receiving pool's geometry
+ * and the payload size that arrived: UBX_ERR_INVALID_ARGUMENT for a bad magic,
+ * version or size, UBX_ERR_UNSUPPORTED for a dtype or geometry other than the
+ * pool's (no conversion is done).
+ */
+int ubx_kv_wire_header_check(const ubx_kv_wire_header* header, int dtype, int num_layers, int num_kv_heads,
+                             int head_dim, int block_size, uint64_t payload_bytes);
+
+/*
+ * Copy num_pages pages of num_layers layers (K and V) from one page layout to
+ * another, on `stream` of the current device. Each side is either a pool --
+ * base of KVPool.data, (num_layers, 2, num_blocks, block_size, num_kv_heads,
+ * head_dim), element strides (s_layer, s_kv, s_block), page ids `pages` (int32
+ * device array, entry i is the i-th page to copy) -- or, with pages == NULL, a
+ * packed wire payload (page i at position i, strides (2 * num_pages *
+ * page_elems, num_pages * page_elems, page_elems)).
+ *   pool -> packed:  serialize (checksum: device uint64 that receives the
+ *                    payload checksum of the header, or NULL)
+ *   packed -> pool:  deserialize into the receiver's own page ids
+ *   pool -> pool:    direct hand-off; dst may be another GPU's memory mapped
+ *                    into this process (ubx_enable_peer_access, ubx_ipc_open_handle)
+ * page_elems = block_size * num_kv_heads * head_dim; every base and stride a
+ * multiple of 16 bytes. A page id outside [0, num_blocks) of its side skips
+ * that page and sets UBX_DEVERR_BAD_PAGE in error_word (may be NULL).
+ */
+int ubx_kv_pages_copy(const void* src, int64_t src_s_layer, int64_t src_s_kv, int64_t src_s_block,
+                      const int32_t* src_pages, int64_t src_num_blocks, void* dst, int64_t dst_s_layer,
+                      int64_t dst_s_kv, int64_t dst_s_block, const int32_t* dst_pages, int64_t dst_num_blocks,
+                      int num_layers, int num_pages, int64_t page_elems, int dtype, uint64_t* checksum,
+                      int32_t* error_word, void* stream);
+
+/* Let the current device read and write `peer_device`'s memory (no-op if already enabled). */
+int ubx_enable_peer_access(int peer_device);
+/*
+ * CUDA IPC of a device buffer for a hand-off between worker processes:
+ * ubx_ipc_get_handle writes the 64-byte handle of the allocation holding
+ * dev_ptr and dev_ptr's offset inside it; ubx_ipc_open_handle maps it in
+ * another process (peer access enabled) and returns the allocation's base
+ * there (add the offset); ubx_ipc_close_handle unmaps it.
+ */
+int ubx_ipc_get_handle(const void* dev_ptr, void* handle_out, uint64_t* offset_out);
+int ubx_ipc_open_handle(const void* handle, void** base_out);
+int ubx_ipc_close_handle(void* base);
+
+/*
  * Allocation-free variant of ubx_paged_decode_attention. No counterpart in the
  * reference: it exists for callers that cannot allocate device memory -- an
  * engine that gives all free HBM to its own KV pool at start-up and owns every

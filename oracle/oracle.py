@@ -12,6 +12,8 @@ Each wrapper names the reference function it restates:
   rms_norm / rotary / qk_norm_rope -> unbox_platform/model/model.py:19-48 as the
                              engine applies them (engine.py:201-210, :121-123);
                              numpy, elementwise, no C library needed
+  gather_pages / scatter_pages / payload_checksum -> KVPool.serialize_blocks /
+                             deserialize_blocks (kvcache.py:268-277), numpy
 """
 from __future__ import annotations
 
@@ -219,3 +221,36 @@ def qk_norm_rope(q, k, q_weight, k_weight, rope, positions, eps: float = 1e-6):
     q_out = rotary(rms_norm(qf, qw, eps, code), cs, code)
     k_out = rotary(rms_norm(kf, kw, eps, code), cs, code)
     return q_out, k_out, bad
+
+
+# ---------------------------------------------------------------------------
+# KV page hand-off (numpy)
+# ---------------------------------------------------------------------------
+
+def _pool_np(pool):
+    """(L, 2, NB, bs, KVH, D) pool as a numpy array of raw elements (bf16 as uint16)."""
+    return _np(pool)
+
+
+def gather_pages(pool, pages) -> bytes:
+    """The payload of KVPool.serialize_blocks (kvcache.py:268-271):
+    data[:, :, pages] in C order, as bytes."""
+    a = _pool_np(pool)
+    return np.ascontiguousarray(a[:, :, np.asarray(pages, dtype=np.int64)]).tobytes()
+
+
+def scatter_pages(payload: bytes, pool, pages) -> None:
+    """KVPool.deserialize_blocks (kvcache.py:273-277) with the payload read in the
+    pool's own dtype: pool[:, :, pages] = payload (in place)."""
+    a = _pool_np(pool)
+    L, two, NB, bs, KVH, D = a.shape
+    idx = np.asarray(pages, dtype=np.int64)
+    a[:, :, idx] = np.frombuffer(payload, dtype=a.dtype).reshape(L, 2, len(idx), bs, KVH, D)
+
+
+def payload_checksum(payload: bytes) -> int:
+    """Sum over the payload's 32-bit little-endian words p[i] of p[i] * (2i + 1), mod 2^64."""
+    w = np.frombuffer(payload, dtype="<u4").astype(np.uint64)
+    i = np.arange(w.shape[0], dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        return int(np.sum(w * (2 * i + 1), dtype=np.uint64))

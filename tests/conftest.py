@@ -42,8 +42,9 @@ def sha(t) -> str:
 
 
 _ALL_GOLDEN = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
-GOLDEN_NAMES = [n for n in _ALL_GOLDEN if not n.startswith("prep_")]   # append + attention cases
+GOLDEN_NAMES = [n for n in _ALL_GOLDEN if not n.startswith(("prep_", "handoff_"))]  # append + attention
 PREP_GOLDEN_NAMES = [n for n in _ALL_GOLDEN if n.startswith("prep_")]  # norm + rotary (+ append, attention)
+HANDOFF_GOLDEN_NAMES = [n for n in _ALL_GOLDEN if n.startswith("handoff_")]  # serialize / deserialize
 
 
 def load_golden(name: str):

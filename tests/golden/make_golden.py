@@ -229,6 +229,34 @@ def run_prep_case(ref_root, wl, name, kind, spec, dtype, seed):
     return rec
 
 
+# KV hand-off case: the reference's KVPool.serialize_blocks / deserialize_blocks
+# (unbox_platform/infer/kvcache.py:268-277) on an fp32 pool, the only dtype its
+# float32 payload decoding round-trips.
+HANDOFF_CASES = {
+    # name: (num_layers, num_blocks, num_kv_heads, head_dim, src pages, dst pages, seed)
+    "handoff_fp32": (3, 12, 8, 112, [5, 0, 9, 3, 11], [7, 2, 11, 4, 0], 8),
+}
+
+
+def run_handoff_case(ref_root, wl, name, L, NB, KVH, D, src_pages, dst_pages, seed):
+    import torch
+    sys.path.insert(0, ref_root)
+    from unbox_platform.infer.kvcache import KVPool
+
+    src = KVPool(L, KVH, D, NB, 16, torch.device("cpu"), torch.float32)
+    src.data.copy_(wl.materialize_pool_host(seed, L, NB, 16, KVH, D, "float32"))
+    payload = src.serialize_blocks(src_pages)
+    dst = KVPool(L, KVH, D, NB, 16, torch.device("cpu"), torch.float32)   # a fresh pool is zeros
+    dst.deserialize_blocks(payload, dst_pages, (L, 2, len(dst_pages), 16, KVH, D))
+    return dict(
+        name=np.array(name), seed=np.array(seed), num_layers=np.array(L), num_blocks=np.array(NB),
+        num_kv_heads=np.array(KVH), head_dim=np.array(D), block_size=np.array(16), dtype=np.array("float32"),
+        src_pages=np.array(src_pages, dtype=np.int32), dst_pages=np.array(dst_pages, dtype=np.int32),
+        sha_src_pool=np.array(sha(src.data)), payload_bytes=np.array(len(payload)),
+        sha_payload=np.array(hashlib.sha256(payload).hexdigest()), sha_dst_after=np.array(sha(dst.data)),
+    )
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -262,6 +290,13 @@ def main():
         path = os.path.join(HERE, f"{name}.npz")
         np.savez_compressed(path, **rec)
         print(f"{name}: B={lay.batch} sum_ctx={lay.kv_tokens()} ref {el:.2f}s -> {os.path.basename(path)}")
+    for name, (L, NB, KVH, D, sp, dp, seed) in HANDOFF_CASES.items():
+        if args.only and name != args.only:
+            continue
+        rec = run_handoff_case(args.reference, wl, name, L, NB, KVH, D, sp, dp, seed)
+        path = os.path.join(HERE, f"{name}.npz")
+        np.savez_compressed(path, **rec)
+        print(f"{name}: {int(rec['payload_bytes'])} payload bytes -> {os.path.basename(path)}")
     for name, (kind, spec, dtype, seed) in PREP_CASES.items():
         if args.only and name != args.only:
             continue

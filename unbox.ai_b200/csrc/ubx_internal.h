@@ -131,6 +131,24 @@ cudaError_t launch_kv_append(const void* k_new, const void* v_new, int64_t n_sto
 
 cudaError_t launch_qk_norm_rope(int dtype, const PrepParams& p, cudaStream_t stream);
 
+// Page copy between two page layouts (kv_transfer.cu); byte strides.
+struct KvCopyParams {
+  const void* src;
+  int64_t src_s_layer, src_s_kv, src_s_block;
+  const int32_t* src_pages;  // null: packed (page i at position i)
+  int64_t src_num_blocks;
+  void* dst;
+  int64_t dst_s_layer, dst_s_kv, dst_s_block;
+  const int32_t* dst_pages;
+  int64_t dst_num_blocks;
+  int num_layers, num_pages;
+  int64_t page_bytes;
+  unsigned long long* checksum;  // null: none
+  int32_t* error;
+};
+
+cudaError_t launch_kv_pages_copy(const KvCopyParams& p, cudaStream_t stream);
+
 cudaError_t launch_slot_mapping(const int32_t* block_table, int64_t bt_s_row, const int32_t* positions,
                                 int64_t* slot_mapping, int batch, int max_blocks, int block_size,
                                 cudaStream_t stream);

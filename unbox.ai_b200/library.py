@@ -46,10 +46,31 @@ SIGNATURES = {
                                                _i32, _i32, _i32, _i64, _i32, _f32, _i32, _i32, _i32, _i32, _vp, _sz,
                                                _vp]),
     "ubx_read_device_error": (_i32, [_vp, ctypes.POINTER(ctypes.c_int32), _i32, _vp]),
+    "ubx_kv_wire_header_init": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, _i32, ctypes.c_uint64]),
+    "ubx_kv_wire_header_check": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, ctypes.c_uint64]),
+    "ubx_kv_pages_copy": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i32, _i32,
+                                 _i64, _i32, _vp, _vp, _vp]),
+    "ubx_enable_peer_access": (_i32, [_i32]),
+    "ubx_ipc_get_handle": (_i32, [_vp, _vp, ctypes.POINTER(ctypes.c_uint64)]),
+    "ubx_ipc_open_handle": (_i32, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
+    "ubx_ipc_close_handle": (_i32, [_vp]),
     "ubx_paged_decode_attention_noalloc": (_i32, [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp,
                                                   _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i64, _i32, _f32, _i32,
                                                   _i32, _i32, _vp, _vp]),
 }
+
+
+
+class KVWireHeader(ctypes.Structure):
+    """ubx_kv_wire_header: the 64-byte header of a KV page message (little-endian)."""
+    _fields_ = [("magic", ctypes.c_char * 8), ("version", ctypes.c_uint32), ("header_bytes", ctypes.c_uint32),
+                ("dtype", ctypes.c_uint32), ("num_layers", ctypes.c_uint32), ("num_kv_heads", ctypes.c_uint32),
+                ("head_dim", ctypes.c_uint32), ("block_size", ctypes.c_uint32), ("num_pages", ctypes.c_uint32),
+                ("payload_bytes", ctypes.c_uint64), ("checksum", ctypes.c_uint64),
+                ("reserved", ctypes.c_uint8 * 8)]
+
+
+assert ctypes.sizeof(KVWireHeader) == 64
 
 _lib = None
 _lock = threading.Lock()

@@ -256,6 +256,16 @@ def materialize_prep_host(seed: int, num_tokens: int, num_heads: int, num_kv_hea
                 q_weight=gen(23, (D,), 0.1, 1.0), k_weight=gen(24, (D,), 0.1, 1.0))
 
 
+def materialize_pool_host(seed: int, num_layers: int, num_blocks: int, block_size: int, num_kv_heads: int,
+                          head_dim: int, dtype: str = "float32", stream: int = 30):
+    """A whole KVPool.data tensor (L, 2, NB, bs, KVH, D) (kvcache.py:248-251) from
+    the portable generator."""
+    import torch
+    shape = (num_layers, 2, num_blocks, block_size, num_kv_heads, head_dim)
+    a = portable_normal(seed, stream, int(np.prod(shape))).astype(np.float32).reshape(shape)
+    return torch.from_numpy(a).to(_torch_dtype(dtype))
+
+
 def materialize_device(lay: Layout, seed: int, dtype: str, value_scale: float, num_layers: int,
                        device="cuda"):
     """Device tensors for a multi-layer decode step drawn with torch's generator.
