@@ -27,6 +27,7 @@ on torch's current stream, and raises without the CUDA library (no fallback).
 from __future__ import annotations
 
 import ctypes
+import warnings
 from typing import Optional, Sequence, Union
 
 import torch
@@ -129,16 +130,21 @@ def _u64(t: torch.Tensor) -> int:
     return int(t.item()) & (2 ** 64 - 1)
 
 
-def serialize_blocks(pool: torch.Tensor, block_indices: Sequence[int]) -> bytes:
-    """KVPool.serialize_blocks (kvcache.py:268-271): header + the pages' bytes.
-    Synchronises the stream (the message is host bytes)."""
+def serialize_blocks(pool: torch.Tensor, block_indices: Sequence[int]) -> bytearray:
+    """KVPool.serialize_blocks (kvcache.py:268-271): header + the pages' bytes, as
+    one bytes-like message that the device-to-host copy writes in place.
+    Synchronises the stream (the message is host memory)."""
     dev = _require_cuda(pool)
     ck = torch.zeros(1, dtype=torch.int64, device=dev)
     payload = pack_pages(pool, block_indices, checksum=ck)
-    host = torch.empty(payload.numel() * payload.element_size(), dtype=torch.uint8, pin_memory=True)
-    host.copy_(payload.view(-1).view(torch.uint8), non_blocking=True)
+    nbytes = payload.numel() * payload.element_size()
+    msg = bytearray(HEADER_BYTES + nbytes)
+    if nbytes:
+        body = torch.frombuffer(msg, dtype=torch.uint8, offset=HEADER_BYTES, count=nbytes)
+        body.copy_(payload.view(-1).view(torch.uint8))
     torch.cuda.current_stream(dev).synchronize()
-    return make_header(pool, len(block_indices), _u64(ck)) + host.numpy().tobytes()
+    msg[:HEADER_BYTES] = make_header(pool, len(block_indices), _u64(ck))
+    return msg
 
 
 def deserialize_blocks(pool: torch.Tensor, data: Union[bytes, bytearray, memoryview],
@@ -154,8 +160,12 @@ def deserialize_blocks(pool: torch.Tensor, data: Union[bytes, bytearray, memoryv
     if h.num_pages != len(block_indices):
         raise ValueError(f"message holds {h.num_pages} pages, {len(block_indices)} destinations given")
     L, NB, bs, KVH, D = _geometry(pool)
-    host = torch.frombuffer(bytearray(body), dtype=torch.uint8) if len(body) else torch.empty(0, dtype=torch.uint8)
-    staged = host.to(dev, non_blocking=False)
+    staged = torch.empty(len(body), dtype=torch.uint8, device=dev)
+    if len(body):
+        with warnings.catch_warnings():  # read-only buffers (bytes) are only read here
+            warnings.simplefilter("ignore", UserWarning)
+            host = torch.frombuffer(data, dtype=torch.uint8, offset=HEADER_BYTES, count=len(body))
+        staged.copy_(host)
     payload = staged.view(pool.dtype).view(L, 2, h.num_pages, bs, KVH, D)
     ck = torch.zeros(1, dtype=torch.int64, device=dev) if verify else None
     unpack_pages(payload, pool, block_indices, checksum=ck)
