@@ -352,6 +352,9 @@ def bench_handoff(args):
                                                           f"layers, {el:.1f} s"}
     if rank == 0:
         print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def main():

@@ -114,6 +114,8 @@ int ubx_kv_pages_copy(const void* src, int64_t src_s_layer, int64_t src_s_kv, in
       (!dst_pages && (dst_s_block != page_elems || dst_s_kv != (int64_t)num_pages * page_elems ||
                       dst_s_layer != 2 * (int64_t)num_pages * page_elems)))
     return hfail(UBX_ERR_INVALID_ARGUMENT, "a packed side must have the wire payload's strides");
+  if ((int64_t)num_layers * 2 * num_pages * (pb / 16) >= ((int64_t)1 << 31))
+    return hfail(UBX_ERR_UNSUPPORTED, "one call copies less than 32 GiB; split the pages over several calls");
   ubx::KvCopyParams p;
   p.src = src;
   p.src_s_layer = src_s_layer * es;

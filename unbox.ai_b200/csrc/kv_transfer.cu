@@ -14,8 +14,7 @@
 // The packed payload has the reference's byte order: (layer, K|V, page, row).
 //
 // A page unit (one layer, K or V, one page) is page_bytes contiguous bytes in
-// both layouts; CTAs take units in a grid-stride loop and move them as 16-byte
-// vectors, four in flight per thread.
+// both layouts.
 #include "ubx_common.cuh"
 #include "ubx_internal.h"
 
@@ -49,41 +48,50 @@ __device__ __forceinline__ uint64_t vec_checksum(const uint4& v, uint64_t w) {
   return (uint64_t)v.x * a + (uint64_t)v.y * (a + 2) + (uint64_t)v.z * (a + 4) + (uint64_t)v.w * (a + 6);
 }
 
+// The copy is one flat array of 16-byte vectors in payload order (unit u =
+// (layer, K|V, page) holds vectors [u * vpu, (u + 1) * vpu)); every thread takes
+// the same share of it, grid-stride, so no CTA is left with an extra page at the
+// end. Four vectors per thread are in flight.
 template <bool CHECKSUM>
 __global__ void __launch_bounds__(kCopyThreads) kv_pages_copy_kernel(const PageSide src, const PageSide dst,
                                                                     int num_layers, int num_pages,
                                                                     int64_t page_bytes, unsigned long long* checksum,
                                                                     int32_t* error) {
-  const int64_t units = (int64_t)num_layers * 2 * num_pages;
-  const int64_t vecs = page_bytes / 16;
+  // 32-bit index math: the host keeps one call's vectors below 2^31
+  const uint32_t vpu = (uint32_t)(page_bytes / 16);
+  const uint32_t np = (uint32_t)num_pages;
+  const uint32_t total = (uint32_t)num_layers * 2u * np * vpu;
+  const uint32_t stride = gridDim.x * kCopyThreads;
   uint64_t sum = 0;
-  for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
-    const int i = (int)(u % num_pages);
-    const int c = (int)((u / num_pages) & 1);
-    const int l = (int)(u / (2 * (int64_t)num_pages));
-    bool ok = true;
-    const uint4* s = reinterpret_cast<const uint4*>(unit_addr(src, l, c, i, ok));
-    uint4* d = reinterpret_cast<uint4*>(const_cast<uint8_t*>(unit_addr(dst, l, c, i, ok)));
-    if (!ok) {
-      if (threadIdx.x == 0) set_error(error, kErrBadPage);
-      continue;
-    }
-    // payload index of this unit's first 32-bit word (packed order = unit order)
-    const uint64_t w0 = (uint64_t)u * (uint64_t)(page_bytes / 4);
-    for (int64_t v0 = threadIdx.x; v0 < vecs; v0 += kCopyThreads * kUnroll) {
-      uint4 r[kUnroll];
+  for (uint32_t v0 = blockIdx.x * kCopyThreads + threadIdx.x; v0 < total; v0 += stride * kUnroll) {
+    uint4 r[kUnroll];
+    uint4* d[kUnroll];
 #pragma unroll
-      for (int k = 0; k < kUnroll; ++k) {
-        const int64_t v = v0 + k * kCopyThreads;
-        if (v < vecs) r[k] = __ldcs(s + v);  // streamed once: evict first
-      }
-#pragma unroll
-      for (int k = 0; k < kUnroll; ++k) {
-        const int64_t v = v0 + k * kCopyThreads;
-        if (v < vecs) {
-          __stcs(d + v, r[k]);
-          if constexpr (CHECKSUM) sum += vec_checksum(r[k], w0 + 4 * (uint64_t)v);
+    for (int k = 0; k < kUnroll; ++k) {
+      const uint32_t v = v0 + k * stride;
+      d[k] = nullptr;
+      if (v < total) {
+        const uint32_t u = v / vpu, off = v - u * vpu;
+        const uint32_t rest = u / np;
+        const int i = (int)(u - rest * np);
+        const int c = (int)(rest & 1u);
+        const int l = (int)(rest >> 1);
+        bool ok = true;
+        const uint4* s = reinterpret_cast<const uint4*>(unit_addr(src, l, c, i, ok));
+        uint4* t = reinterpret_cast<uint4*>(const_cast<uint8_t*>(unit_addr(dst, l, c, i, ok)));
+        if (ok) {
+          r[k] = __ldcs(s + off);  // streamed once: evict first
+          d[k] = t + off;
+        } else if (off == 0) {
+          set_error(error, kErrBadPage);
         }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k) {
+      if (d[k]) {
+        __stcs(d[k], r[k]);
+        if constexpr (CHECKSUM) sum += vec_checksum(r[k], 4 * (uint64_t)(v0 + (uint32_t)k * stride));
       }
     }
   }
@@ -98,14 +106,15 @@ __global__ void __launch_bounds__(kCopyThreads) kv_pages_copy_kernel(const PageS
 }  // namespace
 
 cudaError_t launch_kv_pages_copy(const KvCopyParams& p, cudaStream_t stream) {
-  const int64_t units = (int64_t)p.num_layers * 2 * p.num_pages;
-  if (units == 0) return cudaSuccess;
+  const int64_t vecs = (int64_t)p.num_layers * 2 * p.num_pages * (p.page_bytes / 16);
+  if (vecs == 0) return cudaSuccess;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  // 256-thread CTAs, 8 per SM resident at most; never more CTAs than units
+  // 256-thread CTAs, 8 per SM (a full SM); fewer when the copy is small
   const int64_t want = (int64_t)sms * 8;
-  const int grid = (int)(units < want ? units : want);
+  const int64_t need = (vecs + kCopyThreads * kUnroll - 1) / (kCopyThreads * kUnroll);
+  const int grid = (int)(need < want ? need : want);
   const PageSide src{const_cast<uint8_t*>(static_cast<const uint8_t*>(p.src)), p.src_s_layer, p.src_s_kv,
                      p.src_s_block, p.src_pages, p.src_num_blocks};
   const PageSide dst{static_cast<uint8_t*>(p.dst), p.dst_s_layer, p.dst_s_kv, p.dst_s_block, p.dst_pages,
