@@ -139,3 +139,25 @@ def test_two_rank_handoff_protocol_gloo(tmp_path):
     ok, digest = out.read_text().split()
     z = dict(np.load(os.path.join(ROOT, "tests", "golden", "handoff_fp32.npz")))
     assert ok == "1" and digest == str(z["sha_dst_after"])
+
+
+def test_invariant_divisor_identity():
+    """The page-copy kernel divides by the page vector count and the page count
+    with a multiply-high (Granlund & Montgomery 1994): with s = ceil(log2 d) and
+    m = floor(2^32 (2^s - d) / d) + 1, n // d == (mulhi(n, m) + n) >> s for all
+    32-bit n. Checked here for the divisors the kernel meets and edge values."""
+    import random
+    rng = random.Random(1)
+
+    def magic(d):
+        s = 0
+        while (1 << s) < d:
+            s += 1
+        return ((1 << 32) * ((1 << s) - d)) // d + 1, s
+
+    for d in [1, 2, 3, 7, 14, 112, 128, 1792, 1793, 4096, 65535, 123457, 2 ** 31 - 1, 2 ** 31, 2 ** 32 - 1]:
+        m, s = magic(d)
+        assert m < 2 ** 32
+        for n in [0, 1, d - 1, d, d + 1, 2 ** 31 - 1, 2 ** 32 - 1] + [rng.getrandbits(32) for _ in range(5000)]:
+            if 0 <= n < 2 ** 32:
+                assert (((n * m) >> 32) + n) >> s == n // d, (d, n)

@@ -25,6 +25,25 @@ namespace {
 constexpr int kCopyThreads = 256;
 constexpr int kUnroll = 4;
 
+// Division by a loop-invariant divisor d (Granlund & Montgomery, "Division by
+// invariant integers using multiplication", 1994): with s = ceil(log2 d) and
+// m = floor(2^32 (2^s - d) / d) + 1, n / d = (umulhi(n, m) + n) >> s for every
+// 32-bit n (the sum is formed in 64 bits).
+struct FastDiv {
+  uint32_t d, m, s;
+};
+
+FastDiv make_fast_div(uint32_t d) {
+  uint32_t s = 0;
+  while (((uint64_t)1 << s) < d) ++s;
+  const uint64_t m = (((uint64_t)1 << 32) * (((uint64_t)1 << s) - d)) / d + 1;
+  return FastDiv{d, (uint32_t)m, s};
+}
+
+__device__ __forceinline__ uint32_t fast_div(uint32_t n, const FastDiv& f) {
+  return (uint32_t)(((uint64_t)__umulhi(n, f.m) + n) >> f.s);
+}
+
 struct PageSide {
   uint8_t* base;
   int64_t s_layer, s_kv, s_block;  // byte strides
@@ -54,13 +73,12 @@ __device__ __forceinline__ uint64_t vec_checksum(const uint4& v, uint64_t w) {
 // end. Four vectors per thread are in flight.
 template <bool CHECKSUM>
 __global__ void __launch_bounds__(kCopyThreads) kv_pages_copy_kernel(const PageSide src, const PageSide dst,
-                                                                    int num_layers, int num_pages,
-                                                                    int64_t page_bytes, unsigned long long* checksum,
+                                                                    const FastDiv vpu_div, const FastDiv np_div,
+                                                                    uint32_t total, unsigned long long* checksum,
                                                                     int32_t* error) {
   // 32-bit index math: the host keeps one call's vectors below 2^31
-  const uint32_t vpu = (uint32_t)(page_bytes / 16);
-  const uint32_t np = (uint32_t)num_pages;
-  const uint32_t total = (uint32_t)num_layers * 2u * np * vpu;
+  const uint32_t vpu = vpu_div.d;
+  const uint32_t np = np_div.d;
   const uint32_t stride = gridDim.x * kCopyThreads;
   uint64_t sum = 0;
   for (uint32_t v0 = blockIdx.x * kCopyThreads + threadIdx.x; v0 < total; v0 += stride * kUnroll) {
@@ -71,8 +89,8 @@ __global__ void __launch_bounds__(kCopyThreads) kv_pages_copy_kernel(const PageS
       const uint32_t v = v0 + k * stride;
       d[k] = nullptr;
       if (v < total) {
-        const uint32_t u = v / vpu, off = v - u * vpu;
-        const uint32_t rest = u / np;
+        const uint32_t u = fast_div(v, vpu_div), off = v - u * vpu;
+        const uint32_t rest = fast_div(u, np_div);
         const int i = (int)(u - rest * np);
         const int c = (int)(rest & 1u);
         const int l = (int)(rest >> 1);
@@ -119,12 +137,14 @@ cudaError_t launch_kv_pages_copy(const KvCopyParams& p, cudaStream_t stream) {
                      p.src_s_block, p.src_pages, p.src_num_blocks};
   const PageSide dst{static_cast<uint8_t*>(p.dst), p.dst_s_layer, p.dst_s_kv, p.dst_s_block, p.dst_pages,
                      p.dst_num_blocks};
+  const FastDiv vpu_div = make_fast_div((uint32_t)(p.page_bytes / 16));
+  const FastDiv np_div = make_fast_div((uint32_t)p.num_pages);
   if (p.checksum)
-    kv_pages_copy_kernel<true><<<grid, kCopyThreads, 0, stream>>>(src, dst, p.num_layers, p.num_pages, p.page_bytes,
+    kv_pages_copy_kernel<true><<<grid, kCopyThreads, 0, stream>>>(src, dst, vpu_div, np_div, (uint32_t)vecs,
                                                                   p.checksum, p.error);
   else
-    kv_pages_copy_kernel<false><<<grid, kCopyThreads, 0, stream>>>(src, dst, p.num_layers, p.num_pages,
-                                                                   p.page_bytes, nullptr, p.error);
+    kv_pages_copy_kernel<false><<<grid, kCopyThreads, 0, stream>>>(src, dst, vpu_div, np_div, (uint32_t)vecs,
+                                                                   nullptr, p.error);
   return cudaGetLastError();
 }
 
