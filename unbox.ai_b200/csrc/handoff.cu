@@ -134,6 +134,17 @@ int ubx_kv_pages_copy(const void* src, int64_t src_s_layer, int64_t src_s_kv, in
   p.page_bytes = pb;
   p.checksum = reinterpret_cast<unsigned long long*>(checksum);
   p.error = error_word;
+  {
+    // local destinations take the TMA bulk path; another GPU's memory (peer
+    // access, IPC mapping) gets plain stores
+    int dev = 0;
+    cudaPointerAttributes a;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return hcuda(e, "cudaGetDevice");
+    e = cudaPointerGetAttributes(&a, dst);
+    if (e != cudaSuccess) cudaGetLastError();
+    p.dst_is_peer = !(e == cudaSuccess && a.type == cudaMemoryTypeDevice && a.device == dev);
+  }
   cudaError_t e = ubx::launch_kv_pages_copy(p, s);
   if (e != cudaSuccess) return hcuda(e, "kv_pages_copy launch");
   return UBX_OK;

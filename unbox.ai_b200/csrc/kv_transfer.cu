@@ -121,6 +121,123 @@ __global__ void __launch_bounds__(kCopyThreads) kv_pages_copy_kernel(const PageS
   }
 }
 
+// Local copies go through the TMA engine: a persistent CTA takes an equal
+// contiguous share of the copy's pieces (a page unit cut into equal pieces of at
+// most 16 KB), thread 0 bulk-loads pieces into a ring of shared-memory stages
+// and bulk-stores each one as soon as it lands, so one thread keeps up to
+// kBulkStages pieces moving and the SMs issue almost no instructions. With the
+// checksum, the CTA's threads add up each piece from shared memory meanwhile.
+constexpr int kBulkStages = 4;
+constexpr uint32_t kMaxPieceBytes = 16384;
+constexpr int kBulkThreads = 128;
+
+struct Piece {
+  const uint8_t* src;
+  uint8_t* dst;
+  uint32_t bytes;
+  uint64_t word0;  // payload index of the piece's first 32-bit word
+  bool ok;
+};
+
+__device__ __forceinline__ Piece piece_at(const PageSide& src, const PageSide& dst, uint32_t q, uint32_t ppu,
+                                          uint32_t piece_bytes, uint32_t num_pages, uint64_t page_bytes) {
+  const uint32_t u = q / ppu, part = q - u * ppu;
+  const uint32_t rest = u / num_pages;
+  const int i = (int)(u - rest * num_pages), c = (int)(rest & 1u), l = (int)(rest >> 1);
+  Piece pc;
+  pc.ok = true;
+  const uint64_t off = (uint64_t)part * piece_bytes;
+  pc.src = unit_addr(src, l, c, i, pc.ok) + off;
+  pc.dst = const_cast<uint8_t*>(unit_addr(dst, l, c, i, pc.ok)) + off;
+  pc.bytes = (uint32_t)(page_bytes - off < piece_bytes ? page_bytes - off : piece_bytes);
+  pc.word0 = ((uint64_t)u * page_bytes + off) / 4;
+  return pc;
+}
+
+template <bool CHECKSUM>
+__global__ void __launch_bounds__(kBulkThreads) kv_pages_bulk_kernel(const PageSide src, const PageSide dst,
+                                                                    uint32_t num_pages, uint64_t page_bytes,
+                                                                    uint32_t ppu, uint32_t piece_bytes,
+                                                                    uint32_t total_pieces,
+                                                                    unsigned long long* checksum, int32_t* error) {
+  extern __shared__ __align__(128) uint8_t ring[];  // kBulkStages * piece_bytes
+  __shared__ uint64_t full[kBulkStages];
+  const int tid = threadIdx.x;
+  const uint32_t q0 = (uint32_t)((uint64_t)total_pieces * blockIdx.x / gridDim.x);
+  const uint32_t q1 = (uint32_t)((uint64_t)total_pieces * (blockIdx.x + 1) / gridDim.x);
+  const int n = (int)(q1 - q0);
+  if (tid == 0) {
+    for (int st = 0; st < kBulkStages; ++st) mbar_init(&full[st], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  int issued = 0;  // pieces whose load thread 0 has issued
+  auto issue = [&](int k) {
+    const Piece pc = piece_at(src, dst, q0 + k, ppu, piece_bytes, num_pages, page_bytes);
+    uint64_t* bar = &full[k % kBulkStages];
+    if (pc.ok) {
+      mbar_arrive_expect_tx(bar, pc.bytes);
+      bulk_copy_g2s(ring + (k % kBulkStages) * piece_bytes, pc.src, pc.bytes, bar);
+    } else {
+      set_error(error, kErrBadPage);
+      mbar_arrive(bar);  // the stage completes empty; nothing is stored
+    }
+    issued = k + 1;
+  };
+  if (tid == 0)
+    for (int k = 0; k < n && k < kBulkStages; ++k) issue(k);
+
+  uint64_t sum = 0;
+  int k = 0;
+  if (CHECKSUM || tid == 0) {
+    for (; k < n; ++k) {
+      const int st = k % kBulkStages;
+      const bool landed = mbar_wait_bounded(&full[st], (uint32_t)(k / kBulkStages) & 1u);
+      bool stop;
+      if constexpr (CHECKSUM) {
+        stop = __syncthreads_or(!landed);
+      } else {
+        stop = !landed;
+      }
+      if (stop) {
+        if (tid == 0) set_error(error, kErrTimeout);
+        break;
+      }
+      const Piece pc = piece_at(src, dst, q0 + k, ppu, piece_bytes, num_pages, page_bytes);
+      const uint8_t* stage = ring + st * piece_bytes;
+      if (tid == 0) {
+        if (pc.ok) {
+          fence_proxy_async_smem();
+          bulk_copy_s2g(pc.dst, stage, pc.bytes);
+        }
+        bulk_commit_group();  // one group per piece, empty for a skipped one
+      }
+      if constexpr (CHECKSUM) {
+        if (pc.ok)
+          for (uint32_t v = tid; v < pc.bytes / 16; v += kBulkThreads)
+            sum += vec_checksum(reinterpret_cast<const uint4*>(stage)[v], pc.word0 + 4 * (uint64_t)v);
+        __syncthreads();  // stage st is read by every thread before it is refilled
+      }
+      // refill the previous piece's stage once its store has read it
+      if (tid == 0 && k >= 1 && k - 1 + kBulkStages < n) {
+        bulk_wait_group_read<1>();
+        issue(k - 1 + kBulkStages);
+      }
+    }
+  }
+  if (tid == 0) {
+    // after a timeout: let the loads still in flight land (bounded) before the CTA exits
+    for (int j = k; j < issued; ++j) mbar_wait_bounded(&full[j % kBulkStages], (uint32_t)(j / kBulkStages) & 1u);
+    bulk_wait_group<0>();  // the stores are complete before the CTA's shared memory goes away
+  }
+  if constexpr (CHECKSUM) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if ((tid & 31) == 0 && sum) atomicAdd(checksum, (unsigned long long)sum);
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_kv_pages_copy(const KvCopyParams& p, cudaStream_t stream) {
@@ -137,6 +254,31 @@ cudaError_t launch_kv_pages_copy(const KvCopyParams& p, cudaStream_t stream) {
                      p.src_s_block, p.src_pages, p.src_num_blocks};
   const PageSide dst{static_cast<uint8_t*>(p.dst), p.dst_s_layer, p.dst_s_kv, p.dst_s_block, p.dst_pages,
                      p.dst_num_blocks};
+  if (!p.dst_is_peer) {
+    // TMA bulk path: pieces of equal size (a multiple of 16 bytes), at most 16 KB
+    const uint32_t ppu = (uint32_t)((p.page_bytes + kMaxPieceBytes - 1) / kMaxPieceBytes);
+    const uint32_t piece = (uint32_t)(((p.page_bytes + ppu - 1) / ppu + 15) / 16 * 16);
+    const uint32_t pieces = (uint32_t)((int64_t)p.num_layers * 2 * p.num_pages) * ppu;
+    const int smem = kBulkStages * (int)piece;
+    static int attr_done[64] = {0};
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+      cudaFuncSetAttribute(kv_pages_bulk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBulkStages * 16384);
+      cudaFuncSetAttribute(kv_pages_bulk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kBulkStages * 16384);
+      attr_done[dev] = 1;
+    }
+    // three CTAs per SM (3 x 64 KB of stages), never more CTAs than pieces
+    const int64_t want_b = (int64_t)sms * 3;
+    const int grid_b = (int)(pieces < want_b ? pieces : want_b);
+    if (p.checksum)
+      kv_pages_bulk_kernel<true><<<grid_b, kBulkThreads, smem, stream>>>(
+          src, dst, (uint32_t)p.num_pages, (uint64_t)p.page_bytes, ppu, piece, pieces, p.checksum, p.error);
+    else
+      kv_pages_bulk_kernel<false><<<grid_b, kBulkThreads, smem, stream>>>(
+          src, dst, (uint32_t)p.num_pages, (uint64_t)p.page_bytes, ppu, piece, pieces, nullptr, p.error);
+    return cudaGetLastError();
+  }
+  // destination in another GPU's memory: plain 16-byte stores over NVLink
   const FastDiv vpu_div = make_fast_div((uint32_t)(p.page_bytes / 16));
   const FastDiv np_div = make_fast_div((uint32_t)p.num_pages);
   if (p.checksum)

@@ -108,6 +108,29 @@ __device__ __forceinline__ void bulk_copy_g2s(void* smem_dst, const void* gmem_s
       : "memory");
 }
 
+// Bulk copy shared -> global (TMA engine, non-tensor), tracked in the issuing
+// thread's bulk async-groups. Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_copy_s2g(void* gmem_dst, const void* smem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+               ::"l"(reinterpret_cast<uint64_t>(gmem_dst)), "r"(smem_u32(smem_src)), "r"(bytes)
+               : "memory");
+}
+
+// Closes the bulk operations issued so far into one group (an empty group if none).
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Until at most N of this thread's most recent bulk groups still read their source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// Until at most N of this thread's most recent bulk groups are incomplete.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // ---------------------------------------------------------------- elements
 template <typename T>
 struct Elem;

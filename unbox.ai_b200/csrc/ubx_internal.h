@@ -145,6 +145,7 @@ struct KvCopyParams {
   int64_t page_bytes;
   unsigned long long* checksum;  // null: none
   int32_t* error;
+  bool dst_is_peer;  // destination outside this GPU's memory: no TMA stores to it
 };
 
 cudaError_t launch_kv_pages_copy(const KvCopyParams& p, cudaStream_t stream);
