@@ -1,0 +1,117 @@
+"""CPU: the shared-prefix (cascade) planner (unbox_b200.cascade.plan_cascade).
+
+The plan must split every grouped request's context exactly into the group's
+shared pages and the request's own suffix, so that the log-sum-exp merge of the
+two attentions equals attention over the whole context. Checked with a float64
+numpy attention over the plan's pieces against the oracle's full attention.
+"""
+import numpy as np
+import pytest
+
+from conftest import PKG
+
+
+def plan(lay, **kw):
+    return PKG.cascade.plan_cascade(lay.block_table, lay.context_lens, lay.num_heads, lay.num_kv_heads,
+                                    device="cpu", **kw)
+
+
+def attend(q, k_cache, v_cache, pages, ntok, scale):
+    """(H, D) attention of one request over the first ntok tokens of `pages`;
+    returns (out (H, D), lse (H,)) in float64, natural log."""
+    H, D = q.shape
+    KVH = k_cache.shape[2]
+    G = H // KVH
+    rows_k = np.concatenate([k_cache[p] for p in pages], axis=0)[:ntok]   # (ntok, KVH, D)
+    rows_v = np.concatenate([v_cache[p] for p in pages], axis=0)[:ntok]
+    out = np.zeros((H, D))
+    lse = np.full(H, -np.inf)
+    if ntok == 0:
+        return out, lse
+    for h in range(H):
+        s = rows_k[:, h // G] @ q[h] * scale
+        m = s.max()
+        w = np.exp(s - m)
+        out[h] = w @ rows_v[:, h // G] / w.sum()
+        lse[h] = m + np.log(w.sum())
+    return out, lse
+
+
+def merge(parts):
+    M = max(l.max() for _, l in parts)
+    num = sum(o * np.exp(l - M)[:, None] for o, l in parts)
+    den = sum(np.exp(l - M) for _, l in parts)
+    return num / den[:, None]
+
+
+def test_radix_layout_groups_and_suffix_tables():
+    wl = PKG.workloads
+    lay = wl.layout_radix_prefix(3, batch=20, prefix_pages=12, suffix_lo=1, suffix_hi=70)
+    p = plan(lay)
+    assert len(p.groups) == 1
+    members, shared = p.groups[0]
+    assert sorted(members) == list(range(20)) and len(shared) == 12
+    assert shared == lay.block_table[0, :12].tolist()
+    assert p.max_chunks == 2
+    sbt, sctx = p.suffix_block_table.numpy(), p.suffix_context_lens.numpy()
+    for b in range(20):
+        assert sctx[b] == lay.context_lens[b] - 12 * 16 >= 1
+        n = (sctx[b] + 15) // 16
+        assert np.array_equal(sbt[b, :n], lay.block_table[b, 12:12 + n])
+    # every (member, chunk) pair covered by exactly one work item
+    seen = {}
+    mlist = p.member_list.numpy()
+    for m_off, nm, pg_off, npg, chunk, _ in p.work.numpy():
+        assert 1 <= npg <= 8 and nm * 2 <= 128
+        for b in mlist[m_off:m_off + nm]:
+            seen[(int(b), int(chunk))] = seen.get((int(b), int(chunk)), 0) + 1
+    assert set(seen.values()) == {1} and len(seen) == 20 * 2
+    assert sorted(map(tuple, p.merge_items.numpy().tolist())) == [(b, 2) for b in range(20)]
+
+
+def test_no_sharing_and_short_prefixes_stay_plain():
+    wl = PKG.workloads
+    lay = wl.layout_uniform(4, 9, 20, 300, num_blocks=200)
+    p = plan(lay)
+    assert p.num_work == 0 and p.num_merge == 0
+    assert np.array_equal(p.suffix_block_table.numpy(), lay.block_table)
+    # a shared prefix shorter than min_shared_pages is left alone
+    lay2 = wl.layout_radix_prefix(5, batch=6, prefix_pages=3, suffix_lo=1, suffix_hi=30)
+    assert plan(lay2, min_shared_pages=4).num_work == 0
+    assert plan(lay2, min_shared_pages=2).num_work > 0
+
+
+def test_prefix_cut_leaves_every_member_a_private_token():
+    """A member whose context ends inside (or at the end of) the shared pages
+    caps the group's prefix: the token being decoded stays on a private page."""
+    wl = PKG.workloads
+    lay = wl.layout_radix_prefix(6, batch=5, prefix_pages=10, suffix_lo=5, suffix_hi=40)
+    lay.context_lens[2] = 6 * 16          # ends exactly at the end of page 5
+    p = plan(lay)
+    members, shared = p.groups[0]
+    assert len(shared) == 5               # (96 - 1) // 16
+    assert p.suffix_context_lens.numpy()[2] == 16
+
+
+@pytest.mark.parametrize("heads", [(16, 8, 112), (16, 2, 64), (8, 8, 64)])
+def test_merge_of_plan_pieces_equals_full_attention(heads, oracle):
+    """Attention over the suffix table + attention over the shared pages, merged
+    by log-sum-exp, equals the oracle's attention over the original table."""
+    H, KVH, D = heads
+    wl = PKG.workloads
+    lay = wl.layout_radix_prefix(7, batch=9, prefix_pages=9, suffix_lo=1, suffix_hi=50)
+    lay.num_heads, lay.num_kv_heads, lay.head_dim = H, KVH, D
+    t = wl.materialize_host(lay, 7, dtype="float32")
+    p = plan(lay)
+    full, st = oracle.paged_decode_attention(t["q"], t["k_cache"], t["v_cache"], t["block_table"],
+                                             t["context_lens"])
+    assert st == 0
+    q, kc, vc = (t[k].numpy().astype(np.float64) for k in ("q", "k_cache", "v_cache"))
+    scale = D ** -0.5
+    members, shared = p.groups[0]
+    sbt, sctx = p.suffix_block_table.numpy(), p.suffix_context_lens.numpy()
+    for b in members:
+        n = (sctx[b] + 15) // 16
+        o_s, l_s = attend(q[b], kc, vc, sbt[b, :n], int(sctx[b]), scale)
+        o_p, l_p = attend(q[b], kc, vc, shared, len(shared) * 16, scale)
+        np.testing.assert_allclose(merge([(o_s, l_s), (o_p, l_p)]), full[b], atol=1e-9)

@@ -35,6 +35,10 @@ unbox_platform/infer/kvcache.py of the reference):
   (engine.py:126-128), alone or with its norm and rotary steps (:121-128).
 * ``rope_table(head_dim, num_positions, theta)`` -- the (cos, sin) table of
   precompute_freqs_cis (model.py:30-34).
+* ``plan_cascade(block_table, context_lens, H, KVH)`` /
+  ``paged_attention_cascade(q, k_cache, v_cache, plan, ...)`` -- decode attention
+  that reads radix-shared prefix pages once per step for all requests sharing
+  them (kvcache.py:97-122 produces such tables).
 * ``handoff`` -- KV page hand-off between workers: ``serialize_blocks`` /
   ``deserialize_blocks`` (kvcache.py:268-277) on the device with a typed
   header, and ``transfer_pages`` pool to pool over NVLink.
@@ -45,6 +49,7 @@ __all__ = [
     "paged_decode_attention", "paged_attention", "paged_attention_split", "kv_append",
     "slot_mapping", "DecodeWorkspace", "workloads", "library", "sharding", "qk_norm_rope",
     "paged_decode_prep_attention", "prefill_kv_write", "prefill_prep", "prefill_slots", "rope_table", "handoff",
+    "cascade", "plan_cascade", "paged_attention_cascade",
 ]
 
 
@@ -60,6 +65,8 @@ def __getattr__(name):
     import importlib
     if name in _OPS:
         return getattr(importlib.import_module(__name__ + ".ops"), name)
-    if name in ("library", "sharding", "ops", "build", "handoff"):
+    if name in ("plan_cascade", "paged_attention_cascade", "CascadePlan"):
+        return getattr(importlib.import_module(__name__ + ".cascade"), name)
+    if name in ("library", "sharding", "ops", "build", "handoff", "cascade"):
         return importlib.import_module(__name__ + "." + name)
     raise AttributeError(name)

@@ -353,7 +353,7 @@ int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache
                 const int32_t* context_lens, void* out, int64_t o_s_b, int64_t o_s_h, int batch, int num_heads,
                 int num_kv_heads, int head_dim, int block_size, int64_t num_blocks, int max_blocks_per_seq,
                 float scale, int dtype, int schedule, int split_pages, int flags, void* workspace,
-                size_t workspace_bytes, const AppendArgs* app, const PrepArgs* prep, void* stream) {
+                size_t workspace_bytes, const AppendArgs* app, const PrepArgs* prep, float* lse, void* stream) {
   g_last_error.clear();
   int st = check_shape(num_heads, num_kv_heads, head_dim, block_size, dtype);
   if (st != UBX_OK) return st;
@@ -381,6 +381,8 @@ int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache
     if (!aligned16(app->k_new) || !aligned16(app->v_new) || !m16(app->s_tok) || !m16(app->s_head))
       return fail(UBX_ERR_INVALID_ARGUMENT, "k_new / v_new rows must be 16-byte aligned");
   }
+  if (lse && es != 2)
+    return fail(UBX_ERR_UNSUPPORTED, "the log-sum-exp output is built for bf16/f16");
   if (prep) {
     if (es != 2)
       return fail(UBX_ERR_UNSUPPORTED, "fused pre-attention is built for bf16/f16 (fp32: ubx_qk_norm_rope_append, "
@@ -452,6 +454,7 @@ int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache
   p.rope = prep ? prep->rope : nullptr;
   p.rope_sp = prep ? prep->rope_sp : 0;
   p.rope_n = prep ? prep->rope_n : 0;
+  p.lse = lse;
 
   LaunchShape shape{pl.grid, pl.block, pl.smem, (flags & UBX_FLAG_OVERLAP_PREVIOUS) != 0};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -477,7 +480,7 @@ int ubx_paged_decode_attention(const void* q, int64_t q_s_b, int64_t q_s_h, cons
   return decode_impl(q, q_s_b, q_s_h, k_cache, v_cache, c_s_block, c_s_tok, c_s_head, block_table, bt_s_row,
                      context_lens, out, o_s_b, o_s_h, batch, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
                      max_blocks_per_seq, scale, dtype, schedule, split_pages, 0, workspace, workspace_bytes, nullptr,
-                     nullptr, stream);
+                     nullptr, nullptr, stream);
 }
 
 int ubx_paged_decode_append_attention(const void* k_new, const void* v_new, int64_t new_s_tok, int64_t new_s_head,
@@ -492,7 +495,134 @@ int ubx_paged_decode_append_attention(const void* k_new, const void* v_new, int6
   return decode_impl(q, q_s_b, q_s_h, k_cache, v_cache, c_s_block, c_s_tok, c_s_head, block_table, bt_s_row,
                      context_lens, out, o_s_b, o_s_h, batch, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
                      max_blocks_per_seq, scale, dtype, schedule, split_pages, flags, workspace, workspace_bytes, &app,
-                     nullptr, stream);
+                     nullptr, nullptr, stream);
+}
+
+int ubx_paged_decode_attention_lse(const void* k_new, const void* v_new, int64_t new_s_tok, int64_t new_s_head,
+                                   const void* q, int64_t q_s_b, int64_t q_s_h, void* k_cache, void* v_cache,
+                                   int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head, const int32_t* block_table,
+                                   int64_t bt_s_row, const int32_t* context_lens, void* out, int64_t o_s_b,
+                                   int64_t o_s_h, int batch, int num_heads, int num_kv_heads, int head_dim,
+                                   int block_size, int64_t num_blocks, int max_blocks_per_seq, float scale, int dtype,
+                                   int schedule, int split_pages, int flags, float* lse_out, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+  if ((k_new == nullptr) != (v_new == nullptr)) {
+    g_last_error = "pass both k_new and v_new, or neither";
+    return UBX_ERR_INVALID_ARGUMENT;
+  }
+  if (!lse_out) {
+    g_last_error = "lse_out is required";
+    return UBX_ERR_INVALID_ARGUMENT;
+  }
+  const AppendArgs app{k_new, v_new, new_s_tok, new_s_head};
+  return decode_impl(q, q_s_b, q_s_h, k_cache, v_cache, c_s_block, c_s_tok, c_s_head, block_table, bt_s_row,
+                     context_lens, out, o_s_b, o_s_h, batch, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
+                     max_blocks_per_seq, scale, dtype, schedule, split_pages, flags, workspace, workspace_bytes,
+                     k_new ? &app : nullptr, nullptr, lse_out, stream);
+}
+
+static size_t cascade_ml_bytes(int batch, int num_heads, int max_chunks) {
+  return align256((size_t)batch * num_heads * max_chunks * sizeof(float2));
+}
+
+int ubx_cascade_workspace_size(int batch, int num_heads, int head_dim, int max_chunks, size_t* bytes) {
+  g_last_error.clear();
+  if (!bytes || batch < 0 || num_heads <= 0 || head_dim <= 0 || max_chunks < 0)
+    return fail(UBX_ERR_INVALID_ARGUMENT, "bad cascade workspace query");
+  *bytes = cascade_ml_bytes(batch, num_heads, max_chunks) +
+           (size_t)batch * num_heads * max_chunks * head_dim * sizeof(float);
+  return UBX_OK;
+}
+
+int ubx_cascade_prefix_attention(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache,
+                                 const void* v_cache, int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head,
+                                 int64_t num_blocks, const int32_t* page_list, const int32_t* member_list,
+                                 const int32_t* work_items, int num_work_items, int max_chunks, int batch,
+                                 int num_heads, int num_kv_heads, int head_dim, float scale, int dtype,
+                                 void* cascade_ws, size_t cascade_ws_bytes, int32_t* error_word, void* stream) {
+  g_last_error.clear();
+  int st = check_shape(num_heads, num_kv_heads, head_dim, kBlockSize, dtype);
+  if (st != UBX_OK) return st;
+  if (dtype == UBX_DTYPE_F32) return fail(UBX_ERR_UNSUPPORTED, "the cascade pass is built for bf16/f16");
+  if (num_work_items < 0 || max_chunks <= 0 || batch <= 0 || num_blocks <= 0)
+    return fail(UBX_ERR_INVALID_ARGUMENT, "bad cascade sizes");
+  if (num_work_items == 0) return UBX_OK;
+  if (!q || !k_cache || !v_cache || !page_list || !member_list || !work_items || !cascade_ws)
+    return fail(UBX_ERR_INVALID_ARGUMENT, "null pointer");
+  const int es = 2;
+  auto m16 = [&](int64_t s) { return ((s * es) & 15) == 0; };
+  if (!aligned16(q) || !m16(q_s_b) || !m16(q_s_h) || !aligned16(k_cache) || !aligned16(v_cache) ||
+      !m16(c_s_block) || !m16(c_s_tok))
+    return fail(UBX_ERR_INVALID_ARGUMENT, "q rows and K/V caches must be 16-byte aligned");
+  if (c_s_head != head_dim) return fail(UBX_ERR_UNSUPPORTED, "KV heads must be contiguous within a token row");
+  size_t need = 0;
+  ubx_cascade_workspace_size(batch, num_heads, head_dim, max_chunks, &need);
+  if (cascade_ws_bytes < need)
+    return fail(UBX_ERR_WORKSPACE, "cascade workspace of %zu bytes, this call needs %zu", cascade_ws_bytes, need);
+  if (!(scale > 0.f) && !(scale < 0.f)) return fail(UBX_ERR_INVALID_ARGUMENT, "scale must be finite and non-zero");
+  CascadeParams p;
+  p.q = q;
+  p.q_sb = q_s_b;
+  p.q_sh = q_s_h;
+  p.k_cache = k_cache;
+  p.v_cache = v_cache;
+  p.c_sblk = c_s_block;
+  p.c_stok = c_s_tok;
+  p.num_blocks = num_blocks;
+  p.page_list = page_list;
+  p.member_list = member_list;
+  p.work = work_items;
+  p.num_work = num_work_items;
+  p.batch = batch;
+  p.num_heads = num_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.max_chunks = max_chunks;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.pitch = tile_row_pitch(head_dim * es);
+  uint8_t* ws = static_cast<uint8_t*>(cascade_ws);
+  p.part_ml = reinterpret_cast<float2*>(ws);
+  p.part_o = reinterpret_cast<float*>(ws + cascade_ml_bytes(batch, num_heads, max_chunks));
+  p.error = error_word;
+  cudaError_t e = launch_cascade_prefix(dtype, head_dim, p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cascade prefix launch");
+  return UBX_OK;
+}
+
+int ubx_cascade_merge(void* out, int64_t o_s_b, int64_t o_s_h, const float* lse, const int32_t* merge_items,
+                      int num_merge_items, int max_chunks, int batch, int num_heads, int head_dim, int dtype,
+                      const void* cascade_ws, size_t cascade_ws_bytes, int32_t* error_word, void* stream) {
+  g_last_error.clear();
+  if (dtype != UBX_DTYPE_BF16 && dtype != UBX_DTYPE_F16)
+    return fail(UBX_ERR_UNSUPPORTED, "the cascade merge is built for bf16/f16");
+  if (head_dim != 64 && head_dim != 112 && head_dim != 128)
+    return fail(UBX_ERR_UNSUPPORTED, "head_dim %d not built (64, 112, 128)", head_dim);
+  if (num_merge_items < 0 || max_chunks <= 0 || batch <= 0 || num_heads <= 0)
+    return fail(UBX_ERR_INVALID_ARGUMENT, "bad merge sizes");
+  if (num_merge_items == 0) return UBX_OK;
+  if (!out || !lse || !merge_items || !cascade_ws) return fail(UBX_ERR_INVALID_ARGUMENT, "null pointer");
+  auto m16 = [&](int64_t s) { return ((s * 2) & 15) == 0; };
+  if (!aligned16(out) || !m16(o_s_b) || !m16(o_s_h)) return fail(UBX_ERR_INVALID_ARGUMENT, "out rows must be 16-byte aligned");
+  size_t need = 0;
+  ubx_cascade_workspace_size(batch, num_heads, head_dim, max_chunks, &need);
+  if (cascade_ws_bytes < need)
+    return fail(UBX_ERR_WORKSPACE, "cascade workspace of %zu bytes, this call needs %zu", cascade_ws_bytes, need);
+  CascadeMergeParams p;
+  p.out = out;
+  p.o_sb = o_s_b;
+  p.o_sh = o_s_h;
+  p.lse = lse;
+  p.items = merge_items;
+  p.num_items = num_merge_items;
+  p.batch = batch;
+  p.num_heads = num_heads;
+  p.max_chunks = max_chunks;
+  const uint8_t* ws = static_cast<const uint8_t*>(cascade_ws);
+  p.part_ml = reinterpret_cast<const float2*>(ws);
+  p.part_o = reinterpret_cast<const float*>(ws + cascade_ml_bytes(batch, num_heads, max_chunks));
+  p.error = error_word;
+  cudaError_t e = launch_cascade_merge(dtype, head_dim, p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cascade merge launch");
+  return UBX_OK;
 }
 
 int ubx_paged_decode_prep_attention(const void* q_raw, int64_t q_s_b, int64_t q_s_h, const void* k_raw,
@@ -510,7 +640,7 @@ int ubx_paged_decode_prep_attention(const void* q_raw, int64_t q_s_b, int64_t q_
   return decode_impl(q_raw, q_s_b, q_s_h, k_cache, v_cache, c_s_block, c_s_tok, c_s_head, block_table, bt_s_row,
                      context_lens, out, o_s_b, o_s_h, batch, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
                      max_blocks_per_seq, scale, dtype, schedule, split_pages, flags, workspace, workspace_bytes, &app,
-                     &prep, stream);
+                     &prep, nullptr, stream);
 }
 
 }  // extern "C"

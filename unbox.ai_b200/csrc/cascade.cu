@@ -1,0 +1,306 @@
+// Shared-prefix (cascade) decode attention for radix-shared pages (sm_100a).
+//
+// The reference's radix cache hands several requests the same physical pages
+// for a common prompt prefix (unbox_platform/infer/kvcache.py:97-122, prefix
+// match producing shared block tables); paged_decode_attention_ref then reads
+// those pages once per request. Here a decode step is split in three:
+//   1. the decode kernel attends each request over its private suffix pages
+//      (positions past the shared prefix) and also returns the log-sum-exp;
+//   2. cascade_prefix_kernel attends every request of a prefix group over the
+//      shared pages at once: a CTA loads a chunk of the shared pages of one KV
+//      head into shared memory once, and each warp runs a 16-row tensor-core
+//      tile of (request, query head) rows of that group over them (mma.sync
+//      m16n8k16, full tiles: G query heads x 16/G requests), writing unnormalised
+//      partial (acc, max, sum) rows per chunk;
+//   3. cascade_merge_kernel merges the suffix output with the chunks' partials by
+//      log-sum-exp weights (the same combination the split-KV path uses).
+// The result equals attention over the whole context (softmax is exactly
+// decomposable over disjoint key sets).
+#include "ubx_common.cuh"
+#include "ubx_internal.h"
+#include "ubx_mma.cuh"
+
+namespace ubx {
+
+namespace {
+
+constexpr unsigned kAll = 0xffffffffu;
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kCascadeWarps * 32) cascade_prefix_kernel(const CascadeParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint64_t bar;
+  constexpr int KS = D / 16;  // QK k-steps
+  constexpr int NT = D / 8;   // PV n-tiles
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int kvh = blockIdx.y;
+  const int32_t* item = p.work + kCascadeWorkInts * blockIdx.x;
+  const int m_off = __ldg(item + 0), n_mem = __ldg(item + 1), pg_off = __ldg(item + 2), n_pg = __ldg(item + 3),
+            chunk = __ldg(item + 4);
+  const int G = p.num_heads / p.num_kv_heads;
+  if (n_pg < 1 || n_pg > kCascadeMaxPages || n_mem < 1 || n_mem * G > kCascadeWarps * 16 || chunk < 0 ||
+      chunk >= p.max_chunks) {
+    if (threadIdx.x == 0) set_error(p.error, kErrBadWork);
+    return;
+  }
+  constexpr int kRowBytes = D * (int)sizeof(T);  // one KV head row of one token
+  const int tile = kBlockSize * p.pitch;          // one page of this head, K or V
+  uint8_t* k_s = smem;
+  uint8_t* v_s = smem + n_pg * tile;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 32);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // ---- load: warp 0, lane = (K|V, token row); one bulk copy per row and page
+  if (warp == 0) {
+    const int r = lane & 15;
+    uint8_t* base = lane < 16 ? k_s : v_s;
+    const uint8_t* pool = static_cast<const uint8_t*>(lane < 16 ? p.k_cache : p.v_cache);
+    uint32_t bytes = 0;
+    for (int i = 0; i < n_pg; ++i) {
+      const int page = __ldg(&p.page_list[pg_off + i]);
+      if (page >= 0 && (int64_t)page < p.num_blocks) {
+        bytes += kRowBytes;
+      } else {
+        if (r == 0) set_error(p.error, kErrBadPage);
+        uint4* row = reinterpret_cast<uint4*>(base + i * tile + r * p.pitch);
+        for (int c = 0; c < kRowBytes / 16; ++c) row[c] = make_uint4(0, 0, 0, 0);
+      }
+    }
+    mbar_arrive_expect_tx(&bar, bytes);
+    for (int i = 0; i < n_pg; ++i) {
+      const int page = __ldg(&p.page_list[pg_off + i]);
+      if (page >= 0 && (int64_t)page < p.num_blocks)
+        bulk_copy_g2s(base + i * tile + r * p.pitch,
+                      pool + ((int64_t)page * p.c_sblk + (int64_t)r * p.c_stok + (int64_t)kvh * D) * sizeof(T),
+                      kRowBytes, &bar);
+    }
+  }
+  if (!mbar_wait_bounded(&bar, 0)) {
+    if (threadIdx.x == 0) {
+      set_error(p.error, kErrTimeout);
+      mbar_wait_bounded(&bar, 0);  // give the copies in flight one more bound before the CTA exits
+    }
+    return;
+  }
+
+  // ---- tiles: 16 rows = (request, query head), request-major; G heads x 16/G requests
+  const int MT = 16 / G;
+  const int n_tiles = (n_mem + MT - 1) / MT;
+  const int qr = lane >> 2, qc = lane & 3;
+  const float c = p.scale_log2;
+  const int rs = p.pitch / (int)sizeof(T);
+  const int k_row = (((lane >> 4) & 1) * 8 + (lane & 7)) * rs + ((lane >> 3) & 1) * 8;
+  const int v_row = (((lane >> 3) & 1) * 8 + (lane & 7)) * rs + ((lane >> 4) & 1) * 8;
+  for (int t = warp; t < n_tiles; t += kCascadeWarps) {
+    int bs[2], head[2];
+    bool real[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = qr + 8 * h, mi = t * MT + r / G;
+      real[h] = mi < n_mem;
+      bs[h] = real[h] ? __ldg(&p.member_list[m_off + mi]) : 0;
+      real[h] = real[h] && bs[h] >= 0 && bs[h] < p.batch;
+      head[h] = kvh * G + r % G;
+    }
+    uint32_t qa[KS][4];
+    {
+      const T* q0 = static_cast<const T*>(p.q) + (int64_t)bs[0] * p.q_sb + (int64_t)head[0] * p.q_sh;
+      const T* q1 = static_cast<const T*>(p.q) + (int64_t)bs[1] * p.q_sb + (int64_t)head[1] * p.q_sh;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        qa[ks][0] = real[0] ? __ldg(reinterpret_cast<const uint32_t*>(q0 + 16 * ks + 2 * qc)) : 0u;
+        qa[ks][1] = real[1] ? __ldg(reinterpret_cast<const uint32_t*>(q1 + 16 * ks + 2 * qc)) : 0u;
+        qa[ks][2] = real[0] ? __ldg(reinterpret_cast<const uint32_t*>(q0 + 16 * ks + 8 + 2 * qc)) : 0u;
+        qa[ks][3] = real[1] ? __ldg(reinterpret_cast<const uint32_t*>(q1 + 16 * ks + 8 + 2 * qc)) : 0u;
+      }
+    }
+    float o[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+
+    for (int i = 0; i < n_pg; ++i) {
+      const T* kt = reinterpret_cast<const T*>(k_s + i * tile);
+      const T* vt = reinterpret_cast<const T*>(v_s + i * tile);
+      // S[16 rows x 16 tokens]: sa[n-tile][0..1] row qr, [2..3] row qr + 8
+      float sa[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4(kt + k_row + 16 * ks, r0, r1, r2, r3);
+        mma16816<T>(sa[0], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], r0, r1);
+        mma16816<T>(sa[1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], r2, r3);
+      }
+      float pv[2][4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float mx = fmaxf(fmaxf(sa[0][2 * h], sa[0][2 * h + 1]), fmaxf(sa[1][2 * h], sa[1][2 * h + 1]));
+        mx = fmaxf(mx, __shfl_xor_sync(kAll, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(kAll, mx, 2));
+        const float m_new = fmaxf(m[h], mx);
+        if (m_new != m[h]) {  // rescale this row only when its max moved
+          const float alpha = exp2f((m[h] - m_new) * c);
+          l[h] *= alpha;
+#pragma unroll
+          for (int n = 0; n < NT; ++n) {
+            o[n][2 * h] *= alpha;
+            o[n][2 * h + 1] *= alpha;
+          }
+          m[h] = m_new;
+        }
+        const float mc = m[h] * c;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          pv[nt][2 * h] = exp2f(fmaf(sa[nt][2 * h], c, -mc));
+          pv[nt][2 * h + 1] = exp2f(fmaf(sa[nt][2 * h + 1], c, -mc));
+          l[h] += pv[nt][2 * h] + pv[nt][2 * h + 1];
+        }
+      }
+      // P as the A operand of PV (the S accumulator layout is the A layout)
+      const uint32_t pa0 = Elem<T>::pack2(pv[0][0], pv[0][1]);
+      const uint32_t pa1 = Elem<T>::pack2(pv[0][2], pv[0][3]);
+      const uint32_t pa2 = Elem<T>::pack2(pv[1][0], pv[1][1]);
+      const uint32_t pa3 = Elem<T>::pack2(pv[1][2], pv[1][3]);
+#pragma unroll
+      for (int np = 0; np < NT / 2; ++np) {
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4_trans(vt + v_row + 16 * np, r0, r1, r2, r3);
+        mma16816<T>(o[2 * np], pa0, pa1, pa2, pa3, r0, r1);
+        mma16816<T>(o[2 * np + 1], pa0, pa1, pa2, pa3, r2, r3);
+      }
+    }
+    // ---- partial rows of this chunk
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float lt = l[h];
+      lt += __shfl_xor_sync(kAll, lt, 1);
+      lt += __shfl_xor_sync(kAll, lt, 2);
+      if (!real[h]) continue;
+      const int64_t slot = ((int64_t)bs[h] * p.num_heads + head[h]) * p.max_chunks + chunk;
+      float2* dst = reinterpret_cast<float2*>(p.part_o + slot * D + 2 * qc);
+#pragma unroll
+      for (int n = 0; n < NT; ++n) dst[4 * n] = make_float2(o[n][2 * h], o[n][2 * h + 1]);
+      if (qc == 0) p.part_ml[slot] = make_float2(m[h] * c, lt);
+    }
+  }
+}
+
+// One warp per (merge item, group of heads): lanes are (head, 16-byte chunk of
+// the output row). Part 0 is the suffix: its normalised output row with weight
+// 2^lse (acc = row, max = lse, sum = 1); parts 1.. are the prefix chunks.
+template <typename T, int D>
+__global__ void __launch_bounds__(128) cascade_merge_kernel(const CascadeMergeParams p) {
+  constexpr int EPC = Elem<T>::kPerChunk;
+  constexpr int DCH = D / EPC;
+  constexpr int HPW = 32 / DCH;
+  const int lane = threadIdx.x & 31;
+  const int hgroups = (p.num_heads + HPW - 1) / HPW;
+  const int64_t gw = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (gw >= (int64_t)p.num_items * hgroups) return;
+  const int it = (int)(gw / hgroups), hg = (int)(gw % hgroups);
+  const int b = __ldg(&p.items[2 * it]), nch = __ldg(&p.items[2 * it + 1]);
+  const int h = hg * HPW + lane / DCH, cc = lane % DCH;
+  if (lane >= HPW * DCH || h >= p.num_heads || b < 0 || b >= p.batch) return;
+  if (nch < 0 || nch > p.max_chunks) {
+    if (cc == 0) set_error(p.error, kErrBadWork);
+    return;
+  }
+  T* row = static_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + cc * EPC;
+  float o[EPC];
+  Elem<T>::unpack(*reinterpret_cast<const uint4*>(row), o);
+  float M = p.lse[(int64_t)b * p.num_heads + h], L = 1.f;
+  if (M == -INFINITY) {  // empty suffix: the prefix parts alone
+    L = 0.f;
+#pragma unroll
+    for (int e = 0; e < EPC; ++e) o[e] = 0.f;
+  }
+  const int64_t slot0 = ((int64_t)b * p.num_heads + h) * p.max_chunks;
+#pragma unroll 4
+  for (int k = 0; k < nch; ++k) {
+    const float2 ml = __ldcg(&p.part_ml[slot0 + k]);
+    const float4* src = reinterpret_cast<const float4*>(p.part_o + (slot0 + k) * D + cc * EPC);
+    float4 v[EPC / 4];
+#pragma unroll
+    for (int e4 = 0; e4 < EPC / 4; ++e4) v[e4] = __ldcg(src + e4);
+    if (ml.x > M) {
+      const float sc = exp2f(M - ml.x);
+      L *= sc;
+#pragma unroll
+      for (int e = 0; e < EPC; ++e) o[e] *= sc;
+      M = ml.x;
+    }
+    const float wgt = exp2f(ml.x - M);
+    L = fmaf(ml.y, wgt, L);
+#pragma unroll
+    for (int e4 = 0; e4 < EPC / 4; ++e4) {
+      o[4 * e4 + 0] = fmaf(wgt, v[e4].x, o[4 * e4 + 0]);
+      o[4 * e4 + 1] = fmaf(wgt, v[e4].y, o[4 * e4 + 1]);
+      o[4 * e4 + 2] = fmaf(wgt, v[e4].z, o[4 * e4 + 2]);
+      o[4 * e4 + 3] = fmaf(wgt, v[e4].w, o[4 * e4 + 3]);
+    }
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+  for (int e = 0; e < EPC; ++e) o[e] *= inv;
+  *reinterpret_cast<uint4*>(row) = Elem<T>::pack(o);
+}
+
+template <typename T>
+cudaError_t launch_prefix_t(int head_dim, const CascadeParams& p, int smem, cudaStream_t st) {
+  const dim3 grid(p.num_work, p.num_kv_heads), block(kCascadeWarps * 32);
+  auto go = [&](auto kernel) {
+    static int attr_done[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kCascadeMaxSmem);
+      if (e != cudaSuccess) return e;
+      attr_done[dev] = 1;
+    }
+    kernel<<<grid, block, smem, st>>>(p);
+    return cudaGetLastError();
+  };
+  switch (head_dim) {
+    case 64: return go(cascade_prefix_kernel<T, 64>);
+    case 112: return go(cascade_prefix_kernel<T, 112>);
+    case 128: return go(cascade_prefix_kernel<T, 128>);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <typename T>
+cudaError_t launch_merge_t(int head_dim, const CascadeMergeParams& p, cudaStream_t st) {
+  const int dch = head_dim / Elem<T>::kPerChunk, hpw = 32 / dch;
+  const int64_t warps = (int64_t)p.num_items * ((p.num_heads + hpw - 1) / hpw);
+  const int blocks = (int)((warps + 3) / 4);
+  switch (head_dim) {
+    case 64: cascade_merge_kernel<T, 64><<<blocks, 128, 0, st>>>(p); break;
+    case 112: cascade_merge_kernel<T, 112><<<blocks, 128, 0, st>>>(p); break;
+    case 128: cascade_merge_kernel<T, 128><<<blocks, 128, 0, st>>>(p); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+int cascade_smem_bytes(int head_dim, int elem_bytes, int num_pages) {
+  return num_pages * 2 * kBlockSize * tile_row_pitch(head_dim * elem_bytes);
+}
+
+cudaError_t launch_cascade_prefix(int dtype, int head_dim, const CascadeParams& p, cudaStream_t stream) {
+  if (p.num_work == 0) return cudaSuccess;
+  const int smem = cascade_smem_bytes(head_dim, 2, kCascadeMaxPages);
+  return dtype == 1 ? launch_prefix_t<__nv_bfloat16>(head_dim, p, smem, stream)
+                    : launch_prefix_t<__half>(head_dim, p, smem, stream);
+}
+
+cudaError_t launch_cascade_merge(int dtype, int head_dim, const CascadeMergeParams& p, cudaStream_t stream) {
+  if (p.num_items == 0) return cudaSuccess;
+  return dtype == 1 ? launch_merge_t<__nv_bfloat16>(head_dim, p, stream) : launch_merge_t<__half>(head_dim, p, stream);
+}
+
+}  // namespace ubx

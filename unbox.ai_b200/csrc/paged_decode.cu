@@ -39,6 +39,7 @@
 
 #include "ubx_common.cuh"
 #include "ubx_internal.h"
+#include "ubx_mma.cuh"
 #include "ubx_prep.cuh"
 
 namespace ubx {
@@ -109,6 +110,7 @@ __device__ __forceinline__ void write_zero_row(const DecodeParams& p, int b, int
     const int h = head_begin + i / DCH, c = i % DCH;
     T* o = reinterpret_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + c * EPC;
     *reinterpret_cast<uint4*>(o) = make_uint4(0, 0, 0, 0);
+    if (p.lse && c == 0) p.lse[(int64_t)b * p.num_heads + h] = -INFINITY;  // nothing attended
   }
 }
 
@@ -150,6 +152,7 @@ __device__ __forceinline__ void merge_parts(const DecodeParams& p, int b, int h,
     for (int e = 0; e < EPC; ++e) o[e] *= inv;
     T* dst = reinterpret_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + lane * EPC;
     *reinterpret_cast<uint4*>(dst) = Elem<T>::pack(o);
+    if (p.lse && lane == 0) p.lse[(int64_t)b * p.num_heads + h] = M + log2f(L);
   }
 }
 
@@ -202,6 +205,7 @@ __device__ void merge_rows(const DecodeParams& p, int b, int head0, int nh, int 
     for (int e = 0; e < EPC; ++e) o[e] *= inv;
     T* dst = reinterpret_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)head * p.o_sh + c * EPC;
     *reinterpret_cast<uint4*>(dst) = Elem<T>::pack(o);
+    if (p.lse && c == 0) p.lse[(int64_t)b * H + head] = M + log2f(L);
   }
 }
 
@@ -305,47 +309,6 @@ __device__ __forceinline__ void page_update(const T* __restrict__ kt, const T* _
     }
   }
   __syncwarp();
-}
-
-// ---------------------------------------------------------------- tensor-core helpers
-
-// ldmatrix: four 8x8 b16 matrices, row addresses supplied by lanes 8i..8i+7.
-__device__ __forceinline__ void ldsm_x4(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(smem_u32(p)));
-}
-
-__device__ __forceinline__ void ldsm_x4_trans(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                              uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(smem_u32(p)));
-}
-
-// D(16x8, f32) += A(16x16) * B(16x8) (A row-major, B column-major, 16-bit
-// inputs) for an A whose rows 8..15 are zero (the padding rows of a q-head
-// tile): only D rows 0..7 are kept (d[0], d[1] of this lane); rows 8..15 come
-// back as zeros into registers that die at once, so they hold no accumulator.
-template <typename T>
-__device__ __forceinline__ void mma16816_top(float (&d)[2], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
-  float dead0, dead1;
-  const float zero = 0.f;
-  if constexpr (sizeof(T) == 2 && std::is_same<T, __nv_bfloat16>::value) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-        "{%0, %1, %10, %10};"
-        : "+f"(d[0]), "+f"(d[1]), "=f"(dead0), "=f"(dead1)
-        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1), "f"(zero));
-  } else {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-        "{%0, %1, %10, %10};"
-        : "+f"(d[0]), "+f"(d[1]), "=f"(dead0), "=f"(dead1)
-        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1), "f"(zero));
-  }
-  (void)dead0;
-  (void)dead1;
 }
 
 // ---------------------------------------------------------------- shared CTA plumbing
@@ -939,6 +902,7 @@ __device__ void consume_mma(const DecodeParams& p, const Work& w, const Smem& sm
                                                     (int64_t)(head0 + qr) * p.o_sh + 2 * qc);
 #pragma unroll
         for (int n = 0; n < NT; ++n) dst[4 * n] = Elem<T>::pack2(o[n][0] * inv, o[n][1] * inv);
+        if (p.lse && qc == 0) p.lse[(int64_t)s.b * p.num_heads + head0 + qr] = fmaf(m, c, log2f(l));
       }
     } else {
       const int64_t slot = partial_slot<BAL>(p, w, s.b, first_seg);
