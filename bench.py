@@ -61,6 +61,9 @@ def parse():
     ap.add_argument("--prep", action="store_true",
                     help="layer-call = q/k RMSNorm + rotary embedding + KV append + attention in one launch "
                          "(the attention block between the QKV projection and o_proj)")
+    ap.add_argument("--cascade", action="store_true",
+                    help="read pages shared by several requests (radix prefix) once per layer-call: suffix pass, "
+                         "shared-prefix pass and merge (plan built on the host once per step)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     return ap.parse_args()
@@ -178,6 +181,7 @@ def cpu_layer_call(oracle, host):
     return st
 
 
+PLAN_FIELDS = ("suffix_block_table", "suffix_context_lens", "page_list", "member_list", "work", "merge_items")
 HANDOFF_METRIC = "KV hand-off GB/s of page payload (prefill pool -> decode pool)"
 
 
@@ -350,13 +354,15 @@ def bench_handoff(args):
     if world == 1:
         ach = 2 * payload / (per_step_ms / 1e3) / 1e9
         line["roofline"] = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
-                            "frac": round(ach / peak, 4), "traffic": None, "kernel": "kv_pages_copy_kernel",
+                            "frac": round(ach / peak, 4), "traffic": None,
+                            "kernel": "kv_pages_bulk_kernel (TMA bulk load/store ring)",
                             "algorithmic_bytes_per_launch": 2 * payload, "avg_launch_us": round(per_step_ms * 1e3, 2),
                             "peak_source": f"{kind} (MEASURED_PEAKS.json hbm_gbs, read + write bytes)"}
     else:
         ach = payload / (per_step_ms / 1e3) / 1e9
         line["roofline"] = {"bound": "nvlink", "achieved": round(ach, 1), "peak": 770.0, "unit": "GB/s",
-                            "frac": round(ach / 770.0, 4), "traffic": None, "kernel": "kv_pages_copy_kernel",
+                            "frac": round(ach / 770.0, 4), "traffic": None,
+                            "kernel": "kv_pages_copy_kernel (16-byte stores into the peer's pool)",
                             "algorithmic_bytes_per_launch": payload, "avg_launch_us": round(per_step_ms * 1e3, 2),
                             "peak_source": "measured peer copy per direction on this pool (770 GB/s)"}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -456,6 +462,15 @@ def main():
     outs = [[torch.empty_like(d["q"][l]) for l in range(L)] for d in devs]
     if args.prep and args.separate:
         raise SystemExit("--prep runs the fused launch; it does not combine with --separate")
+    if args.cascade and (args.prep or args.separate):
+        raise SystemExit("--cascade runs the fused append; it does not combine with --prep or --separate")
+    plan_ms = 0.0
+    if args.cascade:
+        for d, (_, lay) in zip(devs, parts):
+            t0 = time.perf_counter()
+            d["plan"] = pkg.plan_cascade(lay.block_table, lay.context_lens, lay.num_heads, lay.num_kv_heads,
+                                         device=device)
+            plan_ms += (time.perf_counter() - t0) * 1e3
     rope = None
     if args.prep:
         # per-layer q_norm / k_norm weights near 1 and the model's rotary table
@@ -470,6 +485,8 @@ def main():
         rope = pkg.rope_table(D, 2 * 2048, 500000.0, device=device)
     kw = dict(schedule=args.schedule, split_pages=args.split_pages)
     launches_per_call = (2 if args.separate else 1) + (1 if args.schedule == "split" else 0)
+    if args.cascade and any(d["plan"].num_work for d in devs):
+        launches_per_call += 2
     calls_per_step = L * len(parts)
 
     def layer_call(d, l, q, k_new, v_new, block_table, context_lens, out, slots=None, timer=None):
@@ -480,6 +497,9 @@ def main():
             timer[0].record()
         if args.separate:
             pkg.paged_attention(q, d["k_caches"][l], d["v_caches"][l], block_table, context_lens, out=out, **kw)
+        elif args.cascade:
+            pkg.paged_attention_cascade(q, d["k_caches"][l], d["v_caches"][l], d["plan"], out=out, k_new=k_new,
+                                        v_new=v_new, overlap_previous=args.overlap, schedule=args.schedule)
         elif args.prep:
             pkg.paged_decode_prep_attention(q, k_new, v_new, d["q_w"][l], d["k_w"][l], rope, d["k_caches"][l],
                                             d["v_caches"][l], block_table, context_lens, 1e-6, out=out,
@@ -559,7 +579,7 @@ def main():
     if graph is None:
         t_ms = [a.elapsed_time(b) for row in timers for (a, b) in row]
         kernel_avg_ms = sum(t_ms) / len(t_ms)
-    elif args.prep or (not args.separate and args.schedule != "split"):
+    elif args.prep or args.cascade or (not args.separate and args.schedule != "split"):
         kernel_avg_ms = ms / (args.steps * calls_per_step)  # the step is exactly these launches
     else:
         def attn_only():
@@ -590,6 +610,8 @@ def main():
         dd = {k: torch.empty_like(v, device=device) for k, v in h.items()}
         dd["pos"] = torch.empty_like(h["cl"], device=device)
         dd["slots"] = torch.empty(h["cl"].shape[0], dtype=torch.int64, device=device)
+        if args.cascade:  # the step's prefix plan travels with its block table
+            h["plan"] = {f: getattr(d["plan"], f).cpu().pin_memory() for f in PLAN_FIELDS}
         hosts.append((h, dd))
 
     def e2e_step():
@@ -599,6 +621,10 @@ def main():
             if args.separate:
                 torch.sub(dd["cl"], 1, out=dd["pos"])
                 pkg.slot_mapping(dd["bt"], dd["pos"], glay.block_size, out=dd["slots"])
+        if args.cascade:
+            for (h, dd), d in zip(hosts, devs):
+                for f in PLAN_FIELDS:
+                    getattr(d["plan"], f).copy_(h["plan"][f], non_blocking=True)
         for l in range(L):
             for (h, dd), d in zip(hosts, devs):
                 layer_call(d, l, dd["q"][l], dd["k_new"][l], dd["v_new"][l], dd["bt"], dd["cl"], dd["out"][l],
@@ -623,6 +649,8 @@ def main():
     barrier()
     e2e_ms = reduce(e0.elapsed_time(e1), dist.ReduceOp.MAX)
     h2d = sum(h[k].numel() * h[k].element_size() for h, _ in hosts for k in ("bt", "cl", "q", "k_new", "v_new"))
+    if args.cascade:
+        h2d += sum(t.numel() * t.element_size() for h, _ in hosts for t in h["plan"].values())
     d2h = sum(h["out"].numel() * h["out"].element_size() for h, _ in hosts)
     for (h, _), o in zip(hosts, outs):
         assert torch.equal(h["out"][0].to(device), o[0]), "end-to-end output differs from the device-resident step"
@@ -647,6 +675,8 @@ def main():
         "clocks": clocks.summary(),
         "graph": bool(graph is not None), "append": "separate launch" if args.separate else "fused",
         "prep": "q/k RMSNorm + rotary fused" if args.prep else None,
+        "cascade": ({"groups": sum(len(d["plan"].groups) for d in devs), "plan_host_ms": round(plan_ms, 3),
+                     "shared_tokens": sum(d["plan"].shared_tokens for d in devs)} if args.cascade else None),
         "overlap_previous": bool(args.overlap and not args.separate),
     }
     achieved = kernel_bytes / (kernel_avg_ms / 1e3) / 1e9
@@ -654,9 +684,11 @@ def main():
                         "frac": round(achieved / peak, 4), "traffic": profiled_traffic(args.workload),
                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                         else "fallback 6650 GB/s",
-                        "kernel": "paged_decode_mma_kernel" + ("" if args.separate else
-                                                               " (q/k RMSNorm, rotary, KV append fused)" if args.prep
-                                                               else " (KV append fused)"),
+                        "kernel": ("cascade layer-call: paged_decode_mma_kernel (suffix, KV append fused) + "
+                                   "cascade_prefix_kernel + cascade_merge_kernel" if args.cascade else
+                                   "paged_decode_mma_kernel" + ("" if args.separate else
+                                                                " (q/k RMSNorm, rotary, KV append fused)" if args.prep
+                                                                else " (KV append fused)")),
                         "algorithmic_bytes_per_launch": int(kernel_bytes),
                         "avg_launch_us": round(kernel_avg_ms * 1e3, 2),
                         "timing": "per-launch CUDA events" if graph is None else "graph replay / launches"}

@@ -250,25 +250,25 @@ __global__ void __launch_bounds__(128) cascade_merge_kernel(const CascadeMergePa
 
 template <typename T>
 cudaError_t launch_prefix_t(int head_dim, const CascadeParams& p, int smem, cudaStream_t st) {
-  const dim3 grid(p.num_work, p.num_kv_heads), block(kCascadeWarps * 32);
-  auto go = [&](auto kernel) {
-    static int attr_done[64] = {0};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kCascadeMaxSmem);
-      if (e != cudaSuccess) return e;
-      attr_done[dev] = 1;
-    }
-    kernel<<<grid, block, smem, st>>>(p);
-    return cudaGetLastError();
-  };
+  void (*kernel)(const CascadeParams);
+  int slot;
   switch (head_dim) {
-    case 64: return go(cascade_prefix_kernel<T, 64>);
-    case 112: return go(cascade_prefix_kernel<T, 112>);
-    case 128: return go(cascade_prefix_kernel<T, 128>);
+    case 64: kernel = cascade_prefix_kernel<T, 64>, slot = 0; break;
+    case 112: kernel = cascade_prefix_kernel<T, 112>, slot = 1; break;
+    case 128: kernel = cascade_prefix_kernel<T, 128>, slot = 2; break;
     default: return cudaErrorInvalidValue;
   }
+  // the shared-memory opt-in is per kernel and per device
+  static int attr_done[3][64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_done[slot][dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kCascadeMaxSmem);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) attr_done[slot][dev] = 1;
+  }
+  kernel<<<dim3(p.num_work, p.num_kv_heads), dim3(kCascadeWarps * 32), smem, st>>>(p);
+  return cudaGetLastError();
 }
 
 template <typename T>
