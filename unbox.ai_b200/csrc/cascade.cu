@@ -29,7 +29,6 @@ constexpr unsigned kAll = 0xffffffffu;
 template <typename T, int D>
 __global__ void __launch_bounds__(kCascadeWarps * 32) cascade_prefix_kernel(const CascadeParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint64_t bar;
   constexpr int KS = D / 16;  // QK k-steps
   constexpr int NT = D / 8;   // PV n-tiles
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -44,47 +43,33 @@ __global__ void __launch_bounds__(kCascadeWarps * 32) cascade_prefix_kernel(cons
     return;
   }
   constexpr int kRowBytes = D * (int)sizeof(T);  // one KV head row of one token
+  constexpr int kVecPerRow = kRowBytes / 16;
   const int tile = kBlockSize * p.pitch;          // one page of this head, K or V
   uint8_t* k_s = smem;
   uint8_t* v_s = smem + n_pg * tile;
-  if (threadIdx.x == 0) {
-    mbar_init(&bar, 32);
-    fence_mbar_init();
-  }
-  __syncthreads();
 
-  // ---- load: warp 0, lane = (K|V, token row); one bulk copy per row and page
-  if (warp == 0) {
-    const int r = lane & 15;
-    uint8_t* base = lane < 16 ? k_s : v_s;
-    const uint8_t* pool = static_cast<const uint8_t*>(lane < 16 ? p.k_cache : p.v_cache);
-    uint32_t bytes = 0;
-    for (int i = 0; i < n_pg; ++i) {
-      const int page = __ldg(&p.page_list[pg_off + i]);
-      if (page >= 0 && (int64_t)page < p.num_blocks) {
-        bytes += kRowBytes;
-      } else {
-        if (r == 0) set_error(p.error, kErrBadPage);
-        uint4* row = reinterpret_cast<uint4*>(base + i * tile + r * p.pitch);
-        for (int c = 0; c < kRowBytes / 16; ++c) row[c] = make_uint4(0, 0, 0, 0);
-      }
-    }
-    mbar_arrive_expect_tx(&bar, bytes);
-    for (int i = 0; i < n_pg; ++i) {
-      const int page = __ldg(&p.page_list[pg_off + i]);
-      if (page >= 0 && (int64_t)page < p.num_blocks)
-        bulk_copy_g2s(base + i * tile + r * p.pitch,
-                      pool + ((int64_t)page * p.c_sblk + (int64_t)r * p.c_stok + (int64_t)kvh * D) * sizeof(T),
-                      kRowBytes, &bar);
+  // ---- load: every thread copies 16-byte pieces of the chunk's K and V rows of
+  // this head (cp.async, no register staging); rows of a bad page are zeroed
+  const int total = n_pg * 2 * kBlockSize * kVecPerRow;
+  for (int v = threadIdx.x; v < total; v += kCascadeWarps * 32) {
+    const int row = v / kVecPerRow, cv = v - row * kVecPerRow;
+    const int i = row / (2 * kBlockSize), r = row % (2 * kBlockSize);
+    const bool is_v = r >= kBlockSize;
+    const int tok = r & (kBlockSize - 1);
+    uint8_t* dst = (is_v ? v_s : k_s) + i * tile + tok * p.pitch + cv * 16;
+    const int page = __ldg(&p.page_list[pg_off + i]);
+    if (page >= 0 && (int64_t)page < p.num_blocks) {
+      const uint8_t* src = static_cast<const uint8_t*>(is_v ? p.v_cache : p.k_cache) +
+                           ((int64_t)page * p.c_sblk + (int64_t)tok * p.c_stok + (int64_t)kvh * D) * sizeof(T) +
+                           cv * 16;
+      cp_async_16(dst, src);
+    } else {
+      if (tok == 0 && cv == 0 && !is_v) set_error(p.error, kErrBadPage);
+      *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
     }
   }
-  if (!mbar_wait_bounded(&bar, 0)) {
-    if (threadIdx.x == 0) {
-      set_error(p.error, kErrTimeout);
-      mbar_wait_bounded(&bar, 0);  // give the copies in flight one more bound before the CTA exits
-    }
-    return;
-  }
+  cp_async_commit_wait_all();
+  __syncthreads();
 
   // ---- tiles: 16 rows = (request, query head), request-major; G heads x 16/G requests
   const int MT = 16 / G;
@@ -188,58 +173,54 @@ __global__ void __launch_bounds__(kCascadeWarps * 32) cascade_prefix_kernel(cons
   }
 }
 
-// One warp per (merge item, group of heads): lanes are (head, 16-byte chunk of
-// the output row). Part 0 is the suffix: its normalised output row with weight
-// 2^lse (acc = row, max = lse, sum = 1); parts 1.. are the prefix chunks.
+// One warp per (merge item, query head). Part 0 is the suffix pass: its
+// normalised output row with weight 2^lse (acc = row, max = lse, sum = 1);
+// parts 1.. are the prefix chunks. The lanes first read every part's (max, sum)
+// in parallel for the common max and the denominator, then lanes = 16-byte
+// output chunks add the weighted rows, all parts' loads independent.
 template <typename T, int D>
 __global__ void __launch_bounds__(128) cascade_merge_kernel(const CascadeMergeParams p) {
   constexpr int EPC = Elem<T>::kPerChunk;
   constexpr int DCH = D / EPC;
-  constexpr int HPW = 32 / DCH;
   const int lane = threadIdx.x & 31;
-  const int hgroups = (p.num_heads + HPW - 1) / HPW;
   const int64_t gw = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
-  if (gw >= (int64_t)p.num_items * hgroups) return;
-  const int it = (int)(gw / hgroups), hg = (int)(gw % hgroups);
+  if (gw >= (int64_t)p.num_items * p.num_heads) return;
+  const int it = (int)(gw / p.num_heads), h = (int)(gw % p.num_heads);
   const int b = __ldg(&p.items[2 * it]), nch = __ldg(&p.items[2 * it + 1]);
-  const int h = hg * HPW + lane / DCH, cc = lane % DCH;
-  if (lane >= HPW * DCH || h >= p.num_heads || b < 0 || b >= p.batch) return;
-  if (nch < 0 || nch > p.max_chunks) {
-    if (cc == 0) set_error(p.error, kErrBadWork);
+  if (b < 0 || b >= p.batch || nch < 0 || nch > p.max_chunks) {
+    if (lane == 0) set_error(p.error, kErrBadWork);
     return;
   }
-  T* row = static_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + cc * EPC;
+  const int64_t slot0 = ((int64_t)b * p.num_heads + h) * p.max_chunks;
+  const float lse = p.lse[(int64_t)b * p.num_heads + h];  // -inf: empty suffix
+  float M = lse;
+  for (int k = lane; k < nch; k += 32) M = fmaxf(M, __ldcg(&p.part_ml[slot0 + k]).x);
+  M = warp_max(M);
+  float L = 0.f;
+  for (int k = lane; k < nch; k += 32) {
+    const float2 ml = __ldcg(&p.part_ml[slot0 + k]);
+    L = fmaf(ml.y, exp2f(ml.x - M), L);
+  }
+  L = warp_sum(L);
+  const float w_s = lse == -INFINITY ? 0.f : exp2f(lse - M);  // 0 for an empty suffix
+  L += w_s;
+  if (lane >= DCH) return;
+  T* row = static_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + lane * EPC;
   float o[EPC];
   Elem<T>::unpack(*reinterpret_cast<const uint4*>(row), o);
-  float M = p.lse[(int64_t)b * p.num_heads + h], L = 1.f;
-  if (M == -INFINITY) {  // empty suffix: the prefix parts alone
-    L = 0.f;
 #pragma unroll
-    for (int e = 0; e < EPC; ++e) o[e] = 0.f;
-  }
-  const int64_t slot0 = ((int64_t)b * p.num_heads + h) * p.max_chunks;
+  for (int e = 0; e < EPC; ++e) o[e] *= w_s;
 #pragma unroll 4
   for (int k = 0; k < nch; ++k) {
-    const float2 ml = __ldcg(&p.part_ml[slot0 + k]);
-    const float4* src = reinterpret_cast<const float4*>(p.part_o + (slot0 + k) * D + cc * EPC);
-    float4 v[EPC / 4];
-#pragma unroll
-    for (int e4 = 0; e4 < EPC / 4; ++e4) v[e4] = __ldcg(src + e4);
-    if (ml.x > M) {
-      const float sc = exp2f(M - ml.x);
-      L *= sc;
-#pragma unroll
-      for (int e = 0; e < EPC; ++e) o[e] *= sc;
-      M = ml.x;
-    }
-    const float wgt = exp2f(ml.x - M);
-    L = fmaf(ml.y, wgt, L);
+    const float wgt = exp2f(__ldcg(&p.part_ml[slot0 + k]).x - M);
+    const float4* src = reinterpret_cast<const float4*>(p.part_o + (slot0 + k) * D + lane * EPC);
 #pragma unroll
     for (int e4 = 0; e4 < EPC / 4; ++e4) {
-      o[4 * e4 + 0] = fmaf(wgt, v[e4].x, o[4 * e4 + 0]);
-      o[4 * e4 + 1] = fmaf(wgt, v[e4].y, o[4 * e4 + 1]);
-      o[4 * e4 + 2] = fmaf(wgt, v[e4].z, o[4 * e4 + 2]);
-      o[4 * e4 + 3] = fmaf(wgt, v[e4].w, o[4 * e4 + 3]);
+      const float4 v = __ldcg(src + e4);
+      o[4 * e4 + 0] = fmaf(wgt, v.x, o[4 * e4 + 0]);
+      o[4 * e4 + 1] = fmaf(wgt, v.y, o[4 * e4 + 1]);
+      o[4 * e4 + 2] = fmaf(wgt, v.z, o[4 * e4 + 2]);
+      o[4 * e4 + 3] = fmaf(wgt, v.w, o[4 * e4 + 3]);
     }
   }
   const float inv = L > 0.f ? 1.f / L : 0.f;
@@ -273,8 +254,7 @@ cudaError_t launch_prefix_t(int head_dim, const CascadeParams& p, int smem, cuda
 
 template <typename T>
 cudaError_t launch_merge_t(int head_dim, const CascadeMergeParams& p, cudaStream_t st) {
-  const int dch = head_dim / Elem<T>::kPerChunk, hpw = 32 / dch;
-  const int64_t warps = (int64_t)p.num_items * ((p.num_heads + hpw - 1) / hpw);
+  const int64_t warps = (int64_t)p.num_items * p.num_heads;
   const int blocks = (int)((warps + 3) / 4);
   switch (head_dim) {
     case 64: cascade_merge_kernel<T, 64><<<blocks, 128, 0, st>>>(p); break;

@@ -132,6 +132,19 @@ __device__ __forceinline__ void bulk_wait_group() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// 16-byte global -> shared copy without register staging (cp.async, L2 only);
+// both addresses 16-byte aligned.
+__device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+               ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(gmem_src))
+               : "memory");
+}
+
+// Closes this thread's cp.async copies into a group and waits until all are done.
+__device__ __forceinline__ void cp_async_commit_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- elements
 template <typename T>
 struct Elem;
