@@ -181,7 +181,7 @@ def cpu_layer_call(oracle, host):
     return st
 
 
-PLAN_FIELDS = ("suffix_block_table", "suffix_context_lens", "page_list", "member_list", "work")
+PLAN_FIELDS = ("suffix_block_table", "suffix_context_lens", "page_list", "member_list", "work", "merge_items")
 HANDOFF_METRIC = "KV hand-off GB/s of page payload (prefill pool -> decode pool)"
 
 
@@ -487,7 +487,7 @@ def main():
     kw = dict(schedule=args.schedule, split_pages=args.split_pages)
     launches_per_call = (2 if args.separate else 1) + (1 if args.schedule == "split" else 0)
     if args.cascade and any(d["plan"].num_work for d in devs):
-        launches_per_call += 1
+        launches_per_call += 2
     calls_per_step = L * len(parts)
 
     def layer_call(d, l, q, k_new, v_new, block_table, context_lens, out, slots=None, timer=None):
@@ -686,7 +686,7 @@ def main():
                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                         else "fallback 6650 GB/s",
                         "kernel": ("cascade layer-call: paged_decode_mma_kernel (suffix, KV append fused) + "
-                                   "cascade_prefix_kernel (shared pages, merge fused)" if args.cascade else
+                                   "cascade_prefix_kernel + cascade_merge_kernel" if args.cascade else
                                    "paged_decode_mma_kernel" + ("" if args.separate else
                                                                 " (q/k RMSNorm, rotary, KV append fused)" if args.prep
                                                                 else " (KV append fused)")),

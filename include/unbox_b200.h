@@ -48,7 +48,7 @@ extern "C" {
 #define UBX_DEVERR_TIMEOUT 8       /* a pipeline wait exceeded its bound; output undefined */
 #define UBX_DEVERR_BAD_SLOT 16     /* kv_append slot >= num_blocks * block_size: row skipped */
 #define UBX_DEVERR_BAD_POSITION 32 /* rotary position outside [0, rope_positions): row left unrotated */
-#define UBX_DEVERR_BAD_WORK 64     /* cascade work item out of range: item skipped */
+#define UBX_DEVERR_BAD_WORK 64     /* cascade work or merge item out of range: item skipped */
 
 /* work schedules of the attention kernel */
 #define UBX_SCHEDULE_AUTO 0     /* library picks */
@@ -250,30 +250,29 @@ int ubx_paged_decode_attention_lse(const void* k_new, const void* v_new, int64_t
  *   2. ubx_cascade_prefix_attention: for each work item and KV head, one CTA
  *      loads up to 8 shared pages of that head once and runs all the item's
  *      requests over them in 16-row tensor-core tiles, writing per-chunk partials
- *      into the cascade workspace; the last chunk to finish a (request, KV head)
- *      merges the partials into that request's rows of out (in place).
+ *      into the cascade workspace;
+ *   3. ubx_cascade_merge: out[b, h] = merge(suffix row with weight 2^lse, chunk partials).
  * Replaces, for those requests, the per-request re-reading of shared pages in
  * paged_decode_attention_ref (unbox_platform/infer/kernels/paged_decode_attention.py:157-191).
  *   page_list:   int32, the shared page ids of every group, concatenated
  *   member_list: int32, the member sequences of every group, concatenated
  *   work_items:  int32 [num_work_items][6] = (member offset, member count, page
- *                offset, page count <= 8, chunk index, chunks of the group
- *                <= max_chunks); member count * (num_heads / num_kv_heads) <= 128;
- *                every (member, chunk) pair of a group in exactly one item
- *   lse, out:    the suffix pass's outputs for the same batch
- *   cascade_ws:  ubx_cascade_workspace_size bytes; its first 256 KiB (the
- *                per-(request, KV head) counters) must be zero before the first
- *                call, the kernel leaves them zero
- * bf16/f16, head_dim 64/112/128, page 16, GQA 1/2/4/8, batch * num_kv_heads <= 65536.
+ *                offset, page count <= 8, chunk index < max_chunks, 0); member
+ *                count * (num_heads / num_kv_heads) <= 128
+ *   merge_items: int32 [num_merge_items][2] = (sequence, number of its prefix chunks)
+ *   cascade_ws:  ubx_cascade_workspace_size bytes (no initialisation needed)
+ * bf16/f16, head_dim 64/112/128, page 16, GQA 1/2/4/8.
  */
 int ubx_cascade_workspace_size(int batch, int num_heads, int head_dim, int max_chunks, size_t* bytes);
 int ubx_cascade_prefix_attention(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache,
                                  const void* v_cache, int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head,
                                  int64_t num_blocks, const int32_t* page_list, const int32_t* member_list,
-                                 const int32_t* work_items, int num_work_items, int max_chunks, const float* lse,
-                                 void* out, int64_t o_s_b, int64_t o_s_h, int batch, int num_heads,
-                                 int num_kv_heads, int head_dim, float scale, int dtype, void* cascade_ws,
-                                 size_t cascade_ws_bytes, int32_t* error_word, void* stream);
+                                 const int32_t* work_items, int num_work_items, int max_chunks, int batch,
+                                 int num_heads, int num_kv_heads, int head_dim, float scale, int dtype,
+                                 void* cascade_ws, size_t cascade_ws_bytes, int32_t* error_word, void* stream);
+int ubx_cascade_merge(void* out, int64_t o_s_b, int64_t o_s_h, const float* lse, const int32_t* merge_items,
+                      int num_merge_items, int max_chunks, int batch, int num_heads, int head_dim, int dtype,
+                      const void* cascade_ws, size_t cascade_ws_bytes, int32_t* error_word, void* stream);
 
 /*
  * KV hand-off between a prefill worker and a decode worker.

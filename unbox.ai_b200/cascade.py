@@ -12,10 +12,10 @@ groups of requests whose block-table rows start with the same pages, and
                     attention of b over the group's shared pages )
 
 with one launch for every request's suffix (the balanced decode kernel, KV
-append fused, returning log-sum-exps) and one launch for all groups' shared
-pages (each page chunk of a KV head loaded into shared memory once for all the
-group's requests, tensor-core tiles of 16 (request, head) rows; the last chunk
-of a request merges it into the output). Softmax splits exactly over disjoint key sets, so the result is the
+append fused, returning log-sum-exps), one launch for all groups' shared pages
+(each page chunk of a KV head loaded into shared memory once for all the
+group's requests, tensor-core tiles of 16 (request, head) rows), and one merge
+launch. Softmax splits exactly over disjoint key sets, so the result is the
 attention over the whole context.
 """
 from __future__ import annotations
@@ -42,8 +42,8 @@ class CascadePlan:
     suffix_context_lens: torch.Tensor  # (B,) int32: context minus the shared tokens
     page_list: torch.Tensor            # int32: shared pages of every group
     member_list: torch.Tensor          # int32: member sequences of every group
-    work: torch.Tensor                 # (W, 6) int32: members, pages, chunk, chunks of the group
-    merge_items: torch.Tensor          # (M, 2) int32: (sequence, prefix chunks), for inspection
+    work: torch.Tensor                 # (W, 6) int32
+    merge_items: torch.Tensor          # (M, 2) int32: (sequence, prefix chunks)
     max_chunks: int
     groups: list = field(default_factory=list)   # host: (members, shared pages) per group
     shared_tokens: int = 0             # tokens the shared pages hold, once per group
@@ -103,7 +103,7 @@ def plan_cascade(block_table, context_lens, num_heads: int, num_kv_heads: int, b
             np_c = min(MAX_CHUNK_PAGES, P - p0)
             for m0 in range(0, mem.size, max_members):
                 nm = min(max_members, mem.size - m0)
-                work.append((m_off + m0, nm, pg_off + p0, np_c, c, n_chunks))
+                work.append((m_off + m0, nm, pg_off + p0, np_c, c, 0))
         merge.extend((int(b), n_chunks) for b in mem)
         suffix_bt[mem, :MB - P] = bt[mem, P:]
         suffix_bt[mem, MB - P:] = -1
@@ -132,7 +132,7 @@ def paged_attention_cascade(q: torch.Tensor, k_cache: torch.Tensor, v_cache: tor
                             schedule: str = "auto", overlap_previous: bool = False) -> torch.Tensor:
     """Paged decode attention (with the KV append when k_new/v_new are given) using
     ``plan``: same result as ``paged_attention`` over the original block tables,
-    two launches (suffix, shared prefix with the merge). bf16/f16."""
+    three launches (suffix, shared prefix, merge). bf16/f16."""
     dev = _require_cuda(q, k_cache, v_cache)
     if q.dtype not in (torch.bfloat16, torch.float16) or k_cache.dtype != q.dtype or v_cache.dtype != q.dtype:
         raise TypeError("the cascade path is built for bf16/f16 (use paged_attention for fp32)")
@@ -159,8 +159,7 @@ def paged_attention_cascade(q: torch.Tensor, k_cache: torch.Tensor, v_cache: tor
     need = ctypes.c_size_t(0)
     _L.check(lib.ubx_cascade_workspace_size(B, H, D, plan.max_chunks, ctypes.byref(need)), "cascade workspace")
     if plan._ws is None or plan._ws.numel() < need.value or plan._ws.device != dev:
-        # zeroed: its leading (request, KV head) counters must start at zero (the kernel re-arms them)
-        plan._ws = torch.zeros(max(int(need.value), 256), dtype=torch.uint8, device=dev)
+        plan._ws = torch.empty(max(int(need.value), 256), dtype=torch.uint8, device=dev)
     dws = workspace_for(dev)
     buf = dws.ensure(B, H, D, sbt.shape[1], 0)
     st_ = _stream(dev)
@@ -184,8 +183,11 @@ def paged_attention_cascade(q: torch.Tensor, k_cache: torch.Tensor, v_cache: tor
         st = lib.ubx_cascade_prefix_attention(
             q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0),
             k_cache.stride(1), k_cache.stride(2), NB, plan.page_list.data_ptr(), plan.member_list.data_ptr(),
-            plan.work.data_ptr(), plan.num_work, plan.max_chunks, plan._lse.data_ptr(), out.data_ptr(),
-            out.stride(0), out.stride(1), B, H, KVH, D, float(scale), dt, plan._ws.data_ptr(), plan._ws.numel(),
-            dws.error_word_ptr(), st_)
+            plan.work.data_ptr(), plan.num_work, plan.max_chunks, B, H, KVH, D, float(scale), dt,
+            plan._ws.data_ptr(), plan._ws.numel(), dws.error_word_ptr(), st_)
         _L.check(st, "cascade prefix pass")
+        st = lib.ubx_cascade_merge(out.data_ptr(), out.stride(0), out.stride(1), plan._lse.data_ptr(),
+                                   plan.merge_items.data_ptr(), plan.num_merge, plan.max_chunks, B, H, D, dt,
+                                   plan._ws.data_ptr(), plan._ws.numel(), dws.error_word_ptr(), st_)
+        _L.check(st, "cascade merge")
     return out

@@ -524,13 +524,12 @@ int ubx_paged_decode_attention_lse(const void* k_new, const void* v_new, int64_t
 static size_t cascade_ml_bytes(int batch, int num_heads, int max_chunks) {
   return align256((size_t)batch * num_heads * max_chunks * sizeof(float2));
 }
-static constexpr size_t kCascadeCounterBytes = (size_t)kCascadeCounters * sizeof(int32_t);
 
 int ubx_cascade_workspace_size(int batch, int num_heads, int head_dim, int max_chunks, size_t* bytes) {
   g_last_error.clear();
   if (!bytes || batch < 0 || num_heads <= 0 || head_dim <= 0 || max_chunks < 0)
     return fail(UBX_ERR_INVALID_ARGUMENT, "bad cascade workspace query");
-  *bytes = kCascadeCounterBytes + cascade_ml_bytes(batch, num_heads, max_chunks) +
+  *bytes = cascade_ml_bytes(batch, num_heads, max_chunks) +
            (size_t)batch * num_heads * max_chunks * head_dim * sizeof(float);
   return UBX_OK;
 }
@@ -538,26 +537,23 @@ int ubx_cascade_workspace_size(int batch, int num_heads, int head_dim, int max_c
 int ubx_cascade_prefix_attention(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache,
                                  const void* v_cache, int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head,
                                  int64_t num_blocks, const int32_t* page_list, const int32_t* member_list,
-                                 const int32_t* work_items, int num_work_items, int max_chunks, const float* lse,
-                                 void* out, int64_t o_s_b, int64_t o_s_h, int batch, int num_heads,
-                                 int num_kv_heads, int head_dim, float scale, int dtype, void* cascade_ws,
-                                 size_t cascade_ws_bytes, int32_t* error_word, void* stream) {
+                                 const int32_t* work_items, int num_work_items, int max_chunks, int batch,
+                                 int num_heads, int num_kv_heads, int head_dim, float scale, int dtype,
+                                 void* cascade_ws, size_t cascade_ws_bytes, int32_t* error_word, void* stream) {
   g_last_error.clear();
   int st = check_shape(num_heads, num_kv_heads, head_dim, kBlockSize, dtype);
   if (st != UBX_OK) return st;
   if (dtype == UBX_DTYPE_F32) return fail(UBX_ERR_UNSUPPORTED, "the cascade pass is built for bf16/f16");
   if (num_work_items < 0 || max_chunks <= 0 || batch <= 0 || num_blocks <= 0)
     return fail(UBX_ERR_INVALID_ARGUMENT, "bad cascade sizes");
-  if ((int64_t)batch * num_kv_heads > kCascadeCounters)
-    return fail(UBX_ERR_UNSUPPORTED, "batch * num_kv_heads above %d", kCascadeCounters);
   if (num_work_items == 0) return UBX_OK;
-  if (!q || !k_cache || !v_cache || !page_list || !member_list || !work_items || !cascade_ws || !lse || !out)
+  if (!q || !k_cache || !v_cache || !page_list || !member_list || !work_items || !cascade_ws)
     return fail(UBX_ERR_INVALID_ARGUMENT, "null pointer");
   const int es = 2;
   auto m16 = [&](int64_t s) { return ((s * es) & 15) == 0; };
   if (!aligned16(q) || !m16(q_s_b) || !m16(q_s_h) || !aligned16(k_cache) || !aligned16(v_cache) ||
-      !m16(c_s_block) || !m16(c_s_tok) || !aligned16(out) || !m16(o_s_b) || !m16(o_s_h))
-    return fail(UBX_ERR_INVALID_ARGUMENT, "q / out rows and K/V caches must be 16-byte aligned");
+      !m16(c_s_block) || !m16(c_s_tok))
+    return fail(UBX_ERR_INVALID_ARGUMENT, "q rows and K/V caches must be 16-byte aligned");
   if (c_s_head != head_dim) return fail(UBX_ERR_UNSUPPORTED, "KV heads must be contiguous within a token row");
   size_t need = 0;
   ubx_cascade_workspace_size(batch, num_heads, head_dim, max_chunks, &need);
@@ -584,16 +580,48 @@ int ubx_cascade_prefix_attention(const void* q, int64_t q_s_b, int64_t q_s_h, co
   p.scale_log2 = scale * 1.4426950408889634f;
   p.pitch = tile_row_pitch(head_dim * es);
   uint8_t* ws = static_cast<uint8_t*>(cascade_ws);
-  p.counters = reinterpret_cast<int32_t*>(ws);
-  p.part_ml = reinterpret_cast<float2*>(ws + kCascadeCounterBytes);
-  p.part_o = reinterpret_cast<float*>(ws + kCascadeCounterBytes + cascade_ml_bytes(batch, num_heads, max_chunks));
+  p.part_ml = reinterpret_cast<float2*>(ws);
+  p.part_o = reinterpret_cast<float*>(ws + cascade_ml_bytes(batch, num_heads, max_chunks));
+  p.error = error_word;
+  cudaError_t e = launch_cascade_prefix(dtype, head_dim, p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cascade prefix launch");
+  return UBX_OK;
+}
+
+int ubx_cascade_merge(void* out, int64_t o_s_b, int64_t o_s_h, const float* lse, const int32_t* merge_items,
+                      int num_merge_items, int max_chunks, int batch, int num_heads, int head_dim, int dtype,
+                      const void* cascade_ws, size_t cascade_ws_bytes, int32_t* error_word, void* stream) {
+  g_last_error.clear();
+  if (dtype != UBX_DTYPE_BF16 && dtype != UBX_DTYPE_F16)
+    return fail(UBX_ERR_UNSUPPORTED, "the cascade merge is built for bf16/f16");
+  if (head_dim != 64 && head_dim != 112 && head_dim != 128)
+    return fail(UBX_ERR_UNSUPPORTED, "head_dim %d not built (64, 112, 128)", head_dim);
+  if (num_merge_items < 0 || max_chunks <= 0 || batch <= 0 || num_heads <= 0)
+    return fail(UBX_ERR_INVALID_ARGUMENT, "bad merge sizes");
+  if (num_merge_items == 0) return UBX_OK;
+  if (!out || !lse || !merge_items || !cascade_ws) return fail(UBX_ERR_INVALID_ARGUMENT, "null pointer");
+  auto m16 = [&](int64_t s) { return ((s * 2) & 15) == 0; };
+  if (!aligned16(out) || !m16(o_s_b) || !m16(o_s_h)) return fail(UBX_ERR_INVALID_ARGUMENT, "out rows must be 16-byte aligned");
+  size_t need = 0;
+  ubx_cascade_workspace_size(batch, num_heads, head_dim, max_chunks, &need);
+  if (cascade_ws_bytes < need)
+    return fail(UBX_ERR_WORKSPACE, "cascade workspace of %zu bytes, this call needs %zu", cascade_ws_bytes, need);
+  CascadeMergeParams p;
   p.out = out;
   p.o_sb = o_s_b;
   p.o_sh = o_s_h;
   p.lse = lse;
+  p.items = merge_items;
+  p.num_items = num_merge_items;
+  p.batch = batch;
+  p.num_heads = num_heads;
+  p.max_chunks = max_chunks;
+  const uint8_t* ws = static_cast<const uint8_t*>(cascade_ws);
+  p.part_ml = reinterpret_cast<const float2*>(ws);
+  p.part_o = reinterpret_cast<const float*>(ws + cascade_ml_bytes(batch, num_heads, max_chunks));
   p.error = error_word;
-  cudaError_t e = launch_cascade_prefix(dtype, head_dim, p, static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) return cuda_fail(e, "cascade prefix launch");
+  cudaError_t e = launch_cascade_merge(dtype, head_dim, p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cascade merge launch");
   return UBX_OK;
 }
 

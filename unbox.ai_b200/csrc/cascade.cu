@@ -12,10 +12,8 @@
 //      tile of (request, query head) rows of that group over them (mma.sync
 //      m16n8k16, full tiles: G query heads x 16/G requests), writing unnormalised
 //      partial (acc, max, sum) rows per chunk;
-//   3. the last chunk to finish a (request, KV head) -- an atomic counter, no
-//      waiting -- merges the suffix output with the chunks' partials by
-//      log-sum-exp weights (the same combination the split-KV path uses), so the
-//      merge runs inside the prefix pass, on partials still in L2.
+//   3. cascade_merge_kernel merges the suffix output with the chunks' partials by
+//      log-sum-exp weights (the same combination the split-KV path uses).
 // The result equals attention over the whole context (softmax is exactly
 // decomposable over disjoint key sets).
 #include "ubx_common.cuh"
@@ -28,55 +26,6 @@ namespace {
 
 constexpr unsigned kAll = 0xffffffffu;
 
-// Merge of heads head0 .. head0 + G - 1 of sequence b (whole warp): the suffix
-// pass's normalised row with weight 2^lse (acc = row, max = lse, sum = 1) and
-// the nch prefix-chunk partials. Lanes are (head, 16-byte output chunk); each
-// lane reads every part's (max, sum) itself, the row loads of all parts are
-// independent of one another.
-template <typename T, int D>
-__device__ void merge_member(const CascadeParams& p, int b, int head0, int G, int nch, int lane) {
-  constexpr int EPC = Elem<T>::kPerChunk;
-  constexpr int DCH = D / EPC;  // output chunks per row
-  constexpr int HPW = 32 / DCH; // heads per pass of the warp
-  for (int hb = 0; hb < G; hb += HPW) {
-    const int g = hb + lane / DCH, cc = lane % DCH;
-    if (lane >= HPW * DCH || g >= G) continue;  // no warp collectives below
-    const int h = head0 + g;
-    const int64_t slot0 = ((int64_t)b * p.num_heads + h) * p.max_chunks;
-    const float lse = p.lse[(int64_t)b * p.num_heads + h];  // -inf: empty suffix
-    float M = lse;
-    for (int k = 0; k < nch; ++k) M = fmaxf(M, __ldcg(&p.part_ml[slot0 + k]).x);
-    const float w_s = lse == -INFINITY ? 0.f : exp2f(lse - M);
-    float L = w_s;
-    T* row = static_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + cc * EPC;
-    float o[EPC];
-    Elem<T>::unpack(*reinterpret_cast<const uint4*>(row), o);
-#pragma unroll
-    for (int e = 0; e < EPC; ++e) o[e] *= w_s;
-#pragma unroll 4
-    for (int k = 0; k < nch; ++k) {
-      const float2 ml = __ldcg(&p.part_ml[slot0 + k]);
-      const float4* src = reinterpret_cast<const float4*>(p.part_o + (slot0 + k) * D + cc * EPC);
-      float4 v[EPC / 4];
-#pragma unroll
-      for (int e4 = 0; e4 < EPC / 4; ++e4) v[e4] = __ldcg(src + e4);
-      const float wgt = exp2f(ml.x - M);
-      L = fmaf(ml.y, wgt, L);
-#pragma unroll
-      for (int e4 = 0; e4 < EPC / 4; ++e4) {
-        o[4 * e4 + 0] = fmaf(wgt, v[e4].x, o[4 * e4 + 0]);
-        o[4 * e4 + 1] = fmaf(wgt, v[e4].y, o[4 * e4 + 1]);
-        o[4 * e4 + 2] = fmaf(wgt, v[e4].z, o[4 * e4 + 2]);
-        o[4 * e4 + 3] = fmaf(wgt, v[e4].w, o[4 * e4 + 3]);
-      }
-    }
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-#pragma unroll
-    for (int e = 0; e < EPC; ++e) o[e] *= inv;
-    *reinterpret_cast<uint4*>(row) = Elem<T>::pack(o);
-  }
-}
-
 template <typename T, int D>
 __global__ void __launch_bounds__(kCascadeWarps * 32) cascade_prefix_kernel(const CascadeParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -86,10 +35,10 @@ __global__ void __launch_bounds__(kCascadeWarps * 32) cascade_prefix_kernel(cons
   const int kvh = blockIdx.y;
   const int32_t* item = p.work + kCascadeWorkInts * blockIdx.x;
   const int m_off = __ldg(item + 0), n_mem = __ldg(item + 1), pg_off = __ldg(item + 2), n_pg = __ldg(item + 3),
-            chunk = __ldg(item + 4), nch = __ldg(item + 5);
+            chunk = __ldg(item + 4);
   const int G = p.num_heads / p.num_kv_heads;
   if (n_pg < 1 || n_pg > kCascadeMaxPages || n_mem < 1 || n_mem * G > kCascadeWarps * 16 || chunk < 0 ||
-      nch > p.max_chunks || chunk >= nch) {
+      chunk >= p.max_chunks) {
     if (threadIdx.x == 0) set_error(p.error, kErrBadWork);
     return;
   }
@@ -221,26 +170,63 @@ __global__ void __launch_bounds__(kCascadeWarps * 32) cascade_prefix_kernel(cons
       for (int n = 0; n < NT; ++n) dst[4 * n] = make_float2(o[n][2 * h], o[n][2 * h + 1]);
       if (qc == 0) p.part_ml[slot] = make_float2(m[h] * c, lt);
     }
-    // ---- the last chunk of a (request, KV head) to finish merges it
-    __threadfence();
-    __syncwarp();
-    int bj = -1, last = 0;
-    if (lane < MT && t * MT + lane < n_mem) {
-      bj = __ldg(&p.member_list[m_off + t * MT + lane]);
-      if (bj >= 0 && bj < p.batch) {
-        int32_t* ctr = &p.counters[(int64_t)bj * p.num_kv_heads + kvh];
-        last = atomicAdd(ctr, 1) == nch - 1;
-        if (last) atomicExch(ctr, 0);  // re-armed for the next call
-      }
-    }
-    unsigned todo = __ballot_sync(kAll, last);
-    if (todo) __threadfence();
-    while (todo) {
-      const int j = __ffs(todo) - 1;
-      todo &= todo - 1;
-      merge_member<T, D>(p, __shfl_sync(kAll, bj, j), kvh * G, G, nch, lane);
+  }
+}
+
+// One warp per (merge item, query head). Part 0 is the suffix pass: its
+// normalised output row with weight 2^lse (acc = row, max = lse, sum = 1);
+// parts 1.. are the prefix chunks. The lanes first read every part's (max, sum)
+// in parallel for the common max and the denominator, then lanes = 16-byte
+// output chunks add the weighted rows, all parts' loads independent.
+template <typename T, int D>
+__global__ void __launch_bounds__(128) cascade_merge_kernel(const CascadeMergeParams p) {
+  constexpr int EPC = Elem<T>::kPerChunk;
+  constexpr int DCH = D / EPC;
+  const int lane = threadIdx.x & 31;
+  const int64_t gw = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (gw >= (int64_t)p.num_items * p.num_heads) return;
+  const int it = (int)(gw / p.num_heads), h = (int)(gw % p.num_heads);
+  const int b = __ldg(&p.items[2 * it]), nch = __ldg(&p.items[2 * it + 1]);
+  if (b < 0 || b >= p.batch || nch < 0 || nch > p.max_chunks) {
+    if (lane == 0) set_error(p.error, kErrBadWork);
+    return;
+  }
+  const int64_t slot0 = ((int64_t)b * p.num_heads + h) * p.max_chunks;
+  const float lse = p.lse[(int64_t)b * p.num_heads + h];  // -inf: empty suffix
+  float M = lse;
+  for (int k = lane; k < nch; k += 32) M = fmaxf(M, __ldcg(&p.part_ml[slot0 + k]).x);
+  M = warp_max(M);
+  float L = 0.f;
+  for (int k = lane; k < nch; k += 32) {
+    const float2 ml = __ldcg(&p.part_ml[slot0 + k]);
+    L = fmaf(ml.y, exp2f(ml.x - M), L);
+  }
+  L = warp_sum(L);
+  const float w_s = lse == -INFINITY ? 0.f : exp2f(lse - M);  // 0 for an empty suffix
+  L += w_s;
+  if (lane >= DCH) return;
+  T* row = static_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + lane * EPC;
+  float o[EPC];
+  Elem<T>::unpack(*reinterpret_cast<const uint4*>(row), o);
+#pragma unroll
+  for (int e = 0; e < EPC; ++e) o[e] *= w_s;
+#pragma unroll 4
+  for (int k = 0; k < nch; ++k) {
+    const float wgt = exp2f(__ldcg(&p.part_ml[slot0 + k]).x - M);
+    const float4* src = reinterpret_cast<const float4*>(p.part_o + (slot0 + k) * D + lane * EPC);
+#pragma unroll
+    for (int e4 = 0; e4 < EPC / 4; ++e4) {
+      const float4 v = __ldcg(src + e4);
+      o[4 * e4 + 0] = fmaf(wgt, v.x, o[4 * e4 + 0]);
+      o[4 * e4 + 1] = fmaf(wgt, v.y, o[4 * e4 + 1]);
+      o[4 * e4 + 2] = fmaf(wgt, v.z, o[4 * e4 + 2]);
+      o[4 * e4 + 3] = fmaf(wgt, v.w, o[4 * e4 + 3]);
     }
   }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+  for (int e = 0; e < EPC; ++e) o[e] *= inv;
+  *reinterpret_cast<uint4*>(row) = Elem<T>::pack(o);
 }
 
 template <typename T>
@@ -266,6 +252,19 @@ cudaError_t launch_prefix_t(int head_dim, const CascadeParams& p, int smem, cuda
   return cudaGetLastError();
 }
 
+template <typename T>
+cudaError_t launch_merge_t(int head_dim, const CascadeMergeParams& p, cudaStream_t st) {
+  const int64_t warps = (int64_t)p.num_items * p.num_heads;
+  const int blocks = (int)((warps + 3) / 4);
+  switch (head_dim) {
+    case 64: cascade_merge_kernel<T, 64><<<blocks, 128, 0, st>>>(p); break;
+    case 112: cascade_merge_kernel<T, 112><<<blocks, 128, 0, st>>>(p); break;
+    case 128: cascade_merge_kernel<T, 128><<<blocks, 128, 0, st>>>(p); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 int cascade_smem_bytes(int head_dim, int elem_bytes, int num_pages) {
@@ -277,6 +276,11 @@ cudaError_t launch_cascade_prefix(int dtype, int head_dim, const CascadeParams& 
   const int smem = cascade_smem_bytes(head_dim, 2, kCascadeMaxPages);
   return dtype == 1 ? launch_prefix_t<__nv_bfloat16>(head_dim, p, smem, stream)
                     : launch_prefix_t<__half>(head_dim, p, smem, stream);
+}
+
+cudaError_t launch_cascade_merge(int dtype, int head_dim, const CascadeMergeParams& p, cudaStream_t stream) {
+  if (p.num_items == 0) return cudaSuccess;
+  return dtype == 1 ? launch_merge_t<__nv_bfloat16>(head_dim, p, stream) : launch_merge_t<__half>(head_dim, p, stream);
 }
 
 }  // namespace ubx

@@ -25,7 +25,7 @@ enum : int32_t {
   kErrTimeout = UBX_DEVERR_TIMEOUT,           // a pipeline wait exceeded its bound
   kErrBadSlot = UBX_DEVERR_BAD_SLOT,          // append slot >= num_blocks * block_size
   kErrBadPosition = UBX_DEVERR_BAD_POSITION,  // rotary position outside the table
-  kErrBadWork = UBX_DEVERR_BAD_WORK,          // a cascade work item out of range
+  kErrBadWork = UBX_DEVERR_BAD_WORK,          // a cascade work or merge item out of range
 };
 
 __device__ __forceinline__ void set_error(int32_t* err, int32_t bit) {

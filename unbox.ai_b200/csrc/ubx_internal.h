@@ -157,7 +157,6 @@ cudaError_t launch_kv_pages_copy(const KvCopyParams& p, cudaStream_t stream);
 constexpr int kCascadeWarps = 8;         // 16-row tiles in flight per CTA
 constexpr int kCascadeMaxPages = 8;      // shared pages one CTA holds in shared memory
 constexpr int kCascadeWorkInts = 6;      // ints per work item
-constexpr int kCascadeCounters = 65536;  // (request, KV head) counters at the start of the workspace
 constexpr int kCascadeMaxSmem = kCascadeMaxPages * 2 * kBlockSize * (128 * 2 + 16);  // head_dim <= 128, 16-bit
 
 struct CascadeParams {
@@ -169,24 +168,31 @@ struct CascadeParams {
   int64_t num_blocks;
   const int32_t* page_list;    // shared page ids of every group, concatenated
   const int32_t* member_list;  // member sequences of every group, concatenated
-  const int32_t* work;         // [num_work][6]: member offset, members, page offset, pages, chunk,
-                               // chunks of the group
+  const int32_t* work;         // [num_work][6]: member offset, members, page offset, pages, chunk, 0
   int num_work;
   int batch, num_heads, num_kv_heads, max_chunks;
   float scale_log2;
   int pitch;                   // shared-memory row pitch (bytes) of one head row
   float* part_o;               // [batch][num_heads][max_chunks][D]
   float2* part_ml;             // [batch][num_heads][max_chunks] (max in log2 units, sum)
-  int32_t* counters;           // [batch][num_kv_heads] chunks done; zero between calls
-  void* out;                   // the suffix pass's output, merged in place
+  int32_t* error;
+};
+
+struct CascadeMergeParams {
+  void* out;
   int64_t o_sb, o_sh;
   const float* lse;            // [batch][num_heads] of the suffix pass
+  const int32_t* items;        // [num_items][2]: sequence, prefix chunks
+  int num_items;
+  int batch, num_heads, max_chunks;
+  const float* part_o;
+  const float2* part_ml;
   int32_t* error;
 };
 
 int cascade_smem_bytes(int head_dim, int elem_bytes, int num_pages);
 cudaError_t launch_cascade_prefix(int dtype, int head_dim, const CascadeParams& p, cudaStream_t stream);
-
+cudaError_t launch_cascade_merge(int dtype, int head_dim, const CascadeMergeParams& p, cudaStream_t stream);
 
 cudaError_t launch_slot_mapping(const int32_t* block_table, int64_t bt_s_row, const int32_t* positions,
                                 int64_t* slot_mapping, int batch, int max_blocks, int block_size,

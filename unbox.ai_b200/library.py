@@ -19,7 +19,7 @@ FLAG_OVERLAP_PREVIOUS = 1
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_WORKSPACE, ERR_CUDA = 0, 1, 2, 3, 4
 DEVERR = {1: "page id outside the pool", 2: "context longer than its block-table row",
           4: "negative context length", 8: "pipeline wait timed out", 16: "append slot outside the pool",
-          32: "rotary position outside the rope table", 64: "cascade work item out of range"}
+          32: "rotary position outside the rope table", 64: "cascade work or merge item out of range"}
 
 # exported symbol -> (restype, argtypes); the test suite checks this list against the header
 _i32, _i64, _vp, _f32, _sz = ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_float, ctypes.c_size_t
@@ -51,8 +51,8 @@ SIGNATURES = {
                                               _f32, _i32, _i32, _i32, _i32, _vp, _vp, _sz, _vp]),
     "ubx_cascade_workspace_size": (_i32, [_i32, _i32, _i32, _i32, ctypes.POINTER(_sz)]),
     "ubx_cascade_prefix_attention": (_i32, [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i32,
-                                            _i32, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _i32, _f32, _i32, _vp,
-                                            _sz, _vp, _vp]),
+                                            _i32, _i32, _i32, _i32, _i32, _f32, _i32, _vp, _sz, _vp, _vp]),
+    "ubx_cascade_merge": (_i32, [_vp, _i64, _i64, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _sz, _vp, _vp]),
     "ubx_kv_wire_header_init": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, _i32, ctypes.c_uint64]),
     "ubx_kv_wire_header_check": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, ctypes.c_uint64]),
     "ubx_kv_pages_copy": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i32, _i32,
