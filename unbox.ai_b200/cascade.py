@@ -31,7 +31,7 @@ from . import library as _L
 from .ops import _DTYPES, _SCHEDULES, _require_cuda, _stream, workspace_for
 
 MAX_CHUNK_PAGES = 8     # shared pages one CTA holds (kCascadeMaxPages)
-TILE_ROWS = 128         # (request, head) rows one CTA covers: 8 warps x 16
+TILE_ROWS = 64          # (request, head) rows one CTA covers: 4 warps x 16
 WORK_INTS = 6
 
 

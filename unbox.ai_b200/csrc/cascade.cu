@@ -107,22 +107,38 @@ __global__ void __launch_bounds__(kCascadeWarps * 32) cascade_prefix_kernel(cons
     for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
     float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
 
-    for (int i = 0; i < n_pg; ++i) {
-      const T* kt = reinterpret_cast<const T*>(k_s + i * tile);
-      const T* vt = reinterpret_cast<const T*>(v_s + i * tile);
-      // S[16 rows x 16 tokens]: sa[n-tile][0..1] row qr, [2..3] row qr + 8
-      float sa[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    // two pages per step: four independent QK accumulation chains, one softmax
+    // update over 32 tokens, then PV of both pages
+    for (int i = 0; i < n_pg; i += 2) {
+      const bool two = i + 1 < n_pg;  // warp-uniform
+      const T* kt0 = reinterpret_cast<const T*>(k_s + i * tile);
+      const T* kt1 = reinterpret_cast<const T*>(k_s + (two ? i + 1 : i) * tile);
+      // S[16 rows x 16 tokens] per page: s[page][n-tile][0..1] row qr, [2..3] row qr + 8
+      float sc[2][2][4] = {};
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks) {
-        uint32_t r0, r1, r2, r3;
-        ldsm_x4(kt + k_row + 16 * ks, r0, r1, r2, r3);
-        mma16816<T>(sa[0], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], r0, r1);
-        mma16816<T>(sa[1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], r2, r3);
+        uint32_t r0, r1, r2, r3, u0, u1, u2, u3;
+        ldsm_x4(kt0 + k_row + 16 * ks, r0, r1, r2, r3);
+        ldsm_x4(kt1 + k_row + 16 * ks, u0, u1, u2, u3);
+        mma16816<T>(sc[0][0], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], r0, r1);
+        mma16816<T>(sc[0][1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], r2, r3);
+        mma16816<T>(sc[1][0], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], u0, u1);
+        mma16816<T>(sc[1][1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], u2, u3);
       }
-      float pv[2][4];
+      if (!two) {  // odd page count: the second page is absent
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) sc[1][nt][e] = -INFINITY;
+      }
+      float pv[2][2][4];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        float mx = fmaxf(fmaxf(sa[0][2 * h], sa[0][2 * h + 1]), fmaxf(sa[1][2 * h], sa[1][2 * h + 1]));
+        float mx = -INFINITY;
+#pragma unroll
+        for (int pg = 0; pg < 2; ++pg)
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) mx = fmaxf(mx, fmaxf(sc[pg][nt][2 * h], sc[pg][nt][2 * h + 1]));
         mx = fmaxf(mx, __shfl_xor_sync(kAll, mx, 1));
         mx = fmaxf(mx, __shfl_xor_sync(kAll, mx, 2));
         const float m_new = fmaxf(m[h], mx);
@@ -138,23 +154,30 @@ __global__ void __launch_bounds__(kCascadeWarps * 32) cascade_prefix_kernel(cons
         }
         const float mc = m[h] * c;
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          pv[nt][2 * h] = exp2f(fmaf(sa[nt][2 * h], c, -mc));
-          pv[nt][2 * h + 1] = exp2f(fmaf(sa[nt][2 * h + 1], c, -mc));
-          l[h] += pv[nt][2 * h] + pv[nt][2 * h + 1];
-        }
+        for (int pg = 0; pg < 2; ++pg)
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            pv[pg][nt][2 * h] = exp2f(fmaf(sc[pg][nt][2 * h], c, -mc));
+            pv[pg][nt][2 * h + 1] = exp2f(fmaf(sc[pg][nt][2 * h + 1], c, -mc));
+            l[h] += pv[pg][nt][2 * h] + pv[pg][nt][2 * h + 1];
+          }
       }
       // P as the A operand of PV (the S accumulator layout is the A layout)
-      const uint32_t pa0 = Elem<T>::pack2(pv[0][0], pv[0][1]);
-      const uint32_t pa1 = Elem<T>::pack2(pv[0][2], pv[0][3]);
-      const uint32_t pa2 = Elem<T>::pack2(pv[1][0], pv[1][1]);
-      const uint32_t pa3 = Elem<T>::pack2(pv[1][2], pv[1][3]);
 #pragma unroll
-      for (int np = 0; np < NT / 2; ++np) {
-        uint32_t r0, r1, r2, r3;
-        ldsm_x4_trans(vt + v_row + 16 * np, r0, r1, r2, r3);
-        mma16816<T>(o[2 * np], pa0, pa1, pa2, pa3, r0, r1);
-        mma16816<T>(o[2 * np + 1], pa0, pa1, pa2, pa3, r2, r3);
+      for (int pg = 0; pg < 2; ++pg) {
+        if (pg == 1 && !two) break;
+        const T* vt = reinterpret_cast<const T*>(v_s + (i + pg) * tile);
+        const uint32_t pa0 = Elem<T>::pack2(pv[pg][0][0], pv[pg][0][1]);
+        const uint32_t pa1 = Elem<T>::pack2(pv[pg][0][2], pv[pg][0][3]);
+        const uint32_t pa2 = Elem<T>::pack2(pv[pg][1][0], pv[pg][1][1]);
+        const uint32_t pa3 = Elem<T>::pack2(pv[pg][1][2], pv[pg][1][3]);
+#pragma unroll
+        for (int np = 0; np < NT / 2; ++np) {
+          uint32_t r0, r1, r2, r3;
+          ldsm_x4_trans(vt + v_row + 16 * np, r0, r1, r2, r3);
+          mma16816<T>(o[2 * np], pa0, pa1, pa2, pa3, r0, r1);
+          mma16816<T>(o[2 * np + 1], pa0, pa1, pa2, pa3, r2, r3);
+        }
       }
     }
     // ---- partial rows of this chunk

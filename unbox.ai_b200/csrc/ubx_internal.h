@@ -154,7 +154,7 @@ struct KvCopyParams {
 cudaError_t launch_kv_pages_copy(const KvCopyParams& p, cudaStream_t stream);
 
 // Shared-prefix (cascade) pass (cascade.cu).
-constexpr int kCascadeWarps = 8;         // 16-row tiles in flight per CTA
+constexpr int kCascadeWarps = 4;         // 16-row tiles in flight per CTA
 constexpr int kCascadeMaxPages = 8;      // shared pages one CTA holds in shared memory
 constexpr int kCascadeWorkInts = 6;      // ints per work item
 constexpr int kCascadeMaxSmem = kCascadeMaxPages * 2 * kBlockSize * (128 * 2 + 16);  // head_dim <= 128, 16-bit
