@@ -48,7 +48,7 @@ def parse():
     ap.add_argument("--workload", default="decode_760m",
                     choices=["decode_760m", "correctness", "long_context", "radix_prefix", "box_scale"])
     ap.add_argument("--layers", type=int, default=24)
-    ap.add_argument("--schedule", default="auto", choices=["auto", "balanced", "split"])
+    ap.add_argument("--schedule", default="auto", choices=["auto", "balanced", "split", "dynamic"])
     ap.add_argument("--split-pages", type=int, default=0)
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="launch every op from Python instead of replaying the step as one CUDA graph")

@@ -161,7 +161,7 @@ def paged_attention_cascade(q: torch.Tensor, k_cache: torch.Tensor, v_cache: tor
     if plan._ws is None or plan._ws.numel() < need.value or plan._ws.device != dev:
         plan._ws = torch.empty(max(int(need.value), 256), dtype=torch.uint8, device=dev)
     dws = workspace_for(dev)
-    buf = dws.ensure(B, H, D, sbt.shape[1], 0)
+    buf = dws.ensure(B, H, D, sbt.shape[1], 0, KVH, q.dtype)
     st_ = _stream(dev)
     dt = _DTYPES[q.dtype]
     if k_new is not None:

@@ -24,7 +24,7 @@
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB per GPU
-static_assert(kNoAllocScratchBytes > ubx::kWsHeaderBytes + ubx::kWsCounterBytes, "scratch holds the fixed prefix");
+static_assert(kNoAllocScratchBytes > ubx::kWsZeroBytes, "scratch holds the fixed prefix");
 
 static __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchBytes];
 
@@ -70,11 +70,9 @@ int ubx_paged_decode_attention_noalloc(const void* q, int64_t q_s_b, int64_t q_s
   cudaError_t e = scratch_for_current_device(&scratch);
   if (e != cudaSuccess) return cuda_status(e, "scratch address lookup (cudaGetSymbolAddress)");
   // The array keeps whatever the previous call left: re-zero the error word and
-  // the merge counters this call can touch before launching.
-  const size_t counters = (size_t)(batch > 0 ? batch : 0) * (size_t)(num_heads > 0 ? num_heads : 0) * 4;
-  const size_t clear = ubx::kWsHeaderBytes + (counters < ubx::kWsCounterBytes ? counters : ubx::kWsCounterBytes);
+  // the counters (the whole zero-initialised prefix of the workspace) before launching.
   if (batch > 0) {
-    e = cudaMemsetAsync(scratch, 0, clear, s);
+    e = cudaMemsetAsync(scratch, 0, ubx::kWsZeroBytes, s);
     if (e != cudaSuccess) return cuda_status(e, "scratch clear");
   }
   int st = ubx_paged_decode_attention(q, q_s_b, q_s_h, k_cache, v_cache, c_s_block, c_s_tok, c_s_head, block_table,

@@ -26,6 +26,7 @@ enum : int32_t {
   kErrBadSlot = UBX_DEVERR_BAD_SLOT,          // append slot >= num_blocks * block_size
   kErrBadPosition = UBX_DEVERR_BAD_POSITION,  // rotary position outside the table
   kErrBadWork = UBX_DEVERR_BAD_WORK,          // a cascade work or merge item out of range
+  kErrCapacity = UBX_DEVERR_CAPACITY,         // dynamic schedule: partial-result storage exhausted
 };
 
 __device__ __forceinline__ void set_error(int32_t* err, int32_t bit) {

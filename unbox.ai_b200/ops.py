@@ -27,7 +27,8 @@ import torch
 from . import library as _L
 
 _DTYPES = {torch.float32: _L.DTYPE_F32, torch.bfloat16: _L.DTYPE_BF16, torch.float16: _L.DTYPE_F16}
-_SCHEDULES = {"auto": _L.SCHEDULE_AUTO, "balanced": _L.SCHEDULE_BALANCED, "split": _L.SCHEDULE_SPLIT}
+_SCHEDULES = {"auto": _L.SCHEDULE_AUTO, "balanced": _L.SCHEDULE_BALANCED, "split": _L.SCHEDULE_SPLIT,
+              "dynamic": _L.SCHEDULE_DYNAMIC}
 
 
 def _stream(device: torch.device) -> int:
@@ -61,12 +62,16 @@ class DecodeWorkspace:
     def nbytes(self) -> int:
         return 0 if self.buf is None else self.buf.numel()
 
-    def ensure(self, batch: int, num_heads: int, head_dim: int, max_blocks: int, split_pages: int = 0):
+    def ensure(self, batch: int, num_heads: int, head_dim: int, max_blocks: int, split_pages: int = 0,
+               num_kv_heads: int = 0, dtype: Optional[torch.dtype] = None):
+        """Grow to what a call with these sizes needs (``num_kv_heads`` and a 16-bit
+        ``dtype`` add room for the dynamic schedule)."""
         lib = _L.load()
         need = ctypes.c_size_t(0)
         with torch.cuda.device(self.device):
-            _L.check(lib.ubx_paged_decode_workspace_size(batch, num_heads, head_dim, max_blocks, split_pages,
-                                                         ctypes.byref(need)), "workspace size")
+            _L.check(lib.ubx_paged_decode_workspace_size(
+                batch, num_heads, num_kv_heads or num_heads, head_dim, max_blocks, split_pages,
+                _DTYPES.get(dtype, _L.DTYPE_F32), ctypes.byref(need)), "workspace size")
         n = max(int(need.value), 1 << 20)
         if self.buf is None or self.buf.numel() < n:
             self.buf = torch.zeros(n, dtype=torch.uint8, device=self.device)
@@ -178,7 +183,7 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
         scale = D ** -0.5
     max_blocks = block_table.shape[1]
     ws = workspace or workspace_for(dev)
-    buf = ws.ensure(B, H, D, max_blocks, split_pages)
+    buf = ws.ensure(B, H, D, max_blocks, split_pages, KVH, q.dtype)
     lib = _L.load()
     tail = (block_table.data_ptr(), block_table.stride(0), context_lens.data_ptr(), out.data_ptr(), out.stride(0),
             out.stride(1), B, H, KVH, D, bs, NB, max_blocks, float(scale), _DTYPES[q.dtype], _SCHEDULES[schedule],
@@ -448,7 +453,7 @@ def paged_decode_prep_attention(q_raw: torch.Tensor, k_raw: torch.Tensor, v_new:
     if scale is None:
         scale = D ** -0.5
     max_blocks = block_table.shape[1]
-    buf = workspace_for(dev).ensure(B, H, D, max_blocks, 0)
+    buf = workspace_for(dev).ensure(B, H, D, max_blocks, 0, KVH, q_raw.dtype)
     lib = _L.load()
     st = lib.ubx_paged_decode_prep_attention(
         q_raw.data_ptr(), q_raw.stride(0), q_raw.stride(1), k_raw.data_ptr(), v_new.data_ptr(), k_raw.stride(0),
