@@ -1271,9 +1271,12 @@ __device__ void consume_dyn(const DecodeParams& p, const Smem& sm, int kh, int k
       break;
     }
     const int4 inf = sm.info[st];  // (sequence, page index, page id, slot of the appended row or -1)
+    if (inf.x < 0) {  // end marker (may be the first stage: a CTA that found no pages)
+      if (cur >= 0) close_run();
+      break;
+    }
     if (inf.x != cur) {
       if (cur >= 0) close_run();
-      if (inf.x < 0) break;  // end marker
       cur = inf.x;
       n_b = sm.prefix[cur + 1] - sm.prefix[cur];
       ctx_raw = __ldg(&p.context_lens[cur]);
