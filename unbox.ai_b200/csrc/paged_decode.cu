@@ -1000,76 +1000,86 @@ __device__ void produce_dyn(const DecodeParams& p, const Work& w, const Smem& sm
   RingPos pos{0, 0};
   bool ok = true;
 
-  // pages [g0, g1) of the flattened list, ascending
-  auto issue = [&](int g0, int g1) {
-    for (int gb = g0; gb < g1 && ok; gb += 32) {
-      const int cnt = min(32, g1 - gb);
-      int my_b = 0, my_lp = 0, my_page = 0, my_slot = -1;
-      if (lane < cnt) {
-        my_b = seq_of(sm.prefix, B, gb + lane);
-        my_lp = gb + lane - sm.prefix[my_b];
-        my_page = __ldg(p.block_table + (int64_t)my_b * p.bt_sb + my_lp);
-        if (my_page < 0 || (int64_t)my_page >= p.num_blocks) set_error(p.error, kErrBadPage);
-        if (nbase != nullptr && my_lp == sm.prefix[my_b + 1] - sm.prefix[my_b] - 1) {
-          const int ctx = __ldg(&p.context_lens[my_b]);
-          if (ctx >= 1 && (ctx - 1) / kBlockSize < p.max_blocks) my_slot = (ctx - 1) & (kBlockSize - 1);
-        }
-      }
-      for (int i = 0; i < cnt; ++i, ++it, pos.next(STAGES)) {
-        const int b = __shfl_sync(kFull, my_b, i), lp = __shfl_sync(kFull, my_lp, i);
-        const int page = __shfl_sync(kFull, my_page, i), a_slot = __shfl_sync(kFull, my_slot, i);
-        const bool in_pool = page >= 0 && (int64_t)page < p.num_blocks;
-        const int st = pos.st;
-        int good = 1;
-        if (lane == 0) {
-          if (!mbar_wait_bounded(&sm.empty_bar[st], pos.ph ^ 1u)) {
-            good = 0;
-          } else {
-            sm.info[st] = make_int4(b, lp, page, in_pool ? a_slot : -1);
-            if (in_pool) mbar_arrive_expect_tx(&sm.full_bar[st], 2 * kBlockSize * p.row_bytes);
-          }
-        }
-        if (!__shfl_sync(kFull, good, 0)) {
-          ok = false;
-          break;
-        }
-        uint8_t* dst = sm.stages + st * stage_bytes;
-        if (in_pool) {
-          const char* src = t == a_slot ? nbase + (int64_t)b * p.n_stok * (int64_t)sizeof(T)
-                                        : base + ((int64_t)page * p.c_sblk + (int64_t)t * p.c_stok) *
-                                                     (int64_t)sizeof(T);
-          bulk_copy_g2s(dst + dst_off, src, p.row_bytes, &sm.full_bar[st]);
-        } else {
-          // a page outside the pool (reported above) reads as zeros
-          for (int i2 = lane * 16; i2 < stage_bytes; i2 += 32 * 16)
-            *reinterpret_cast<uint4*>(dst + i2) = make_uint4(0, 0, 0, 0);
-          fence_proxy_async_smem();  // before later bulk copies refill this stage
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&sm.full_bar[st]);
-        }
+  // Window of 32 consecutive flattened pages whose (sequence, page index, page
+  // id, appended-row slot) the lanes hold: one block-table read per 32 pages.
+  int win = -1, wb = 0, wlp = 0, wpage = 0, wslot = -1;
+  auto fill = [&](int g0) {
+    win = g0;
+    wslot = -1;
+    const int g = g0 + lane;
+    if (g < w.total) {
+      wb = seq_of(sm.prefix, B, g);
+      wlp = g - sm.prefix[wb];
+      wpage = __ldg(p.block_table + (int64_t)wb * p.bt_sb + wlp);
+      if (nbase != nullptr && wlp == sm.prefix[wb + 1] - sm.prefix[wb] - 1) {
+        const int ctx = __ldg(&p.context_lens[wb]);
+        if (ctx >= 1 && (ctx - 1) / kBlockSize < p.max_blocks) wslot = (ctx - 1) & (kBlockSize - 1);
       }
     }
+  };
+  // page g of the flattened list into the next stage
+  auto issue_one = [&](int g) {
+    if (win < 0 || g < win || g >= win + 32) fill(g);
+    const int i = g - win;
+    const int b = __shfl_sync(kFull, wb, i), lp = __shfl_sync(kFull, wlp, i);
+    const int page = __shfl_sync(kFull, wpage, i), a_slot = __shfl_sync(kFull, wslot, i);
+    const bool in_pool = page >= 0 && (int64_t)page < p.num_blocks;
+    if (!in_pool && lane == 0) set_error(p.error, kErrBadPage);
+    const int st = pos.st;
+    int good = 1;
+    if (lane == 0) {
+      if (!mbar_wait_bounded(&sm.empty_bar[st], pos.ph ^ 1u)) {
+        good = 0;
+      } else {
+        sm.info[st] = make_int4(b, lp, page, in_pool ? a_slot : -1);
+        if (in_pool) mbar_arrive_expect_tx(&sm.full_bar[st], 2 * kBlockSize * p.row_bytes);
+      }
+    }
+    if (!__shfl_sync(kFull, good, 0)) {
+      ok = false;
+      return;
+    }
+    uint8_t* dst = sm.stages + st * stage_bytes;
+    if (in_pool) {
+      const char* src = t == a_slot ? nbase + (int64_t)b * p.n_stok * (int64_t)sizeof(T)
+                                    : base + ((int64_t)page * p.c_sblk + (int64_t)t * p.c_stok) * (int64_t)sizeof(T);
+      bulk_copy_g2s(dst + dst_off, src, p.row_bytes, &sm.full_bar[st]);
+    } else {
+      // a page outside the pool (reported above) reads as zeros
+      for (int i2 = lane * 16; i2 < stage_bytes; i2 += 32 * 16)
+        *reinterpret_cast<uint4*>(dst + i2) = make_uint4(0, 0, 0, 0);
+      fence_proxy_async_smem();  // before later bulk copies refill this stage
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.full_bar[st]);
+    }
+    ++it;
+    pos.next(STAGES);
   };
 
   // the head of the own range needs no grab: stream it at once
   const DynRange me = dyn_range(w.total, w.w_eff, STAGES, blockIdx.x);
-  issue(me.begin, me.begin + me.fixed);
+  for (int g = me.begin; g < me.begin + me.fixed && ok; ++g) issue_one(g);
   // the owner words are re-zeroed by the previous grid's last CTA: touch them only after it completed
   griddep_wait();
-  // own range, kDynOwnerPages at a time, while nobody has stolen up to the front
+  // Own range in grabs from the front, each requested one grab ahead so its
+  // atomic round trip overlaps the streaming of the previous one. Grabs shrink
+  // with the pages left, so little of the range is reserved near its end.
+  auto grab_size = [&](int left) { return min(kDynOwnerPages, max(2, left / 4)); };
+  uint32_t inc = (uint32_t)(grab_size(me.end - me.begin - me.fixed) + me.fixed);
+  unsigned long long pend = 0;
+  if (lane == 0) pend = atomicAdd(own + blockIdx.x, (unsigned long long)inc);
   for (bool first = true; ok;) {
-    const uint32_t inc = kDynOwnerPages + (first ? me.fixed : 0);
-    unsigned long long old = 0;
-    if (lane == 0) old = atomicAdd(own + blockIdx.x, (unsigned long long)inc);
-    old = __shfl_sync(kFull, old, 0);
+    const unsigned long long old = __shfl_sync(kFull, pend, 0);
     const int lo = (int)(uint32_t)old, hi = (int)(old >> 32);
     const int from = me.begin + (first ? me.fixed : lo);
     const int to = min(me.begin + lo + (int)inc, me.end - hi);
     first = false;
     if (from >= to) break;
-    issue(from, to);
+    inc = (uint32_t)grab_size(me.end - hi - to);
+    if (lane == 0) pend = atomicAdd(own + blockIdx.x, (unsigned long long)inc);
+    for (int g = from; g < to && ok; ++g) issue_one(g);
   }
-  // steal from the back of the CTA with the most pages left
+  // steal from the back of the CTA with the most pages left (worth it from 4 pages)
   for (int runs = 0; ok && runs < kDynMaxStealRuns;) {
     int best = 0, victim = -1;
     for (int v = lane; v < w.w_eff; v += 32) {
@@ -1089,8 +1099,8 @@ __device__ void produce_dyn(const DecodeParams& p, const Work& w, const Smem& sm
     }
     best = __shfl_sync(kFull, best, 0);
     victim = __shfl_sync(kFull, victim, 0);
-    if (best <= 0 || victim < 0) break;
-    const int k = min(kDynMaxStealPages, max(1, (best + 1) / 2));
+    if (best < 4 || victim < 0) break;
+    const int k = min(kDynMaxStealPages, best / 2);
     unsigned long long old = 0;
     if (lane == 0) old = atomicAdd(own + victim, (unsigned long long)k << 32);
     old = __shfl_sync(kFull, old, 0);
@@ -1098,7 +1108,7 @@ __device__ void produce_dyn(const DecodeParams& p, const Work& w, const Smem& sm
     const int back = r.end - (int)(old >> 32);
     const int from = max(back - k, r.begin + max((int)(uint32_t)old, r.fixed));
     if (from < back) {
-      issue(from, back);
+      for (int g = from; g < back && ok; ++g) issue_one(g);
       ++runs;
     }
   }

@@ -18,7 +18,7 @@ constexpr int kSmemReservedPerCta = 1024 + 512;  // per-CTA reservation + static
 constexpr int kMaxCtasPerSm = 4;              // CTAs of one balanced launch per SM (small head groups)
 
 // Dynamic (work-sharing) schedule.
-constexpr int kDynOwnerPages = 4;     // pages a CTA takes from its own range per grab
+constexpr int kDynOwnerPages = 16;    // most pages a CTA takes from its own range per grab
 constexpr int kDynMaxStealPages = 8;  // most pages one steal takes
 constexpr int kDynMaxStealRuns = 6;   // steals per CTA (bounds its partial results)
 constexpr int kDynSlotsPerCta = 16;   // partial-result slots per CTA (3 + 2 per steal suffice)
