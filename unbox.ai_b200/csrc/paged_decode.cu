@@ -972,7 +972,7 @@ __device__ __forceinline__ int seq_of(const int32_t* prefix, int B, int g) {
   int lo = 0, hi = B - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
-    if (prefix[mid] <= g) lo = mid; else hi = mid - 1;
+    if (lds_int(prefix + mid) <= g) lo = mid; else hi = mid - 1;
   }
   return lo;
 }
@@ -1009,9 +1009,10 @@ __device__ void produce_dyn(const DecodeParams& p, const Work& w, const Smem& sm
     const int g = g0 + lane;
     if (g < w.total) {
       wb = seq_of(sm.prefix, B, g);
-      wlp = g - sm.prefix[wb];
+      const int p0 = lds_int(sm.prefix + wb), p1 = lds_int(sm.prefix + wb + 1);
+      wlp = g - p0;
       wpage = __ldg(p.block_table + (int64_t)wb * p.bt_sb + wlp);
-      if (nbase != nullptr && wlp == sm.prefix[wb + 1] - sm.prefix[wb] - 1) {
+      if (nbase != nullptr && wlp == p1 - p0 - 1) {
         const int ctx = __ldg(&p.context_lens[wb]);
         if (ctx >= 1 && (ctx - 1) / kBlockSize < p.max_blocks) wslot = (ctx - 1) & (kBlockSize - 1);
       }
@@ -1031,7 +1032,7 @@ __device__ void produce_dyn(const DecodeParams& p, const Work& w, const Smem& sm
       if (!mbar_wait_bounded(&sm.empty_bar[st], pos.ph ^ 1u)) {
         good = 0;
       } else {
-        sm.info[st] = make_int4(b, lp, page, in_pool ? a_slot : -1);
+        sts_int4(sm.info + st, make_int4(b, lp, page, in_pool ? a_slot : -1));
         if (in_pool) mbar_arrive_expect_tx(&sm.full_bar[st], 2 * kBlockSize * p.row_bytes);
       }
     }
@@ -1120,7 +1121,7 @@ __device__ void produce_dyn(const DecodeParams& p, const Work& w, const Smem& sm
       if (!mbar_wait_bounded(&sm.empty_bar[st], pos.ph ^ 1u)) {
         good = 0;
       } else {
-        sm.info[st] = make_int4(-1, 0, 0, -1);
+        sts_int4(sm.info + st, make_int4(-1, 0, 0, -1));
         mbar_arrive(&sm.full_bar[st]);
       }
     }
@@ -1280,7 +1281,7 @@ __device__ void consume_dyn(const DecodeParams& p, const Smem& sm, int kh, int k
       ok = false;
       break;
     }
-    const int4 inf = sm.info[st];  // (sequence, page index, page id, slot of the appended row or -1)
+    const int4 inf = lds_int4(sm.info + st);  // (sequence, page index, page id, appended-row slot or -1)
     if (inf.x < 0) {  // end marker (may be the first stage: a CTA that found no pages)
       if (cur >= 0) close_run();
       break;
@@ -1288,7 +1289,7 @@ __device__ void consume_dyn(const DecodeParams& p, const Smem& sm, int kh, int k
     if (inf.x != cur) {
       if (cur >= 0) close_run();
       cur = inf.x;
-      n_b = sm.prefix[cur + 1] - sm.prefix[cur];
+      n_b = lds_int(sm.prefix + cur + 1) - lds_int(sm.prefix + cur);
       ctx_raw = __ldg(&p.context_lens[cur]);
       ctx = min(max(ctx_raw, 0), n_b * kBlockSize);
       run = 0;
