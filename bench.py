@@ -12,7 +12,8 @@ consecutive layer-calls overlap through programmatic dependent launch.
 head), q, out, block-table rows, context lengths, append rows) with all inputs
 resident in HBM; ``e2e`` is the same metric through the public API with the
 step's per-token inputs (q, new K/V rows, block table, context lengths) copied
-from pinned host memory and the outputs copied back inside the timed region.
+from pinned host memory and the outputs copied back inside the timed region, on
+copy streams that overlap the layer-calls (layer l waits for its own inputs).
 
 ``--impl reference`` times the CPU oracle (the reference algorithm restated in
 C, OpenMP over all host cores) on one layer-call of the same workload per step.
@@ -138,6 +139,32 @@ class ClockSampler:
     def summary(self):
         return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
                 "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+class Staging:
+    """A pinned host buffer and a device buffer with the same layout of named,
+    256-byte aligned sections; copy_range moves sections first..last (in
+    layout order) host -> device in one copy."""
+
+    def __init__(self, specs, device):
+        import torch
+        self.layout, off = {}, 0
+        for name, shape, dtype in specs:
+            n = torch.Size(shape).numel() * torch.empty((), dtype=dtype).element_size()
+            self.layout[name] = (off, n, tuple(shape), dtype)
+            off = (off + n + 255) // 256 * 256
+        self.host = torch.empty(off, dtype=torch.uint8).pin_memory()
+        self.dev = torch.empty(off, dtype=torch.uint8, device=device)
+        self.nbytes = sum(n for _, n, _, _ in self.layout.values())  # payload, without the alignment gaps
+
+    def view(self, buf, name):
+        off, n, shape, dtype = self.layout[name]
+        return buf[off:off + n].view(dtype).view(shape)
+
+    def copy_range(self, first, last):
+        a = self.layout[first][0]
+        off, n, _, _ = self.layout[last]
+        self.dev[a:off + n].copy_(self.host[a:off + n], non_blocking=True)
 
 
 def build_parts(pkg, workload: str, rank: int, world: int):
@@ -601,37 +628,72 @@ def main():
     kernel_bytes = (bytes_attn if args.separate else bytes_call) / len(parts)
 
     # ---- end to end through the public API with host buffers
+    # One pinned staging buffer per part, mirrored on the device: block table,
+    # context lengths, then each layer's q / new K / new V rows, so a group of
+    # layers' inputs moves in one copy.
     hosts = []
     for d in devs:
-        h = dict(q=torch.stack([x.cpu() for x in d["q"]]).pin_memory(),
-                 k_new=torch.stack([x.cpu() for x in d["k_new"]]).pin_memory(),
-                 v_new=torch.stack([x.cpu() for x in d["v_new"]]).pin_memory(),
-                 bt=d["block_table"].cpu().pin_memory(), cl=d["context_lens"].cpu().pin_memory())
+        specs = [("bt", d["block_table"]), ("cl", d["context_lens"])]
+        for l in range(L):
+            specs += [(f"q{l}", d["q"][l]), (f"k{l}", d["k_new"][l]), (f"v{l}", d["v_new"][l])]
+        stg = Staging([(name, t.shape, t.dtype) for name, t in specs], device)
+        for name, t in specs:
+            stg.view(stg.host, name).copy_(t.cpu())
+        h = {name: stg.view(stg.host, name) for name, _ in specs}
+        dd = {name: stg.view(stg.dev, name) for name, _ in specs}
         h["out"] = torch.empty((L,) + tuple(d["q"][0].shape), dtype=d["q"][0].dtype).pin_memory()
-        dd = {k: torch.empty_like(v, device=device) for k, v in h.items()}
-        dd["pos"] = torch.empty_like(h["cl"], device=device)
-        dd["slots"] = torch.empty(h["cl"].shape[0], dtype=torch.int64, device=device)
+        dd["out"] = torch.empty_like(h["out"], device=device)
+        dd["pos"] = torch.empty_like(dd["cl"])
+        dd["slots"] = torch.empty(dd["cl"].shape[0], dtype=torch.int64, device=device)
         if args.cascade:  # the step's prefix plan travels with its block table
             h["plan"] = {f: getattr(d["plan"], f).cpu().pin_memory() for f in PLAN_FIELDS}
-        hosts.append((h, dd))
+        hosts.append((h, dd, stg))
+
+    # Copies run on their own streams so they overlap the attention launches;
+    # each output leaves for the host as soon as it is written. The launching
+    # stream waits for the inputs in growing groups of layers (1, 3, 9, ...):
+    # a wait between two layer-calls also ends their programmatic overlap, and
+    # a layer's inputs copy about three or more times faster than its attention
+    # runs. The step ends when the last output has arrived (the copy streams
+    # join the launching stream).
+    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    groups, l0, n = [], 0, 1
+    while l0 < L:
+        groups.append((l0, min(L, l0 + n) - 1))
+        l0, n = l0 + n, 3 * n
+    ev_in = [torch.cuda.Event() for _ in groups]
+    ev_out = [torch.cuda.Event() for _ in range(L)]
 
     def e2e_step():
-        for h, dd in hosts:
-            for k in ("bt", "cl", "q", "k_new", "v_new"):
-                dd[k].copy_(h[k], non_blocking=True)
-            if args.separate:
-                torch.sub(dd["cl"], 1, out=dd["pos"])
-                pkg.slot_mapping(dd["bt"], dd["pos"], glay.block_size, out=dd["slots"])
-        if args.cascade:
-            for (h, dd), d in zip(hosts, devs):
-                for f in PLAN_FIELDS:
-                    getattr(d["plan"], f).copy_(h["plan"][f], non_blocking=True)
-        for l in range(L):
-            for (h, dd), d in zip(hosts, devs):
-                layer_call(d, l, dd["q"][l], dd["k_new"][l], dd["v_new"][l], dd["bt"], dd["cl"], dd["out"][l],
-                           dd["slots"])
-        for h, dd in hosts:
-            h["out"].copy_(dd["out"], non_blocking=True)
+        main = torch.cuda.current_stream(device)
+        s_in.wait_stream(main)
+        s_out.wait_stream(main)
+        with torch.cuda.stream(s_in):
+            if args.cascade:
+                for (h, dd, stg), d in zip(hosts, devs):
+                    for f in PLAN_FIELDS:
+                        getattr(d["plan"], f).copy_(h["plan"][f], non_blocking=True)
+            for gi, (a, b) in enumerate(groups):
+                for h, dd, stg in hosts:
+                    stg.copy_range("bt" if a == 0 else f"q{a}", f"v{b}")
+                ev_in[gi].record(s_in)
+        for gi, (a, b) in enumerate(groups):
+            main.wait_event(ev_in[gi])
+            if a == 0 and args.separate:
+                for h, dd, stg in hosts:
+                    torch.sub(dd["cl"], 1, out=dd["pos"])
+                    pkg.slot_mapping(dd["bt"], dd["pos"], glay.block_size, out=dd["slots"])
+            for l in range(a, b + 1):
+                for (h, dd, stg), d in zip(hosts, devs):
+                    layer_call(d, l, dd[f"q{l}"], dd[f"k{l}"], dd[f"v{l}"], dd["bt"], dd["cl"], dd["out"][l],
+                               dd["slots"])
+                ev_out[l].record(main)
+                s_out.wait_event(ev_out[l])
+                with torch.cuda.stream(s_out):
+                    for h, dd, stg in hosts:
+                        h["out"][l].copy_(dd["out"][l], non_blocking=True)
+        main.wait_stream(s_in)
+        main.wait_stream(s_out)
 
     for _ in range(3):
         e2e_step()
@@ -649,12 +711,13 @@ def main():
     torch.cuda.synchronize()
     barrier()
     e2e_ms = reduce(e0.elapsed_time(e1), dist.ReduceOp.MAX)
-    h2d = sum(h[k].numel() * h[k].element_size() for h, _ in hosts for k in ("bt", "cl", "q", "k_new", "v_new"))
+    h2d = sum(stg.nbytes for _, _, stg in hosts)
     if args.cascade:
-        h2d += sum(t.numel() * t.element_size() for h, _ in hosts for t in h["plan"].values())
-    d2h = sum(h["out"].numel() * h["out"].element_size() for h, _ in hosts)
-    for (h, _), o in zip(hosts, outs):
-        assert torch.equal(h["out"][0].to(device), o[0]), "end-to-end output differs from the device-resident step"
+        h2d += sum(t.numel() * t.element_size() for h, _, _ in hosts for t in h["plan"].values())
+    d2h = sum(h["out"].numel() * h["out"].element_size() for h, _, _ in hosts)
+    for (h, _, _), o in zip(hosts, outs):
+        assert all(torch.equal(h["out"][l].to(device), o[l]) for l in range(L)), \
+            "end-to-end output differs from the device-resident step"
     del eg
 
     step_bytes_all = reduce(float(bytes_call * L), dist.ReduceOp.SUM)
