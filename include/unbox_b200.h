@@ -264,6 +264,14 @@ int ubx_paged_decode_attention_lse(const void* k_new, const void* v_new, int64_t
  *                count * (num_heads / num_kv_heads) <= 64
  *   merge_items: int32 [num_merge_items][2] = (sequence, number of its prefix chunks)
  *   cascade_ws:  ubx_cascade_workspace_size bytes (no initialisation needed)
+ *   flags:       UBX_FLAG_OVERLAP_PREVIOUS = programmatic dependent launch: the
+ *                kernel may start while the previous kernel on the stream drains.
+ *                The prefix pass then loads its shared pages before waiting for
+ *                that kernel (the caller promises it writes neither those pages
+ *                nor page_list / member_list / work_items, which holds for the
+ *                suffix pass of step 1: its append lands in private pages); q, the
+ *                workspace and the outputs are touched only after the wait. The
+ *                merge reads merge_items before the wait.
  * bf16/f16, head_dim 64/112/128, page 16, GQA 1/2/4/8.
  */
 int ubx_cascade_workspace_size(int batch, int num_heads, int head_dim, int max_chunks, size_t* bytes);
@@ -272,10 +280,12 @@ int ubx_cascade_prefix_attention(const void* q, int64_t q_s_b, int64_t q_s_h, co
                                  int64_t num_blocks, const int32_t* page_list, const int32_t* member_list,
                                  const int32_t* work_items, int num_work_items, int max_chunks, int batch,
                                  int num_heads, int num_kv_heads, int head_dim, float scale, int dtype,
-                                 void* cascade_ws, size_t cascade_ws_bytes, int32_t* error_word, void* stream);
+                                 void* cascade_ws, size_t cascade_ws_bytes, int32_t* error_word, int flags,
+                                 void* stream);
 int ubx_cascade_merge(void* out, int64_t o_s_b, int64_t o_s_h, const float* lse, const int32_t* merge_items,
                       int num_merge_items, int max_chunks, int batch, int num_heads, int head_dim, int dtype,
-                      const void* cascade_ws, size_t cascade_ws_bytes, int32_t* error_word, void* stream);
+                      const void* cascade_ws, size_t cascade_ws_bytes, int32_t* error_word, int flags,
+                      void* stream);
 
 /*
  * KV hand-off between a prefill worker and a decode worker.

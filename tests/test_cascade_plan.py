@@ -62,7 +62,7 @@ def test_radix_layout_groups_and_suffix_tables():
     seen = {}
     mlist = p.member_list.numpy()
     for m_off, nm, pg_off, npg, chunk, _ in p.work.numpy():
-        assert 1 <= npg <= 8 and nm * 2 <= 128
+        assert 1 <= npg <= PKG.cascade.MAX_CHUNK_PAGES and nm * 2 <= 128
         for b in mlist[m_off:m_off + nm]:
             seen[(int(b), int(chunk))] = seen.get((int(b), int(chunk)), 0) + 1
     assert set(seen.values()) == {1} and len(seen) == 20 * 2
@@ -91,6 +91,23 @@ def test_prefix_cut_leaves_every_member_a_private_token():
     members, shared = p.groups[0]
     assert len(shared) == 5               # (96 - 1) // 16
     assert p.suffix_context_lens.numpy()[2] == 16
+
+
+def test_prefix_cut_before_another_requests_append_page():
+    """A shared page that also holds another request's append slot (a table no
+    radix cache makes) is left out of the prefix: the shared pages are read while
+    the suffix pass appends."""
+    wl = PKG.workloads
+    lay = wl.layout_radix_prefix(7, batch=5, prefix_pages=10, suffix_lo=5, suffix_hi=40)
+    shared_page = int(lay.block_table[0, 7])
+    outsider = wl.layout_uniform(8, 1, 40, 41, num_blocks=lay.num_blocks)
+    bt = np.full((6, lay.block_table.shape[1]), -1, dtype=np.int32)
+    bt[:5] = lay.block_table
+    bt[5, :3] = [int(outsider.block_table[0, 0]), int(outsider.block_table[0, 1]), shared_page]
+    ctx = np.concatenate([lay.context_lens, [40]]).astype(np.int32)   # position 39 lies on page index 2
+    lay2 = wl.Layout(ctx, bt, lay.num_blocks)
+    members, shared = plan(lay2).groups[0]
+    assert len(shared) == 7 and shared_page not in shared
 
 
 @pytest.mark.parametrize("heads", [(16, 8, 112), (16, 2, 64), (8, 8, 64)])

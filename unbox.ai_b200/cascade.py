@@ -66,7 +66,9 @@ def plan_cascade(block_table, context_lens, num_heads: int, num_kv_heads: int, b
     A group is the requests whose rows start with the same page id; its shared
     prefix is the longest run of leading page ids all members have in common,
     cut so that every member keeps at least one token of its own (the token being
-    decoded is written to a private page). Groups with fewer than
+    decoded is written to a private page) and before any page that holds some
+    request's append slot (the shared pages are read while the suffix pass
+    appends). Groups with fewer than
     ``min_shared_pages`` shared pages, or a single member, stay on the plain path.
     ``block_table`` / ``context_lens`` are host arrays (or CPU tensors).
     """
@@ -81,6 +83,10 @@ def plan_cascade(block_table, context_lens, num_heads: int, num_kv_heads: int, b
     pages, members, work, merge, groups = [], [], [], [], []
     max_chunks = 1
     shared_tokens = 0
+    # pages that receive this step's appended token (position ctx - 1)
+    last = (ctx - 1) // block_size
+    has_last = (ctx >= 1) & (last < MB)
+    append_pages = np.unique(bt[np.nonzero(has_last)[0], last[has_last]])
     eligible = np.nonzero((ctx > block_size) & (bt[:, 0] >= 0))[0]
     firsts = bt[eligible, 0]
     for first in np.unique(firsts):
@@ -91,6 +97,9 @@ def plan_cascade(block_table, context_lens, num_heads: int, num_kv_heads: int, b
         eq = np.all(rows == rows[0], axis=0) & (rows[0] >= 0)
         P = int(np.argmin(eq)) if not eq.all() else MB
         P = min(P, int(((ctx[mem] - 1) // block_size).min()))
+        hit = np.isin(rows[0, :P], append_pages)
+        if hit.any():
+            P = int(np.argmax(hit))
         if P < min_shared_pages:
             continue
         n_chunks = (P + MAX_CHUNK_PAGES - 1) // MAX_CHUNK_PAGES
@@ -180,14 +189,18 @@ def paged_attention_cascade(q: torch.Tensor, k_cache: torch.Tensor, v_cache: tor
         buf.data_ptr(), buf.numel(), st_)
     _L.check(st, "cascade suffix pass")
     if plan.num_work:
+        # Both follow a kernel of this call on the stream, so they start while it
+        # drains: the suffix pass writes no shared page (the plan keeps every
+        # request's append page private) and neither writes the plan arrays.
         st = lib.ubx_cascade_prefix_attention(
             q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0),
             k_cache.stride(1), k_cache.stride(2), NB, plan.page_list.data_ptr(), plan.member_list.data_ptr(),
             plan.work.data_ptr(), plan.num_work, plan.max_chunks, B, H, KVH, D, float(scale), dt,
-            plan._ws.data_ptr(), plan._ws.numel(), dws.error_word_ptr(), st_)
+            plan._ws.data_ptr(), plan._ws.numel(), dws.error_word_ptr(), _L.FLAG_OVERLAP_PREVIOUS, st_)
         _L.check(st, "cascade prefix pass")
         st = lib.ubx_cascade_merge(out.data_ptr(), out.stride(0), out.stride(1), plan._lse.data_ptr(),
                                    plan.merge_items.data_ptr(), plan.num_merge, plan.max_chunks, B, H, D, dt,
-                                   plan._ws.data_ptr(), plan._ws.numel(), dws.error_word_ptr(), st_)
+                                   plan._ws.data_ptr(), plan._ws.numel(), dws.error_word_ptr(),
+                                   _L.FLAG_OVERLAP_PREVIOUS, st_)
         _L.check(st, "cascade merge")
     return out

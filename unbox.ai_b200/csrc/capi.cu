@@ -595,8 +595,10 @@ int ubx_cascade_prefix_attention(const void* q, int64_t q_s_b, int64_t q_s_h, co
                                  int64_t num_blocks, const int32_t* page_list, const int32_t* member_list,
                                  const int32_t* work_items, int num_work_items, int max_chunks, int batch,
                                  int num_heads, int num_kv_heads, int head_dim, float scale, int dtype,
-                                 void* cascade_ws, size_t cascade_ws_bytes, int32_t* error_word, void* stream) {
+                                 void* cascade_ws, size_t cascade_ws_bytes, int32_t* error_word, int flags,
+                                 void* stream) {
   g_last_error.clear();
+  if (flags & ~UBX_FLAG_OVERLAP_PREVIOUS) return fail(UBX_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
   int st = check_shape(num_heads, num_kv_heads, head_dim, kBlockSize, dtype);
   if (st != UBX_OK) return st;
   if (dtype == UBX_DTYPE_F32) return fail(UBX_ERR_UNSUPPORTED, "the cascade pass is built for bf16/f16");
@@ -639,6 +641,7 @@ int ubx_cascade_prefix_attention(const void* q, int64_t q_s_b, int64_t q_s_h, co
   p.part_ml = reinterpret_cast<float2*>(ws);
   p.part_o = reinterpret_cast<float*>(ws + cascade_ml_bytes(batch, num_heads, max_chunks));
   p.error = error_word;
+  p.overlap = (flags & UBX_FLAG_OVERLAP_PREVIOUS) != 0;
   cudaError_t e = launch_cascade_prefix(dtype, head_dim, p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "cascade prefix launch");
   return UBX_OK;
@@ -646,8 +649,10 @@ int ubx_cascade_prefix_attention(const void* q, int64_t q_s_b, int64_t q_s_h, co
 
 int ubx_cascade_merge(void* out, int64_t o_s_b, int64_t o_s_h, const float* lse, const int32_t* merge_items,
                       int num_merge_items, int max_chunks, int batch, int num_heads, int head_dim, int dtype,
-                      const void* cascade_ws, size_t cascade_ws_bytes, int32_t* error_word, void* stream) {
+                      const void* cascade_ws, size_t cascade_ws_bytes, int32_t* error_word, int flags,
+                      void* stream) {
   g_last_error.clear();
+  if (flags & ~UBX_FLAG_OVERLAP_PREVIOUS) return fail(UBX_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
   if (dtype != UBX_DTYPE_BF16 && dtype != UBX_DTYPE_F16)
     return fail(UBX_ERR_UNSUPPORTED, "the cascade merge is built for bf16/f16");
   if (head_dim != 64 && head_dim != 112 && head_dim != 128)
@@ -676,6 +681,7 @@ int ubx_cascade_merge(void* out, int64_t o_s_b, int64_t o_s_h, const float* lse,
   p.part_ml = reinterpret_cast<const float2*>(ws);
   p.part_o = reinterpret_cast<const float*>(ws + cascade_ml_bytes(batch, num_heads, max_chunks));
   p.error = error_word;
+  p.overlap = (flags & UBX_FLAG_OVERLAP_PREVIOUS) != 0;
   cudaError_t e = launch_cascade_merge(dtype, head_dim, p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "cascade merge launch");
   return UBX_OK;

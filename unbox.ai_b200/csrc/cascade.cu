@@ -33,12 +33,18 @@ __global__ void __launch_bounds__(kCascadeWarps * 32) cascade_prefix_kernel(cons
   constexpr int NT = D / 8;   // PV n-tiles
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int kvh = blockIdx.y;
+  // Launched with programmatic overlap, this CTA may run while the previous
+  // kernel drains: it reads only the plan arrays and the shared pages before
+  // griddepcontrol.wait (the caller's promise), and q, the workspace and the
+  // error word after it. Without the launch attribute the wait returns at once.
+  griddep_launch_dependents();
   const int32_t* item = p.work + kCascadeWorkInts * blockIdx.x;
   const int m_off = __ldg(item + 0), n_mem = __ldg(item + 1), pg_off = __ldg(item + 2), n_pg = __ldg(item + 3),
             chunk = __ldg(item + 4);
   const int G = p.num_heads / p.num_kv_heads;
   if (n_pg < 1 || n_pg > kCascadeMaxPages || n_mem < 1 || n_mem * G > kCascadeWarps * 16 || chunk < 0 ||
       chunk >= p.max_chunks) {
+    griddep_wait();
     if (threadIdx.x == 0) set_error(p.error, kErrBadWork);
     return;
   }
@@ -51,6 +57,7 @@ __global__ void __launch_bounds__(kCascadeWarps * 32) cascade_prefix_kernel(cons
   // ---- load: every thread copies 16-byte pieces of the chunk's K and V rows of
   // this head (cp.async, no register staging); rows of a bad page are zeroed
   const int total = n_pg * 2 * kBlockSize * kVecPerRow;
+  bool bad_page = false;
   for (int v = threadIdx.x; v < total; v += kCascadeWarps * 32) {
     const int row = v / kVecPerRow, cv = v - row * kVecPerRow;
     const int i = row / (2 * kBlockSize), r = row % (2 * kBlockSize);
@@ -64,10 +71,12 @@ __global__ void __launch_bounds__(kCascadeWarps * 32) cascade_prefix_kernel(cons
                            cv * 16;
       cp_async_16(dst, src);
     } else {
-      if (tok == 0 && cv == 0 && !is_v) set_error(p.error, kErrBadPage);
+      if (tok == 0 && cv == 0 && !is_v) bad_page = true;
       *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
     }
   }
+  griddep_wait();  // the page copies stay in flight across the wait
+  if (bad_page) set_error(p.error, kErrBadPage);
   cp_async_commit_wait_all();
   __syncthreads();
 
@@ -206,10 +215,14 @@ __global__ void __launch_bounds__(128) cascade_merge_kernel(const CascadeMergePa
   constexpr int EPC = Elem<T>::kPerChunk;
   constexpr int DCH = D / EPC;
   const int lane = threadIdx.x & 31;
+  // programmatic overlap: only the merge items are read before the wait
+  griddep_launch_dependents();
   const int64_t gw = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
-  if (gw >= (int64_t)p.num_items * p.num_heads) return;
-  const int it = (int)(gw / p.num_heads), h = (int)(gw % p.num_heads);
-  const int b = __ldg(&p.items[2 * it]), nch = __ldg(&p.items[2 * it + 1]);
+  const bool in_range = gw < (int64_t)p.num_items * p.num_heads;
+  const int it = in_range ? (int)(gw / p.num_heads) : 0, h = in_range ? (int)(gw % p.num_heads) : 0;
+  const int b = in_range ? __ldg(&p.items[2 * it]) : 0, nch = in_range ? __ldg(&p.items[2 * it + 1]) : 0;
+  griddep_wait();
+  if (!in_range) return;
   if (b < 0 || b >= p.batch || nch < 0 || nch > p.max_chunks) {
     if (lane == 0) set_error(p.error, kErrBadWork);
     return;
@@ -252,6 +265,26 @@ __global__ void __launch_bounds__(128) cascade_merge_kernel(const CascadeMergePa
   *reinterpret_cast<uint4*>(row) = Elem<T>::pack(o);
 }
 
+// Launch with or without programmatic dependent launch (the kernel may start
+// while the previous kernel on the stream drains).
+template <typename Params>
+cudaError_t launch_overlapped(void (*kernel)(const Params), dim3 grid, dim3 block, int smem, cudaStream_t st,
+                              bool overlap, const Params& p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = overlap ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
 template <typename T>
 cudaError_t launch_prefix_t(int head_dim, const CascadeParams& p, int smem, cudaStream_t st) {
   void (*kernel)(const CascadeParams);
@@ -271,21 +304,20 @@ cudaError_t launch_prefix_t(int head_dim, const CascadeParams& p, int smem, cuda
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) attr_done[slot][dev] = 1;
   }
-  kernel<<<dim3(p.num_work, p.num_kv_heads), dim3(kCascadeWarps * 32), smem, st>>>(p);
-  return cudaGetLastError();
+  return launch_overlapped(kernel, dim3(p.num_work, p.num_kv_heads), dim3(kCascadeWarps * 32), smem, st, p.overlap,
+                           p);
 }
 
 template <typename T>
 cudaError_t launch_merge_t(int head_dim, const CascadeMergeParams& p, cudaStream_t st) {
   const int64_t warps = (int64_t)p.num_items * p.num_heads;
-  const int blocks = (int)((warps + 3) / 4);
+  const dim3 blocks((unsigned)((warps + 3) / 4));
   switch (head_dim) {
-    case 64: cascade_merge_kernel<T, 64><<<blocks, 128, 0, st>>>(p); break;
-    case 112: cascade_merge_kernel<T, 112><<<blocks, 128, 0, st>>>(p); break;
-    case 128: cascade_merge_kernel<T, 128><<<blocks, 128, 0, st>>>(p); break;
+    case 64: return launch_overlapped(cascade_merge_kernel<T, 64>, blocks, dim3(128), 0, st, p.overlap, p);
+    case 112: return launch_overlapped(cascade_merge_kernel<T, 112>, blocks, dim3(128), 0, st, p.overlap, p);
+    case 128: return launch_overlapped(cascade_merge_kernel<T, 128>, blocks, dim3(128), 0, st, p.overlap, p);
     default: return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
 }
 
 }  // namespace

@@ -200,6 +200,7 @@ struct CascadeParams {
   float* part_o;               // [batch][num_heads][max_chunks][D]
   float2* part_ml;             // [batch][num_heads][max_chunks] (max in log2 units, sum)
   int32_t* error;
+  bool overlap;                // programmatic dependent launch; shared pages load before the wait
 };
 
 struct CascadeMergeParams {
@@ -212,6 +213,7 @@ struct CascadeMergeParams {
   const float* part_o;
   const float2* part_ml;
   int32_t* error;
+  bool overlap;                // programmatic dependent launch
 };
 
 int cascade_smem_bytes(int head_dim, int elem_bytes, int num_pages);
