@@ -205,64 +205,87 @@ __global__ void __launch_bounds__(kCascadeWarps * 32) cascade_prefix_kernel(cons
   }
 }
 
-// One warp per (merge item, query head). Part 0 is the suffix pass: its
-// normalised output row with weight 2^lse (acc = row, max = lse, sum = 1);
-// parts 1.. are the prefix chunks. The lanes first read every part's (max, sum)
-// in parallel for the common max and the denominator, then lanes = 16-byte
-// output chunks add the weighted rows, all parts' loads independent.
+// One warp task per (merge item, group of 32 / (D / 8) query heads); lanes are
+// (head, 16-byte output chunk). Part 0 is the suffix pass: its normalised
+// output row with weight 2^lse (acc = row, max = lse, sum = 1); parts 1.. are
+// the prefix chunks. Parts are read kMergeBatch at a time, every load of a
+// batch issued before any is used, and folded in with a running max: a merge
+// of up to kMergeBatch chunks costs about two memory round trips.
+constexpr int kMergeBatch = 8;
+
 template <typename T, int D>
-__global__ void __launch_bounds__(128) cascade_merge_kernel(const CascadeMergeParams p) {
+__device__ __forceinline__ void merge_task(const CascadeMergeParams& p, int64_t task, int hgroups, int lane) {
   constexpr int EPC = Elem<T>::kPerChunk;
-  constexpr int DCH = D / EPC;
-  const int lane = threadIdx.x & 31;
-  // programmatic overlap: only the merge items are read before the wait
-  griddep_launch_dependents();
-  const int64_t gw = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
-  const bool in_range = gw < (int64_t)p.num_items * p.num_heads;
-  const int it = in_range ? (int)(gw / p.num_heads) : 0, h = in_range ? (int)(gw % p.num_heads) : 0;
-  const int b = in_range ? __ldg(&p.items[2 * it]) : 0, nch = in_range ? __ldg(&p.items[2 * it + 1]) : 0;
-  griddep_wait();
-  if (!in_range) return;
+  constexpr int DCH = D / EPC;   // output chunks per row
+  constexpr int HPW = 32 / DCH;  // heads per warp
+  const int it = (int)(task / hgroups);
+  const int h = (int)(task % hgroups) * HPW + lane / DCH, c = lane % DCH;
+  const int b = __ldg(&p.items[2 * it]), nch = __ldg(&p.items[2 * it + 1]);
   if (b < 0 || b >= p.batch || nch < 0 || nch > p.max_chunks) {
     if (lane == 0) set_error(p.error, kErrBadWork);
     return;
   }
+  if (lane >= HPW * DCH || h >= p.num_heads) return;  // no warp collectives below
   const int64_t slot0 = ((int64_t)b * p.num_heads + h) * p.max_chunks;
+  T* row = static_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + c * EPC;
   const float lse = p.lse[(int64_t)b * p.num_heads + h];  // -inf: empty suffix
-  float M = lse;
-  for (int k = lane; k < nch; k += 32) M = fmaxf(M, __ldcg(&p.part_ml[slot0 + k]).x);
-  M = warp_max(M);
-  float L = 0.f;
-  for (int k = lane; k < nch; k += 32) {
-    const float2 ml = __ldcg(&p.part_ml[slot0 + k]);
-    L = fmaf(ml.y, exp2f(ml.x - M), L);
-  }
-  L = warp_sum(L);
-  const float w_s = lse == -INFINITY ? 0.f : exp2f(lse - M);  // 0 for an empty suffix
-  L += w_s;
-  if (lane >= DCH) return;
-  T* row = static_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + lane * EPC;
   float o[EPC];
   Elem<T>::unpack(*reinterpret_cast<const uint4*>(row), o);
+  float M = lse, L = 1.f;
+  if (lse == -INFINITY) {
+    L = 0.f;
 #pragma unroll
-  for (int e = 0; e < EPC; ++e) o[e] *= w_s;
-#pragma unroll 4
-  for (int k = 0; k < nch; ++k) {
-    const float wgt = exp2f(__ldcg(&p.part_ml[slot0 + k]).x - M);
-    const float4* src = reinterpret_cast<const float4*>(p.part_o + (slot0 + k) * D + lane * EPC);
+    for (int e = 0; e < EPC; ++e) o[e] = 0.f;
+  }
+  for (int k0 = 0; k0 < nch; k0 += kMergeBatch) {
+    float2 ml[kMergeBatch];
+    float4 v[kMergeBatch][EPC / 4];
 #pragma unroll
-    for (int e4 = 0; e4 < EPC / 4; ++e4) {
-      const float4 v = __ldcg(src + e4);
-      o[4 * e4 + 0] = fmaf(wgt, v.x, o[4 * e4 + 0]);
-      o[4 * e4 + 1] = fmaf(wgt, v.y, o[4 * e4 + 1]);
-      o[4 * e4 + 2] = fmaf(wgt, v.z, o[4 * e4 + 2]);
-      o[4 * e4 + 3] = fmaf(wgt, v.w, o[4 * e4 + 3]);
+    for (int j = 0; j < kMergeBatch; ++j) {
+      const bool have = k0 + j < nch;
+      const int64_t slot = slot0 + k0 + (have ? j : 0);
+      ml[j] = have ? __ldcg(&p.part_ml[slot]) : make_float2(-INFINITY, 0.f);
+      const float4* src = reinterpret_cast<const float4*>(p.part_o + slot * D + c * EPC);
+#pragma unroll
+      for (int e4 = 0; e4 < EPC / 4; ++e4) v[j][e4] = have ? __ldcg(src + e4) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int j = 0; j < kMergeBatch; ++j) {
+      if (ml[j].x == -INFINITY) continue;  // past the last chunk
+      if (ml[j].x > M) {
+        const float sc = exp2f(M - ml[j].x);  // M = -inf (empty suffix, first part): 0
+        L *= sc;
+#pragma unroll
+        for (int e = 0; e < EPC; ++e) o[e] *= sc;
+        M = ml[j].x;
+      }
+      const float w = exp2f(ml[j].x - M);
+      L = fmaf(ml[j].y, w, L);
+#pragma unroll
+      for (int e4 = 0; e4 < EPC / 4; ++e4) {
+        o[4 * e4 + 0] = fmaf(w, v[j][e4].x, o[4 * e4 + 0]);
+        o[4 * e4 + 1] = fmaf(w, v[j][e4].y, o[4 * e4 + 1]);
+        o[4 * e4 + 2] = fmaf(w, v[j][e4].z, o[4 * e4 + 2]);
+        o[4 * e4 + 3] = fmaf(w, v[j][e4].w, o[4 * e4 + 3]);
+      }
     }
   }
   const float inv = L > 0.f ? 1.f / L : 0.f;
 #pragma unroll
   for (int e = 0; e < EPC; ++e) o[e] *= inv;
   *reinterpret_cast<uint4*>(row) = Elem<T>::pack(o);
+}
+
+// One warp per task.
+template <typename T, int D>
+__global__ void __launch_bounds__(128) cascade_merge_kernel(const CascadeMergeParams p) {
+  constexpr int HPW = 32 / (D / Elem<T>::kPerChunk);
+  const int lane = threadIdx.x & 31;
+  griddep_launch_dependents();
+  griddep_wait();  // the suffix and prefix passes have completed
+  const int hgroups = (p.num_heads + HPW - 1) / HPW;
+  const int64_t t = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (t < (int64_t)p.num_items * hgroups) merge_task<T, D>(p, t, hgroups, lane);
 }
 
 // Launch with or without programmatic dependent launch (the kernel may start
@@ -310,7 +333,8 @@ cudaError_t launch_prefix_t(int head_dim, const CascadeParams& p, int smem, cuda
 
 template <typename T>
 cudaError_t launch_merge_t(int head_dim, const CascadeMergeParams& p, cudaStream_t st) {
-  const int64_t warps = (int64_t)p.num_items * p.num_heads;
+  const int hpw = 32 / (head_dim / 8);  // heads per warp (16-byte chunks of 16-bit elements)
+  const int64_t warps = (int64_t)p.num_items * ((p.num_heads + hpw - 1) / hpw);
   const dim3 blocks((unsigned)((warps + 3) / 4));
   switch (head_dim) {
     case 64: return launch_overlapped(cascade_merge_kernel<T, 64>, blocks, dim3(128), 0, st, p.overlap, p);
