@@ -229,8 +229,9 @@ int ubx_paged_decode_prep_attention(const void* q_raw, int64_t q_s_b, int64_t q_
  * head), lse_out[b * num_heads + h] = log2 of the softmax denominator in the
  * exp2 domain: max_j(s_j) + log2(sum_j 2^(s_j - max)), s_j = scale * log2(e) *
  * q . K_j (-inf for an empty context). k_new / v_new may both be NULL (no
- * append). bf16/f16. Used by the cascade below (the suffix pass); no counterpart
- * in the reference.
+ * append). bf16/f16. Used by the cascade below (the suffix pass), so it leaves
+ * 4 KB of each SM's shared memory to the small CTAs of the launches that follow
+ * it with programmatic overlap; no counterpart in the reference.
  */
 int ubx_paged_decode_attention_lse(const void* k_new, const void* v_new, int64_t new_s_tok, int64_t new_s_head,
                                    const void* q, int64_t q_s_b, int64_t q_s_h, void* k_cache, void* v_cache,

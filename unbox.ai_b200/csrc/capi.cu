@@ -93,8 +93,11 @@ struct Plan {
   int64_t slots;
 };
 
+// smem_reserve: shared memory per SM left to the small CTAs of the launches
+// that follow (with programmatic overlap they become resident while this grid
+// runs, and a CTA reserves 1 KB even with no shared memory of its own).
 int make_plan(int batch, int num_heads, int num_kv_heads, int head_dim, int dtype, int max_blocks, int schedule,
-              int split_pages, int num_sms, Plan* pl) {
+              int split_pages, int num_sms, Plan* pl, int smem_reserve = 0) {
   const int G = num_heads / num_kv_heads;
   const int es = dtype_bytes(dtype);
   const bool mma = es == 2;  // 16-bit: tensor-core consumer, one warp per KV head
@@ -129,8 +132,8 @@ int make_plan(int batch, int num_heads, int num_kv_heads, int head_dim, int dtyp
   const int ncw = pl->hg * pl->wpk;
   int ctas = std::min(kMaxCtasPerSm, (kMaxConsumerWarps + ncw - 1) / ncw);
   for (;; --ctas) {
-    const int budget = ctas == 1 ? kSmemLimit : kSmemPerSm / ctas - kSmemReservedPerCta;
-    pl->stages = std::min(6, (budget - fixed) / (2 * pl->tile));
+    const int budget = (ctas == 1 ? kSmemLimit : kSmemPerSm / ctas - kSmemReservedPerCta) - smem_reserve / ctas;
+    pl->stages = std::min(6, (budget - fixed) / (2 * pl->tile + kStageSlotBytes));
     if (pl->stages >= 2 || ctas == 1) break;
   }
   if (pl->stages < 2) return fail(UBX_ERR_UNSUPPORTED, "shared memory too small for a 2-stage pipeline");
@@ -438,8 +441,12 @@ int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache
   int sms = 0;
   st = num_sms_current_device(&sms);
   if (st != UBX_OK) return st;
+  // The log-sum-exp variant is the cascade's suffix pass: its prefix and merge
+  // launches follow with programmatic overlap, so leave their CTAs room.
+  const int reserve = lse ? kCascadeFollowerSmem : 0;
   Plan pl;
-  st = make_plan(batch, num_heads, num_kv_heads, head_dim, dtype, max_blocks_per_seq, schedule, split_pages, sms, &pl);
+  st = make_plan(batch, num_heads, num_kv_heads, head_dim, dtype, max_blocks_per_seq, schedule, split_pages, sms, &pl,
+                 reserve);
   if (st != UBX_OK) return st;
   if (pl.dynamic) {
     // the producer copies the appended token's heads as one row: they must be contiguous in k_new / v_new
@@ -450,7 +457,7 @@ int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache
                   head_dim);
     if (schedule == UBX_SCHEDULE_AUTO && (!rows_ok || !fits)) {
       st = make_plan(batch, num_heads, num_kv_heads, head_dim, dtype, max_blocks_per_seq, UBX_SCHEDULE_BALANCED,
-                     split_pages, sms, &pl);
+                     split_pages, sms, &pl, reserve);
       if (st != UBX_OK) return st;
     }
   }

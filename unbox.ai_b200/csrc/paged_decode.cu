@@ -351,16 +351,18 @@ struct Smem {
   int32_t* prefix;
 };
 
-// Layout: [stages][p_buf][full x kMaxStages][empty x kMaxStages][info x kMaxStages][prefix]
+// Layout: [stages][p_buf][full x stages][empty x stages][info x stages][prefix]
+// (per-stage slots sized by the launch's stage count: every byte counts toward
+// fitting one more stage)
 __device__ __forceinline__ Smem carve_smem(uint8_t* smem, const DecodeParams& p) {
   Smem s;
   const int stage_bytes = 2 * p.tile_bytes;
   s.stages = smem;
   s.p_buf = reinterpret_cast<float*>(smem + p.stages * stage_bytes);
   s.full_bar = reinterpret_cast<uint64_t*>(smem + p.stages * stage_bytes + p.pbuf_bytes);
-  s.empty_bar = s.full_bar + kMaxStages;
-  s.info = reinterpret_cast<int4*>(s.empty_bar + kMaxStages);
-  s.prefix = reinterpret_cast<int32_t*>(s.info + kMaxStages);
+  s.empty_bar = s.full_bar + p.stages;
+  s.info = reinterpret_cast<int4*>(s.empty_bar + p.stages);  // 16-byte aligned: 2 x stages x 8 bytes before
+  s.prefix = reinterpret_cast<int32_t*>(s.info + p.stages);
   return s;
 }
 
@@ -1522,7 +1524,7 @@ __global__ void __launch_bounds__(128) lse_combine_kernel(const DecodeParams p) 
 // ---------------------------------------------------------------- host side
 
 int decode_smem_bytes(int tile_bytes, int pbuf_bytes, int stages, int prefix_entries) {
-  return stages * 2 * tile_bytes + pbuf_bytes + 2 * kMaxStages * 8 + kMaxStages * 16 + prefix_entries * 4;
+  return stages * (2 * tile_bytes + kStageSlotBytes) + pbuf_bytes + prefix_entries * 4;
 }
 
 template <typename Kern>

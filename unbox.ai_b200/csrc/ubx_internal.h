@@ -8,14 +8,16 @@
 namespace ubx {
 
 constexpr int kBlockSize = 16;          // tokens per page (configs/infer/serve.yaml block_size)
-constexpr int kMaxStages = 8;           // pipeline depth limit (mbarrier slots reserved)
+constexpr int kMaxStages = 8;           // pipeline depth limit
+constexpr int kStageSlotBytes = 2 * 8 + 16;  // per stage: full and empty mbarriers, stage record
 constexpr int kMaxConsumerWarps = 8;    // consumer warps per CTA
 constexpr int kMaxBatchSmem = 2048;     // balanced schedule keeps a (B+1) page prefix in smem
 constexpr int kMaxTileBytes = 36864;    // one K (or V) page tile of a head group
-constexpr int kSmemLimit = 227 * 1024 - 512;  // dynamic smem budget: 227 KB opt-in minus static smem
+constexpr int kSmemLimit = 227 * 1024 - 256;  // dynamic smem budget: 227 KB opt-in minus static smem (128 B)
 constexpr int kSmemPerSm = 228 * 1024;        // shared memory of one SM
 constexpr int kSmemReservedPerCta = 1024 + 512;  // per-CTA reservation + static smem
 constexpr int kMaxCtasPerSm = 4;              // CTAs of one balanced launch per SM (small head groups)
+constexpr int kCascadeFollowerSmem = 4096;     // per SM, left by the cascade's suffix pass to the merge CTAs
 
 // Dynamic (work-sharing) schedule.
 constexpr int kDynOwnerPages = 16;    // most pages a CTA takes from its own range per grab
