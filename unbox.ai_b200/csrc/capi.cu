@@ -37,10 +37,11 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // ---- workspace layout (fixed prefix so that counters stay zero across calls)
 constexpr size_t kHeaderBytes = kWsHeaderBytes;        // error word + reserved
 constexpr size_t kCounterEntries = kWsCounterEntries;  // merge counters, re-armed by the kernel
-constexpr size_t kCounterBytes = kWsCounterBytes;      // zeroed once by ubx_workspace_init
 constexpr int kDefaultSplitPages = 32;                 // 512-token split-KV chunks
-// The library's own choice under UBX_SCHEDULE_AUTO for bf16/f16 batches the
-// balanced schedule can take: the dynamic (work-sharing) variant.
+// Whether UBX_SCHEDULE_AUTO picks the dynamic (work-sharing) variant for the
+// bf16/f16 batches the balanced schedule can take. Off: on the measured
+// workloads the dynamic kernel streams each page more slowly than the balanced
+// one gains by evening out the CTAs' end times.
 constexpr bool kAutoDynamic = false;
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
