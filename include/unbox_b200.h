@@ -253,8 +253,8 @@ int ubx_paged_decode_attention_lse(const void* k_new, const void* v_new, int64_t
  *      the fused append, writing out and lse;
  *   2. ubx_cascade_prefix_attention: for each work item and KV head, one CTA
  *      loads up to 8 shared pages of that head once and runs all the item's
- *      requests over them in 16-row tensor-core tiles (4 per CTA), writing per-chunk partials
- *      into the cascade workspace;
+ *      (request, query head) rows over them as one 128-row tile on the tcgen05
+ *      tensor cores, writing per-chunk partials into the cascade workspace;
  *   3. ubx_cascade_merge: out[b, h] = merge(suffix row with weight 2^lse, chunk partials).
  * Replaces, for those requests, the per-request re-reading of shared pages in
  * paged_decode_attention_ref (unbox_platform/infer/kernels/paged_decode_attention.py:157-191).
@@ -262,7 +262,7 @@ int ubx_paged_decode_attention_lse(const void* k_new, const void* v_new, int64_t
  *   member_list: int32, the member sequences of every group, concatenated
  *   work_items:  int32 [num_work_items][6] = (member offset, member count, page
  *                offset, page count <= 8, chunk index < max_chunks, 0); member
- *                count * (num_heads / num_kv_heads) <= 64
+ *                count * (num_heads / num_kv_heads) <= 128
  *   merge_items: int32 [num_merge_items][2] = (sequence, number of its prefix chunks)
  *   cascade_ws:  ubx_cascade_workspace_size bytes (no initialisation needed)
  *   flags:       UBX_FLAG_OVERLAP_PREVIOUS = programmatic dependent launch: the

@@ -13,9 +13,9 @@ groups of requests whose block-table rows start with the same pages, and
 
 with one launch for every request's suffix (the balanced decode kernel, KV
 append fused, returning log-sum-exps), one launch for all groups' shared pages
-(each page chunk of a KV head loaded into shared memory once for all the
-group's requests, tensor-core tiles of 16 (request, head) rows), and one merge
-launch. Softmax splits exactly over disjoint key sets, so the result is the
+(each page chunk of a KV head loaded into shared memory once for up to 128
+(request, head) rows of the group, tcgen05 tensor-core MMAs with accumulators
+in tensor memory), and one merge launch. Softmax splits exactly over disjoint key sets, so the result is the
 attention over the whole context.
 """
 from __future__ import annotations
@@ -31,7 +31,7 @@ from . import library as _L
 from .ops import _DTYPES, _SCHEDULES, _require_cuda, _stream, workspace_for
 
 MAX_CHUNK_PAGES = 8     # shared pages one CTA holds (kCascadeMaxPages)
-TILE_ROWS = 64          # (request, head) rows one CTA covers: 4 warps x 16
+TILE_ROWS = 128         # (request, head) rows one CTA covers: the M of its tensor-core tile
 WORK_INTS = 6
 
 

@@ -7,31 +7,58 @@
 //   1. the decode kernel attends each request over its private suffix pages
 //      (positions past the shared prefix) and also returns the log-sum-exp;
 //   2. cascade_prefix_kernel attends every request of a prefix group over the
-//      shared pages at once: a CTA loads a chunk of the shared pages of one KV
-//      head into shared memory once, and each warp runs a 16-row tensor-core
-//      tile of (request, query head) rows of that group over them (mma.sync
-//      m16n8k16, full tiles: G query heads x 16/G requests), writing unnormalised
-//      partial (acc, max, sum) rows per chunk;
+//      shared pages at once: a CTA loads a chunk of up to 8 shared pages of one
+//      KV head into shared memory once, with the q rows of up to 128 (request,
+//      query head) pairs of that group, and runs S = Q K^T and O = P V as two
+//      chains of 5th-generation tensor-core MMAs (tcgen05.mma, M = 128, fp32
+//      accumulators in tensor memory), the softmax in between on one thread per
+//      row; it writes unnormalised partial (acc, max, sum) rows per chunk;
 //   3. cascade_merge_kernel merges the suffix output with the chunks' partials by
 //      log-sum-exp weights (the same combination the split-KV path uses).
 // The result equals attention over the whole context (softmax is exactly
 // decomposable over disjoint key sets).
+#include <type_traits>
+
 #include "ubx_common.cuh"
 #include "ubx_internal.h"
 #include "ubx_mma.cuh"
+#include "ubx_tcgen05.cuh"
 
 namespace ubx {
 
 namespace {
 
-constexpr unsigned kAll = 0xffffffffu;
+// Shared-memory layout of one prefix CTA (tcgen05 operands, SWIZZLE_NONE
+// canonical layout: a tile of R rows x C 16-byte chunks is stored chunk-major,
+// [chunk][row][16 B], so 8 consecutive rows of one chunk form a contiguous
+// 128-byte core matrix):
+//   Q [D/8][128 rows][16 B]  (rows = (member, query head), member-major)
+//   K [D/8][128 tokens][16 B], V [D/8][128 tokens][16 B]
+//   P [128/8 token chunks][128 rows][16 B] over Q and K once S is complete
+//   2 mbarriers, the TMEM base address, the row max / sum of each half [2][128]
+constexpr int kTcRows = kCascadeRows;               // M of both MMAs
+constexpr int kTcTokens = kCascadeMaxPages * 16;    // N of S, K of O (at most)
+constexpr uint32_t kTcCols = 256;                   // TMEM: S (128 columns) + O (head_dim <= 128)
+constexpr int kTcThreads = 256;                     // two threads per row: one per column half
+constexpr int kTcTailBytes = 64 + 2 * 2 * kTcRows * 4 + (kCascadeMaxPages + kTcRows) * 4;
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kCascadeWarps * 32) cascade_prefix_kernel(const CascadeParams p) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  constexpr int KS = D / 16;  // QK k-steps
-  constexpr int NT = D / 8;   // PV n-tiles
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+__global__ void __launch_bounds__(kTcThreads) cascade_prefix_kernel(const CascadeParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  constexpr int CH = D / 8;  // 16-byte chunks of a head row
+  constexpr int R = kTcRows, TT = kTcTokens, NTH = kTcThreads;
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  uint8_t* q_s = smem;
+  uint8_t* k_s = q_s + CH * R * 16;
+  uint8_t* v_s = k_s + CH * TT * 16;
+  uint8_t* p_s = smem;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(v_s + CH * TT * 16);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 2);
+  float* red_max = reinterpret_cast<float*>(smem + 3 * CH * R * 16 + 64);  // [2][R], 16-byte aligned
+  float* red_sum = red_max + 2 * R;                                        // [2][R]
+  int32_t* pg_s = reinterpret_cast<int32_t*>(red_sum + 2 * R);             // the chunk's page ids
+  int32_t* mem_s = pg_s + kCascadeMaxPages;                                // the item's member sequences
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int kvh = blockIdx.y;
   // Launched with programmatic overlap, this CTA may run while the previous
   // kernel drains: it reads only the plan arrays and the shared pages before
@@ -42,166 +69,169 @@ __global__ void __launch_bounds__(kCascadeWarps * 32) cascade_prefix_kernel(cons
   const int m_off = __ldg(item + 0), n_mem = __ldg(item + 1), pg_off = __ldg(item + 2), n_pg = __ldg(item + 3),
             chunk = __ldg(item + 4);
   const int G = p.num_heads / p.num_kv_heads;
-  if (n_pg < 1 || n_pg > kCascadeMaxPages || n_mem < 1 || n_mem * G > kCascadeWarps * 16 || chunk < 0 ||
-      chunk >= p.max_chunks) {
+  if (n_pg < 1 || n_pg > kCascadeMaxPages || n_mem < 1 || n_mem * G > R || chunk < 0 || chunk >= p.max_chunks) {
     griddep_wait();
-    if (threadIdx.x == 0) set_error(p.error, kErrBadWork);
+    if (tid == 0) set_error(p.error, kErrBadWork);
     return;
   }
-  constexpr int kRowBytes = D * (int)sizeof(T);  // one KV head row of one token
-  constexpr int kVecPerRow = kRowBytes / 16;
-  const int tile = kBlockSize * p.pitch;          // one page of this head, K or V
-  uint8_t* k_s = smem;
-  uint8_t* v_s = smem + n_pg * tile;
+  const int NT = n_pg * 16;  // tokens of this chunk: N of S, K of O (a multiple of 16)
+  if (warp == 0) tc::tmem_alloc(tmem_slot, kTcCols);
+  if (tid == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    fence_mbar_init();
+  }
+  // the item's page ids and member sequences, read once (plan arrays)
+  if (tid < n_pg) pg_s[tid] = __ldg(&p.page_list[pg_off + tid]);
+  if (tid >= 128 && tid - 128 < n_mem) mem_s[tid - 128] = __ldg(&p.member_list[m_off + tid - 128]);
+  __syncthreads();
 
-  // ---- load: every thread copies 16-byte pieces of the chunk's K and V rows of
-  // this head (cp.async, no register staging); rows of a bad page are zeroed
-  const int total = n_pg * 2 * kBlockSize * kVecPerRow;
+  // ---- K and V of the chunk's pages (this KV head): 16-byte pieces, 8
+  // consecutive lanes = 8 consecutive tokens of one chunk (one core matrix)
   bool bad_page = false;
-  for (int v = threadIdx.x; v < total; v += kCascadeWarps * 32) {
-    const int row = v / kVecPerRow, cv = v - row * kVecPerRow;
-    const int i = row / (2 * kBlockSize), r = row % (2 * kBlockSize);
-    const bool is_v = r >= kBlockSize;
-    const int tok = r & (kBlockSize - 1);
-    uint8_t* dst = (is_v ? v_s : k_s) + i * tile + tok * p.pitch + cv * 16;
-    const int page = __ldg(&p.page_list[pg_off + i]);
+  for (int v = tid; v < 2 * NT * CH; v += NTH) {
+    const int is_v = v >= NT * CH;
+    const int u = is_v ? v - NT * CH : v;
+    const int t = (u / (8 * CH)) * 8 + (u & 7), c = (u >> 3) % CH;
+    uint8_t* dst = (is_v ? v_s : k_s) + (c * TT + t) * 16;
+    const int page = pg_s[t >> 4];
     if (page >= 0 && (int64_t)page < p.num_blocks) {
       const uint8_t* src = static_cast<const uint8_t*>(is_v ? p.v_cache : p.k_cache) +
-                           ((int64_t)page * p.c_sblk + (int64_t)tok * p.c_stok + (int64_t)kvh * D) * sizeof(T) +
-                           cv * 16;
+                           ((int64_t)page * p.c_sblk + (int64_t)(t & 15) * p.c_stok + (int64_t)kvh * D) * sizeof(T) +
+                           c * 16;
       cp_async_16(dst, src);
     } else {
-      if (tok == 0 && cv == 0 && !is_v) bad_page = true;
+      if ((t & 15) == 0 && c == 0 && !is_v) bad_page = true;
       *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
     }
   }
   griddep_wait();  // the page copies stay in flight across the wait
   if (bad_page) set_error(p.error, kErrBadPage);
+  // ---- Q rows: row r = (member r / G, query head kvh * G + r % G); rows past
+  // the members are zero
+  for (int v = tid; v < R * CH; v += NTH) {
+    const int r = (v / (8 * CH)) * 8 + (v & 7), c = (v >> 3) % CH;
+    uint8_t* dst = q_s + (c * R + r) * 16;
+    const int mi = r / G;
+    const int b = mi < n_mem ? mem_s[mi] : -1;
+    if (b >= 0 && b < p.batch) {
+      cp_async_16(dst, static_cast<const uint8_t*>(p.q) +
+                           ((int64_t)b * p.q_sb + (int64_t)(kvh * G + r % G) * p.q_sh) * sizeof(T) + c * 16);
+    } else {
+      *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+    }
+  }
   cp_async_commit_wait_all();
+  fence_proxy_async_smem();  // these generic-proxy writes before the MMAs' reads
+  tc::fence_before_thread_sync();
   __syncthreads();
+  tc::fence_after_thread_sync();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_s = tmem, tmem_o = tmem + TT;  // columns [0, 128) and [128, 128 + D)
 
-  // ---- tiles: 16 rows = (request, query head), request-major; G heads x 16/G requests
-  const int MT = 16 / G;
-  const int n_tiles = (n_mem + MT - 1) / MT;
-  const int qr = lane >> 2, qc = lane & 3;
-  const float c = p.scale_log2;
-  const int rs = p.pitch / (int)sizeof(T);
-  const int k_row = (((lane >> 4) & 1) * 8 + (lane & 7)) * rs + ((lane >> 3) & 1) * 8;
-  const int v_row = (((lane >> 3) & 1) * 8 + (lane & 7)) * rs + ((lane >> 4) & 1) * 8;
-  for (int t = warp; t < n_tiles; t += kCascadeWarps) {
-    int bs[2], head[2];
-    bool real[2];
+  // ---- S = Q K^T (M = 128 rows, N = NT tokens, K = D): A and B K-major
+  if (tid == 0) {
+    const uint32_t idesc = tc::instr_desc_f16(kBf16, R, NT, false, false);
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int r = qr + 8 * h, mi = t * MT + r / G;
-      real[h] = mi < n_mem;
-      bs[h] = real[h] ? __ldg(&p.member_list[m_off + mi]) : 0;
-      real[h] = real[h] && bs[h] >= 0 && bs[h] < p.batch;
-      head[h] = kvh * G + r % G;
-    }
-    uint32_t qa[KS][4];
-    {
-      const T* q0 = static_cast<const T*>(p.q) + (int64_t)bs[0] * p.q_sb + (int64_t)head[0] * p.q_sh;
-      const T* q1 = static_cast<const T*>(p.q) + (int64_t)bs[1] * p.q_sb + (int64_t)head[1] * p.q_sh;
-#pragma unroll
-      for (int ks = 0; ks < KS; ++ks) {
-        qa[ks][0] = real[0] ? __ldg(reinterpret_cast<const uint32_t*>(q0 + 16 * ks + 2 * qc)) : 0u;
-        qa[ks][1] = real[1] ? __ldg(reinterpret_cast<const uint32_t*>(q1 + 16 * ks + 2 * qc)) : 0u;
-        qa[ks][2] = real[0] ? __ldg(reinterpret_cast<const uint32_t*>(q0 + 16 * ks + 8 + 2 * qc)) : 0u;
-        qa[ks][3] = real[1] ? __ldg(reinterpret_cast<const uint32_t*>(q1 + 16 * ks + 8 + 2 * qc)) : 0u;
-      }
-    }
-    float o[NT][4];
-#pragma unroll
-    for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+    for (int ks = 0; ks < D / 16; ++ks)
+      tc::mma_f16(tmem_s, tc::smem_desc(q_s + ks * 2 * R * 16, R * 16, 128),
+                  tc::smem_desc(k_s + ks * 2 * TT * 16, TT * 16, 128), idesc, ks > 0);
+    tc::commit(&bar[0]);
+  }
+  bool ok = mbar_wait_bounded(&bar[0], 0);
+  tc::fence_after_thread_sync();
 
-    // two pages per step: four independent QK accumulation chains, one softmax
-    // update over 32 tokens, then PV of both pages
-    for (int i = 0; i < n_pg; i += 2) {
-      const bool two = i + 1 < n_pg;  // warp-uniform
-      const T* kt0 = reinterpret_cast<const T*>(k_s + i * tile);
-      const T* kt1 = reinterpret_cast<const T*>(k_s + (two ? i + 1 : i) * tile);
-      // S[16 rows x 16 tokens] per page: s[page][n-tile][0..1] row qr, [2..3] row qr + 8
-      float sc[2][2][4] = {};
+  // ---- softmax: warp w reads TMEM lanes 32 (w % 4) ..; thread = (row, column
+  // half h): tokens [64 h, 64 h + 64) of its row
+  const int row = (warp & 3) * 32 + lane, h = warp >> 2;
+  const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+  const int c0 = h * (TT / 2);
+  const float cs = p.scale_log2;
+  float s[TT / 2];
 #pragma unroll
-      for (int ks = 0; ks < KS; ++ks) {
-        uint32_t r0, r1, r2, r3, u0, u1, u2, u3;
-        ldsm_x4(kt0 + k_row + 16 * ks, r0, r1, r2, r3);
-        ldsm_x4(kt1 + k_row + 16 * ks, u0, u1, u2, u3);
-        mma16816<T>(sc[0][0], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], r0, r1);
-        mma16816<T>(sc[0][1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], r2, r3);
-        mma16816<T>(sc[1][0], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], u0, u1);
-        mma16816<T>(sc[1][1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], u2, u3);
-      }
-      if (!two) {  // odd page count: the second page is absent
+  for (int j = 0; j < TT / 32; ++j) {
+    if (c0 + j * 16 < NT) {
+      float v16[16];
+      tc::ld16(tmem_s + lane_off + c0 + j * 16, v16);
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) sc[1][nt][e] = -INFINITY;
-      }
-      float pv[2][2][4];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        float mx = -INFINITY;
-#pragma unroll
-        for (int pg = 0; pg < 2; ++pg)
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt) mx = fmaxf(mx, fmaxf(sc[pg][nt][2 * h], sc[pg][nt][2 * h + 1]));
-        mx = fmaxf(mx, __shfl_xor_sync(kAll, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(kAll, mx, 2));
-        const float m_new = fmaxf(m[h], mx);
-        if (m_new != m[h]) {  // rescale this row only when its max moved
-          const float alpha = exp2f((m[h] - m_new) * c);
-          l[h] *= alpha;
-#pragma unroll
-          for (int n = 0; n < NT; ++n) {
-            o[n][2 * h] *= alpha;
-            o[n][2 * h + 1] *= alpha;
-          }
-          m[h] = m_new;
-        }
-        const float mc = m[h] * c;
-#pragma unroll
-        for (int pg = 0; pg < 2; ++pg)
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt) {
-            pv[pg][nt][2 * h] = exp2f(fmaf(sc[pg][nt][2 * h], c, -mc));
-            pv[pg][nt][2 * h + 1] = exp2f(fmaf(sc[pg][nt][2 * h + 1], c, -mc));
-            l[h] += pv[pg][nt][2 * h] + pv[pg][nt][2 * h + 1];
-          }
-      }
-      // P as the A operand of PV (the S accumulator layout is the A layout)
-#pragma unroll
-      for (int pg = 0; pg < 2; ++pg) {
-        if (pg == 1 && !two) break;
-        const T* vt = reinterpret_cast<const T*>(v_s + (i + pg) * tile);
-        const uint32_t pa0 = Elem<T>::pack2(pv[pg][0][0], pv[pg][0][1]);
-        const uint32_t pa1 = Elem<T>::pack2(pv[pg][0][2], pv[pg][0][3]);
-        const uint32_t pa2 = Elem<T>::pack2(pv[pg][1][0], pv[pg][1][1]);
-        const uint32_t pa3 = Elem<T>::pack2(pv[pg][1][2], pv[pg][1][3]);
-#pragma unroll
-        for (int np = 0; np < NT / 2; ++np) {
-          uint32_t r0, r1, r2, r3;
-          ldsm_x4_trans(vt + v_row + 16 * np, r0, r1, r2, r3);
-          mma16816<T>(o[2 * np], pa0, pa1, pa2, pa3, r0, r1);
-          mma16816<T>(o[2 * np + 1], pa0, pa1, pa2, pa3, r2, r3);
-        }
-      }
+      for (int i = 0; i < 16; ++i) s[j * 16 + i] = v16[i];
     }
-    // ---- partial rows of this chunk
+  }
+  float mx = -INFINITY;
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      float lt = l[h];
-      lt += __shfl_xor_sync(kAll, lt, 1);
-      lt += __shfl_xor_sync(kAll, lt, 2);
-      if (!real[h]) continue;
-      const int64_t slot = ((int64_t)bs[h] * p.num_heads + head[h]) * p.max_chunks + chunk;
-      float2* dst = reinterpret_cast<float2*>(p.part_o + slot * D + 2 * qc);
+  for (int j = 0; j < TT / 2; ++j)
+    if (c0 + j < NT) mx = fmaxf(mx, s[j]);
+  red_max[h * R + row] = mx;
+  __syncthreads();
+  mx = fmaxf(red_max[row], red_max[R + row]);
+  const float mc = mx * cs;
+  float l = 0.f;
 #pragma unroll
-      for (int n = 0; n < NT; ++n) dst[4 * n] = make_float2(o[n][2 * h], o[n][2 * h + 1]);
-      if (qc == 0) p.part_ml[slot] = make_float2(m[h] * c, lt);
+  for (int j8 = 0; j8 < TT / 16; ++j8) {
+    if (c0 + j8 * 8 < NT) {
+      float pv[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        pv[i] = exp2f(fmaf(s[j8 * 8 + i], cs, -mc));
+        l += pv[i];
+      }
+      *reinterpret_cast<uint4*>(p_s + ((c0 / 8 + j8) * R + row) * 16) = Elem<T>::pack(pv);
     }
+  }
+  red_sum[h * R + row] = l;
+  fence_proxy_async_smem();
+  tc::fence_before_thread_sync();
+  __syncthreads();
+  tc::fence_after_thread_sync();
+
+  // ---- O = P V (M = 128 rows, N = D, K = NT tokens): P K-major, V MN-major
+  if (tid == 0) {
+    const uint32_t idesc = tc::instr_desc_f16(kBf16, R, D, false, true);
+    for (int ks = 0; ks < NT / 16; ++ks)
+      tc::mma_f16(tmem_o, tc::smem_desc(p_s + ks * 2 * R * 16, R * 16, 128),
+                  tc::smem_desc(v_s + ks * 2 * 128, 128, TT * 16), idesc, ks > 0);
+    tc::commit(&bar[1]);
+  }
+  ok = mbar_wait_bounded(&bar[1], 0) && ok;
+  tc::fence_after_thread_sync();
+
+  // ---- partial rows of this chunk: unnormalised O and (max in log2 units,
+  // sum). Staged through shared memory (rows of D floats + 16 bytes: 8
+  // consecutive rows fall in 8 different 16-byte bank groups) over Q, K and V,
+  // all consumed, then written row by row with whole warps on each row.
+  constexpr int HD = D / 2;
+  constexpr int OP = D * 4 + 16;  // staged row pitch (bytes)
+  uint8_t* o_s = smem;
+  int64_t* slot_s = reinterpret_cast<int64_t*>(red_max);  // [R], over the row max (consumed)
+#pragma unroll
+  for (int j = 0; j < HD / 8; ++j) {
+    float o8[8];
+    tc::ld8(tmem_o + lane_off + h * HD + j * 8, o8);
+    float4* dst = reinterpret_cast<float4*>(o_s + row * OP + (h * HD + j * 8) * 4);
+    dst[0] = make_float4(o8[0], o8[1], o8[2], o8[3]);
+    dst[1] = make_float4(o8[4], o8[5], o8[6], o8[7]);
+  }
+  if (h == 0) {
+    const int mi = row / G;
+    const int b = mi < n_mem ? mem_s[mi] : -1;
+    const bool real = ok && b >= 0 && b < p.batch;
+    const int64_t slot = ((int64_t)b * p.num_heads + kvh * G + row % G) * p.max_chunks + chunk;
+    slot_s[row] = real ? slot : -1;
+    if (real) p.part_ml[slot] = make_float2(mc, red_sum[row] + red_sum[R + row]);
+  }
+  __syncthreads();
+  for (int v = tid; v < R * (D / 4); v += NTH) {
+    const int r = v / (D / 4), q4 = v - r * (D / 4);
+    const int64_t slot = slot_s[r];
+    if (slot >= 0)
+      reinterpret_cast<float4*>(p.part_o + slot * D)[q4] = *reinterpret_cast<const float4*>(o_s + r * OP + q4 * 16);
+  }
+  if (!ok && tid == 0) set_error(p.error, kErrTimeout);
+  tc::fence_before_thread_sync();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after_thread_sync();
+    tc::tmem_dealloc(tmem, kTcCols);
   }
 }
 
@@ -323,12 +353,11 @@ cudaError_t launch_prefix_t(int head_dim, const CascadeParams& p, int smem, cuda
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_done[slot][dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kCascadeMaxSmem);
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) attr_done[slot][dev] = 1;
   }
-  return launch_overlapped(kernel, dim3(p.num_work, p.num_kv_heads), dim3(kCascadeWarps * 32), smem, st, p.overlap,
-                           p);
+  return launch_overlapped(kernel, dim3(p.num_work, p.num_kv_heads), dim3(kTcThreads), smem, st, p.overlap, p);
 }
 
 template <typename T>
@@ -346,13 +375,17 @@ cudaError_t launch_merge_t(int head_dim, const CascadeMergeParams& p, cudaStream
 
 }  // namespace
 
-int cascade_smem_bytes(int head_dim, int elem_bytes, int num_pages) {
-  return num_pages * 2 * kBlockSize * tile_row_pitch(head_dim * elem_bytes);
+// Q, K and V tiles of 128 rows of 16-bit elements, two mbarriers and the TMEM
+// address; never below 80 KB, so that at most two CTAs share an SM and their
+// tensor memory (2 x 256 columns) never has to wait for a free column.
+int cascade_smem_bytes(int head_dim) {
+  const int need = 3 * kTcRows * head_dim * 2 + kTcTailBytes;
+  return need > kCascadeMinSmem ? need : kCascadeMinSmem;
 }
 
 cudaError_t launch_cascade_prefix(int dtype, int head_dim, const CascadeParams& p, cudaStream_t stream) {
   if (p.num_work == 0) return cudaSuccess;
-  const int smem = cascade_smem_bytes(head_dim, 2, kCascadeMaxPages);
+  const int smem = cascade_smem_bytes(head_dim);
   return dtype == 1 ? launch_prefix_t<__nv_bfloat16>(head_dim, p, smem, stream)
                     : launch_prefix_t<__half>(head_dim, p, smem, stream);
 }

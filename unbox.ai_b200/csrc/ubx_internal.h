@@ -180,10 +180,10 @@ struct KvCopyParams {
 cudaError_t launch_kv_pages_copy(const KvCopyParams& p, cudaStream_t stream);
 
 // Shared-prefix (cascade) pass (cascade.cu).
-constexpr int kCascadeWarps = 4;         // 16-row tiles in flight per CTA
-constexpr int kCascadeMaxPages = 8;      // shared pages one CTA holds in shared memory
+constexpr int kCascadeMaxPages = 8;      // shared pages one CTA holds in shared memory (128 tokens)
 constexpr int kCascadeWorkInts = 6;      // ints per work item
-constexpr int kCascadeMaxSmem = kCascadeMaxPages * 2 * kBlockSize * (128 * 2 + 16);  // head_dim <= 128, 16-bit
+constexpr int kCascadeRows = 128;        // (member, query head) rows of one work item: M of the MMAs
+constexpr int kCascadeMinSmem = 80 * 1024;  // at most two prefix CTAs per SM
 
 struct CascadeParams {
   const void* q;
@@ -218,7 +218,7 @@ struct CascadeMergeParams {
   bool overlap;                // programmatic dependent launch
 };
 
-int cascade_smem_bytes(int head_dim, int elem_bytes, int num_pages);
+int cascade_smem_bytes(int head_dim);
 cudaError_t launch_cascade_prefix(int dtype, int head_dim, const CascadeParams& p, cudaStream_t stream);
 cudaError_t launch_cascade_merge(int dtype, int head_dim, const CascadeMergeParams& p, cudaStream_t stream);
 
