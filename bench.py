@@ -716,8 +716,14 @@ def main():
         h2d += sum(t.numel() * t.element_size() for h, _, _ in hosts for t in h["plan"].values())
     d2h = sum(h["out"].numel() * h["out"].element_size() for h, _, _ in hosts)
     for (h, _, _), o in zip(hosts, outs):
-        assert all(torch.equal(h["out"][l].to(device), o[l]) for l in range(L)), \
-            "end-to-end output differs from the device-resident step"
+        if args.schedule == "dynamic":
+            # grabs and steals split each sequence differently from run to run, so the
+            # partial sums (and the last bit of the output) may differ: the attention tolerance
+            worst = max((h["out"][l].to(device).float() - o[l].float()).abs().max().item() for l in range(L))
+            assert worst <= 2e-2, f"end-to-end output differs from the device-resident step by {worst}"
+        else:
+            assert all(torch.equal(h["out"][l].to(device), o[l]) for l in range(L)), \
+                "end-to-end output differs from the device-resident step"
     del eg
 
     step_bytes_all = reduce(float(bytes_call * L), dist.ReduceOp.SUM)
