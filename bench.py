@@ -455,6 +455,7 @@ def main():
         del dev
         from oracle import oracle
         oracle.build()
+        oracle.use_all_cores()  # torchrun sets OMP_NUM_THREADS=1 for its ranks
         times = []
         for i in range(args.warmup + args.steps):
             t0 = time.perf_counter()
@@ -765,6 +766,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import oracle
         oracle.build()
+        oracle.use_all_cores()
         host = host_layer(devs[0], 0)
         if args.prep:
             host["prep"] = {"q_w": devs[0]["q_w"][0].cpu(), "k_w": devs[0]["k_w"][0].cpu(), "rope": rope.cpu()}

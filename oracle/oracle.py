@@ -58,12 +58,22 @@ def lib():
         L.oracle_slot_mapping.restype = i32
         L.oracle_num_threads.argtypes = []
         L.oracle_num_threads.restype = i32
+        L.oracle_set_num_threads.argtypes = [i32]
+        L.oracle_set_num_threads.restype = i32
         _lib = L
     return _lib
 
 
 def num_threads() -> int:
     return lib().oracle_num_threads()
+
+
+def use_all_cores() -> int:
+    """Run the oracle's parallel regions on every core this process may use
+    (whatever OMP_NUM_THREADS says); returns that thread count."""
+    import os
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    return lib().oracle_set_num_threads(n)
 
 
 def _np(x):

@@ -86,6 +86,16 @@ int oracle_num_threads(void) {
 #endif
 }
 
+/* Threads of the parallel regions that follow (a launcher such as torchrun may
+ * have set OMP_NUM_THREADS=1 for its ranks; the CPU baseline wants every core
+ * it may run on). Returns the count now in effect. */
+int oracle_set_num_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#endif
+  return oracle_num_threads();
+}
+
 /*
  * Paged GQA decode attention, following paged_decode_attention.py:157-191.
  *
