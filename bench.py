@@ -57,8 +57,9 @@ def parse():
                     help="KV append as its own launch before attention (default: fused into one launch)")
     ap.add_argument("--no-overlap", dest="overlap", action="store_false",
                     help="no programmatic dependent launch between consecutive layer-calls")
-    ap.add_argument("--op", choices=["decode", "handoff"], default="decode",
-                    help="decode: the decode layer-call (default); handoff: KV page hand-off between workers")
+    ap.add_argument("--op", choices=["decode", "handoff", "prefill"], default="decode",
+                    help="decode: the decode layer-call (default); handoff: KV page hand-off between workers; "
+                         "prefill: the KV write of a 2048-token prompt chunk into every layer's pool")
     ap.add_argument("--prep", action="store_true",
                     help="layer-call = q/k RMSNorm + rotary embedding + KV append + attention in one launch "
                          "(the attention block between the QKV projection and o_proj)")
@@ -210,6 +211,7 @@ def cpu_layer_call(oracle, host):
 
 PLAN_FIELDS = ("suffix_block_table", "suffix_context_lens", "page_list", "member_list", "work", "merge_items")
 HANDOFF_METRIC = "KV hand-off GB/s of page payload (prefill pool -> decode pool)"
+PREFILL_METRIC = "prefill KV write GB/s of algorithmic bytes (chunk rows -> paged pool)"
 
 
 def bench_handoff(args):
@@ -411,10 +413,262 @@ def bench_handoff(args):
         dist.destroy_process_group()
 
 
+def bench_prefill(args):
+    """One step = the KV write of one 2048-token prompt chunk of the 760M model into
+    all 24 layers' pools (prefill_step, engine.py:121-128): per layer the slot
+    computation over the chunk's positions and one append launch
+    (``ops.prefill_kv_write``), or with ``--prep`` the q/k RMSNorm + rotary + append
+    launch (``ops.prefill_prep``). Inputs > L2: 24 layers' chunk rows (352 MB with
+    q) and 24 pools of 1536 pages. N GPUs: each rank writes its own prompt (weak
+    scaling, no collective on the data path); value = all ranks' bytes / the
+    slowest rank's time."""
+    import torch
+    import torch.distributed as dist
+    from __graft_entry__ import load_package
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    L, T, H, KVH, D, bs, NB = args.layers, 2048, 16, 8, 112, 16, 1536
+    npg = T // bs
+    row_b = KVH * D * 2                      # one token's K (or V) row, bf16
+    # algorithmic bytes per layer: the chunk's K/V rows read and written into the
+    # pool, the slots written (and, with --prep, read back), the block-table row
+    lay_b = 2 * T * row_b * 2 + T * 8 * (2 if args.prep else 1) + npg * 4
+    if args.prep:  # + q read and written, k written out, rotary rows, weights, positions
+        lay_b += 2 * T * H * D * 2 + T * row_b + T * (D // 2) * 8 + 2 * D * 2 + T * 4
+    config = {"workload": "prefill_760m_chunk2048", "layers": L, "tokens": T, "heads": [H, KVH, D], "page": bs,
+              "pool_pages": NB, "dtype": "bf16",
+              "layer_call": "q/k RMSNorm + rotary + KV write" if args.prep else "slot mapping + KV write",
+              "l2": "inputs > L2: per-layer chunk rows and pools",
+              "parallelism": f"{world} GPU(s), one prompt each, no collective"}
+
+    def host_chunk(seed):
+        g = torch.Generator()
+        g.manual_seed(seed)
+        c = {"k": torch.randn((L, T, KVH, D), generator=g).to(torch.bfloat16),
+             "v": torch.randn((L, T, KVH, D), generator=g).to(torch.bfloat16),
+             "row": torch.randperm(NB, generator=g)[:npg].to(torch.int32)}
+        if args.prep:
+            c["q"] = torch.randn((L, T, H, D), generator=g).to(torch.bfloat16)
+            c["q_w"] = (1 + 0.1 * torch.randn((L, D), generator=g)).to(torch.bfloat16)
+            c["k_w"] = (1 + 0.1 * torch.randn((L, D), generator=g)).to(torch.bfloat16)
+        return c
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        from oracle import oracle
+        oracle.build()
+        cores = oracle.use_all_cores()
+        c = host_chunk(1000)
+        kc = torch.zeros((NB, bs, KVH, D), dtype=torch.bfloat16)
+        vc = torch.zeros_like(kc)
+        pkg = load_package()
+        rope = pkg.rope_table(D, 2 * T, 500000.0, device="cpu") if args.prep else None
+        slots = (c["row"].long()[torch.arange(T) // bs] * bs + torch.arange(T) % bs)
+        times = []
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            k, v = c["k"][0], c["v"][0]
+            if args.prep:
+                _, k_r, _ = oracle.qk_norm_rope(c["q"][0], k, c["q_w"][0], c["k_w"][0], rope,
+                                                torch.arange(T).numpy(), 1e-6)
+                k = torch.from_numpy(k_r).to(torch.bfloat16)
+            oracle.kv_append(k, v, kc, vc, slots)
+            if i >= args.warmup:
+                times.append(time.perf_counter() - t0)
+        v = lay_b * len(times) / sum(times) / 1e9
+        print(json.dumps({
+            "metric": PREFILL_METRIC, "value": round(v, 4), "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(times) / len(times),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": config,
+            "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                             "sample": "one layer of the 2048-token chunk per step: "
+                                       + ("numpy q/k norm + rotary, then " if args.prep else "")
+                                       + "the C oracle's slot write"},
+            "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return
+
+    pkg = load_package()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    c = host_chunk(1000 + rank)
+    g = torch.Generator(device=device)
+    g.manual_seed(2000 + rank)
+    kcs = [torch.randn((NB, bs, KVH, D), generator=g, device=device).to(torch.bfloat16) for _ in range(L)]
+    vcs = [torch.randn((NB, bs, KVH, D), generator=g, device=device).to(torch.bfloat16) for _ in range(L)]
+    dk, dv, drow = c["k"].to(device), c["v"].to(device), c["row"].to(device)
+    rope = pkg.rope_table(D, 2 * T, 500000.0, device=device) if args.prep else None
+    if args.prep:
+        dq, dqw, dkw = c["q"].to(device), c["q_w"].to(device), c["k_w"].to(device)
+    outs = {}
+
+    def layer(l, k, v, row, q=None):
+        if args.prep:
+            outs[l] = pkg.prefill_prep(q, k, v, dqw[l], dkw[l], rope, kcs[l], vcs[l], row, 0)
+        else:
+            outs[l] = pkg.prefill_kv_write(k, v, kcs[l], vcs[l], row, 0)
+
+    def step():
+        for l in range(L):
+            layer(l, dk[l], dv[l], drow, dq[l] if args.prep else None)
+
+    def capture(fn):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            fn()
+        return gr
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+
+    def reduce_max(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    pkg.check_device_errors(device)
+    # the pool rows equal the chunk rows (K after the norm and rotary with --prep)
+    slots = outs[0] if not args.prep else pkg.prefill_slots(drow, 0, T, bs)
+    if not args.prep:
+        got = kcs[0].view(-1, KVH, D)[slots]
+        assert torch.equal(got, dk[0]), "pool rows differ from the chunk's K rows"
+    graph = capture(step)
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        ev0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        ev1.record()
+        torch.cuda.synchronize()
+    barrier()
+    ms = reduce_max(ev0.elapsed_time(ev1))
+    del graph
+    step_b = L * lay_b
+
+    # e2e: the chunk's rows from pinned host memory every step (on a copy stream,
+    # in growing layer groups), the last layer's slots back to the host
+    hk, hv = c["k"].pin_memory(), c["v"].pin_memory()
+    hq = c["q"].pin_memory() if args.prep else None
+    h_out = torch.empty(T, dtype=torch.int64).pin_memory()
+    ek, ev_ = torch.empty_like(dk), torch.empty_like(dv)
+    eq = torch.empty_like(dq) if args.prep else None
+    s_in = torch.cuda.Stream(device)
+    groups, l0, n = [], 0, 1
+    while l0 < L:
+        groups.append((l0, min(L, l0 + n) - 1))
+        l0, n = l0 + n, 3 * n
+    ev_in = [torch.cuda.Event() for _ in groups]
+
+    def e2e_step():
+        main = torch.cuda.current_stream(device)
+        s_in.wait_stream(main)
+        with torch.cuda.stream(s_in):
+            for gi, (a, b) in enumerate(groups):
+                ek[a:b + 1].copy_(hk[a:b + 1], non_blocking=True)
+                ev_[a:b + 1].copy_(hv[a:b + 1], non_blocking=True)
+                if args.prep:
+                    eq[a:b + 1].copy_(hq[a:b + 1], non_blocking=True)
+                ev_in[gi].record(s_in)
+        for gi, (a, b) in enumerate(groups):
+            main.wait_event(ev_in[gi])
+            for l in range(a, b + 1):
+                layer(l, ek[l], ev_[l], drow, eq[l] if args.prep else None)
+        main.wait_stream(s_in)
+        res = outs[L - 1] if not args.prep else slots
+        h_out.copy_(res, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    eg = capture(e2e_step)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        eg.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e_ms = reduce_max(e0.elapsed_time(e1))
+    del eg
+    pkg.check_device_errors(device)
+    h2d = (hk.numel() + hv.numel() + (hq.numel() if args.prep else 0)) * 2
+    peak, kind = peaks()
+    per_layer_us = ms / args.steps / L * 1e3
+    line = {"metric": PREFILL_METRIC, "value": round(world * step_b * args.steps / (ms / 1e3) / 1e9, 2),
+            "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config,
+            "tokens_per_s": round(world * T * args.steps / (ms / 1e3), 1),
+            "gpu_launches": args.steps * L * (2 if args.prep else 1),
+            "e2e": {"value": round(world * step_b * args.steps / (e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": int(world * h2d), "d2h_bytes_per_step": int(world * T * 8),
+                    "ms_per_step": round(e_ms / args.steps, 4)},
+            "clocks": clocks.summary(),
+            "roofline": {"bound": "hbm", "achieved": round(lay_b / (per_layer_us / 1e6) / 1e9, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(lay_b / (per_layer_us / 1e6) / 1e9 / peak, 4),
+                         "traffic": None, "peak_source": f"{kind} (MEASURED_PEAKS.json hbm_gbs)",
+                         "kernel": ("slot_mapping_kernel + qk_norm_rope_kernel (append fused)" if args.prep
+                                    else "prefill_append_kernel (slots computed in the kernel)"),
+                         "algorithmic_bytes_per_launch": int(lay_b), "avg_launch_us": round(per_layer_us, 2),
+                         "timing": "graph replay / layers (the layer's launches together)"}}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle
+        oracle.build()
+        cores = oracle.use_all_cores()
+        kc = kcs[0].cpu()
+        vc = vcs[0].cpu()
+        hs = slots.cpu()
+        hrope = rope.cpu() if args.prep else None
+        t0, calls = time.perf_counter(), 0
+        while True:
+            k, v = c["k"][calls % L], c["v"][calls % L]
+            if args.prep:
+                _, k_r, _ = oracle.qk_norm_rope(c["q"][calls % L], k, c["q_w"][calls % L], c["k_w"][calls % L],
+                                                hrope, torch.arange(T).numpy(), 1e-6)
+                k = torch.from_numpy(k_r).to(torch.bfloat16)
+            oracle.kv_append(k, v, kc, vc, hs)
+            calls += 1
+            el = time.perf_counter() - t0
+            if el >= min(args.cpu_seconds, 5.0) or calls >= 100000:
+                break
+        line["cpu_baseline"] = {"value": round(lay_b * calls / el / 1e9, 4), "unit": "GB/s", "cores": cores,
+                                "kind": "port", "sample": f"{calls} layer write(s) of the 2048-token chunk, {el:.1f} s"}
+    if rank == 0:
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.op == "handoff":
         return bench_handoff(args)
+    if args.op == "prefill":
+        return bench_prefill(args)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

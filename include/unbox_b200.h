@@ -91,6 +91,23 @@ int ubx_kv_append(const void* k_new, const void* v_new, int64_t new_s_tok, int64
                   int block_size, int64_t num_blocks, int dtype, int32_t* error_word, void* stream);
 
 /*
+ * Prefill chunk KV write: the K/V rows of tokens t = 0 .. num_tokens-1 of one
+ * sequence, at positions start_pos + t, go to slot = block_table_row[pos // bs]
+ * * bs + pos % bs (no slot, nothing written, for a position past the row's
+ * max_blocks_per_seq entries or a negative page, as in ubx_slot_mapping; a page
+ * outside the pool sets UBX_DEVERR_BAD_SLOT). One launch, slots computed in the
+ * kernel; slots_out (num_tokens,) int64 receives them when not NULL.
+ * Replaces: the per-token PagedKVCache.write_kv loop of prefill_step
+ * (unbox_platform/infer/engine.py:126-128, kvcache.py:330-340).
+ * Strides as in ubx_kv_append (k, v share s_tok / s_head).
+ */
+int ubx_prefill_kv_write(const void* k, const void* v, int64_t s_tok, int64_t s_head, void* k_cache, void* v_cache,
+                         int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head, const int32_t* block_table_row,
+                         int max_blocks_per_seq, int64_t start_pos, int64_t num_tokens, int num_kv_heads, int head_dim,
+                         int block_size, int64_t num_blocks, int dtype, int64_t* slots_out, int32_t* error_word,
+                         void* stream);
+
+/*
  * Slot mapping of one decode step: slot[b] = block_table[b, pos // bs] * bs + pos % bs
  * with pos = positions[b] (the index arithmetic of PagedKVCache.write_kv,
  * kvcache.py:338-339). A negative position or page gives slot -1.

@@ -245,6 +245,38 @@ int ubx_slot_mapping(const int32_t* block_table, int64_t bt_s_row, const int32_t
   return UBX_OK;
 }
 
+int ubx_prefill_kv_write(const void* k, const void* v, int64_t s_tok, int64_t s_head, void* k_cache, void* v_cache,
+                         int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head, const int32_t* block_table_row,
+                         int max_blocks_per_seq, int64_t start_pos, int64_t num_tokens, int num_kv_heads, int head_dim,
+                         int block_size, int64_t num_blocks, int dtype, int64_t* slots_out, int32_t* error_word,
+                         void* stream) {
+  g_last_error.clear();
+  if (dtype != UBX_DTYPE_F32 && dtype != UBX_DTYPE_BF16 && dtype != UBX_DTYPE_F16)
+    return fail(UBX_ERR_INVALID_ARGUMENT, "unknown dtype code %d", dtype);
+  if (num_tokens < 0 || num_kv_heads <= 0 || head_dim <= 0 || block_size <= 0 || num_blocks <= 0 ||
+      max_blocks_per_seq < 0 || start_pos < 0)
+    return fail(UBX_ERR_INVALID_ARGUMENT, "non-positive size or negative start position");
+  if (num_tokens == 0) return UBX_OK;
+  if (!k || !v || !k_cache || !v_cache || !block_table_row) return fail(UBX_ERR_INVALID_ARGUMENT, "null pointer");
+  const int es = dtype_bytes(dtype);
+  const int row = head_dim * es;
+  int vec = 16;  // widest copy unit that every address and stride allows
+  auto ok_for = [&](int w) {
+    auto a = [&](const void* p) { return (reinterpret_cast<uintptr_t>(p) % w) == 0; };
+    auto st = [&](int64_t x) { return ((x * es) % w) == 0; };
+    return row % w == 0 && a(k) && a(v) && a(k_cache) && a(v_cache) && st(s_tok) && st(s_head) && st(c_s_block) &&
+           st(c_s_tok) && st(c_s_head);
+  };
+  while (vec > es && !ok_for(vec)) vec >>= 1;
+  if (!ok_for(vec)) return fail(UBX_ERR_INVALID_ARGUMENT, "misaligned K/V row");
+  cudaError_t e = launch_prefill_append(k, v, s_tok * es, s_head * es, k_cache, v_cache, c_s_block * es, c_s_tok * es,
+                                        c_s_head * es, block_table_row, max_blocks_per_seq, start_pos, num_tokens,
+                                        num_kv_heads, row, block_size, num_blocks, vec, slots_out, error_word,
+                                        static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "prefill_kv_write launch");
+  return UBX_OK;
+}
+
 int ubx_qk_norm_rope_append(const void* q_in, int64_t q_s_tok, int64_t q_s_head, const void* k_in, int64_t k_s_tok,
                             int64_t k_s_head, const void* v_in, int64_t v_s_tok, int64_t v_s_head,
                             const void* q_weight, const void* k_weight, float eps, const float* rope,

@@ -23,8 +23,36 @@ struct VecT<4> { using type = uint32_t; };
 template <>
 struct VecT<2> { using type = uint16_t; };
 
-// One thread per VEC-byte piece of a (token, K|V, head) row. Grid-stride.
-template <int VEC>
+// Copy one (token, K|V) row of kvh head rows (row_bytes each) with the 32
+// lanes of a warp, VEC bytes per access, 32-bit offsets inside the row. FLAT:
+// the heads are contiguous in both the new rows and the pool, so the row is one
+// contiguous span on each side.
+template <int VEC, bool FLAT>
+__device__ __forceinline__ void copy_row(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int64_t n_sh_b,
+                                         int64_t c_sh_b, int kvh, int row_bytes, int lane) {
+  using V = typename VecT<VEC>::type;
+  const int pieces = row_bytes / VEC;
+  if constexpr (FLAT) {
+    // four loads in flight per lane before their stores
+    const int per_tok = kvh * pieces;
+    for (int base = lane; base < per_tok; base += 4 * 32) {
+      V r[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (base + 32 * k < per_tok) r[k] = *reinterpret_cast<const V*>(src + (base + 32 * k) * VEC);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (base + 32 * k < per_tok) *reinterpret_cast<V*>(dst + (base + 32 * k) * VEC) = r[k];
+    }
+  } else {
+    for (int h = 0; h < kvh; ++h)
+      for (int c = lane; c < pieces; c += 32)
+        *reinterpret_cast<V*>(dst + h * c_sh_b + c * VEC) = *reinterpret_cast<const V*>(src + h * n_sh_b + c * VEC);
+  }
+}
+
+// One warp per (token, K|V) row, grid-stride over rows; the slot is read once per row.
+template <int VEC, bool FLAT>
 __global__ void __launch_bounds__(256) kv_append_kernel(const uint8_t* __restrict__ k_new,
                                                         const uint8_t* __restrict__ v_new, int64_t n_stok_b,
                                                         int64_t n_sh_b, uint8_t* __restrict__ k_cache,
@@ -33,27 +61,63 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const uint8_t* __restric
                                                         const int64_t* __restrict__ slots, int64_t num_tokens,
                                                         int kvh, int row_bytes, int block_size, int64_t num_blocks,
                                                         int32_t* error_word) {
-  using V = typename VecT<VEC>::type;
-  const int pieces = row_bytes / VEC;
-  const int64_t total = num_tokens * 2 * kvh * pieces;
   const int64_t limit = num_blocks * block_size;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int c = (int)(i % pieces);
-    int64_t rest = i / pieces;
-    const int h = (int)(rest % kvh);
-    rest /= kvh;
-    const int which = (int)(rest & 1);
-    const int64_t t = rest >> 1;
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; r < 2 * num_tokens; r += nwarps) {
+    const int64_t t = r >> 1;
+    const int which = (int)(r & 1);
     const int64_t slot = __ldg(&slots[t]);
     if (slot < 0) continue;  // padding token
     if (slot >= limit) {
-      if (c == 0 && h == 0 && which == 0) set_error(error_word, kErrBadSlot);
+      if (lane == 0 && which == 0) set_error(error_word, kErrBadSlot);
       continue;
     }
-    const int64_t blk = slot / block_size, off = slot % block_size;
-    const uint8_t* src = (which ? v_new : k_new) + t * n_stok_b + h * n_sh_b + (int64_t)c * VEC;
-    uint8_t* dst = (which ? v_cache : k_cache) + blk * c_sblk_b + off * c_stok_b + h * c_sh_b + (int64_t)c * VEC;
-    *reinterpret_cast<V*>(dst) = *reinterpret_cast<const V*>(src);
+    const int64_t blk = slot / block_size;
+    const int off = (int)(slot - blk * block_size);
+    copy_row<VEC, FLAT>((which ? v_new : k_new) + t * n_stok_b,
+                        (which ? v_cache : k_cache) + blk * c_sblk_b + (int64_t)off * c_stok_b, n_sh_b, c_sh_b, kvh,
+                        row_bytes, lane);
+  }
+}
+
+// Prefill chunk: tokens t = 0 .. T-1 of one sequence at positions start + t;
+// the slot is computed here from the sequence's block-table row (the same
+// rule as slot_mapping_kernel: past the row or a negative page = no slot) and
+// optionally stored to slots_out.
+template <int VEC, bool FLAT>
+__global__ void __launch_bounds__(256) prefill_append_kernel(const uint8_t* __restrict__ k_new,
+                                                             const uint8_t* __restrict__ v_new, int64_t n_stok_b,
+                                                             int64_t n_sh_b, uint8_t* __restrict__ k_cache,
+                                                             uint8_t* __restrict__ v_cache, int64_t c_sblk_b,
+                                                             int64_t c_stok_b, int64_t c_sh_b,
+                                                             const int32_t* __restrict__ bt_row, int max_blocks,
+                                                             int64_t start_pos, int64_t num_tokens, int kvh,
+                                                             int row_bytes, int block_size, int64_t num_blocks,
+                                                             int64_t* __restrict__ slots_out, int32_t* error_word) {
+  const int64_t limit = num_blocks * block_size;
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; r < 2 * num_tokens; r += nwarps) {
+    const int64_t t = r >> 1;
+    const int which = (int)(r & 1);
+    const int64_t pos = start_pos + t;
+    int64_t slot = -1;
+    if (pos >= 0 && pos / block_size < max_blocks) {
+      const int page = __ldg(&bt_row[pos / block_size]);
+      if (page >= 0) slot = (int64_t)page * block_size + pos % block_size;
+    }
+    if (slots_out != nullptr && which == 0 && lane == 0) slots_out[t] = slot;
+    if (slot < 0) continue;
+    if (slot >= limit) {
+      if (lane == 0 && which == 0) set_error(error_word, kErrBadSlot);
+      continue;
+    }
+    const int64_t blk = slot / block_size;
+    const int off = (int)(slot - blk * block_size);
+    copy_row<VEC, FLAT>((which ? v_new : k_new) + t * n_stok_b,
+                        (which ? v_cache : k_cache) + blk * c_sblk_b + (int64_t)off * c_stok_b, n_sh_b, c_sh_b, kvh,
+                        row_bytes, lane);
   }
 }
 
@@ -78,24 +142,52 @@ cudaError_t launch_kv_append(const void* k_new, const void* v_new, int64_t n_sto
                              const int64_t* slots, int64_t num_tokens, int num_kv_heads, int row_bytes,
                              int block_size, int64_t num_blocks, int vec_bytes, int32_t* error_word,
                              cudaStream_t stream) {
-  const int64_t total = num_tokens * 2 * num_kv_heads * (row_bytes / vec_bytes);
-  if (total == 0) return cudaSuccess;
+  const int64_t rows = num_tokens * 2;  // one warp per (token, K|V) row
+  if (rows == 0) return cudaSuccess;
   const int threads = 256;
-  const int64_t blocks64 = (total + threads - 1) / threads;
-  const int blocks = (int)(blocks64 < 148 * 16 ? blocks64 : 148 * 16);
-#define UBX_APPEND(VB)                                                                                          \
-  kv_append_kernel<VB><<<blocks, threads, 0, stream>>>(                                                         \
+  const int64_t blocks64 = (rows + 7) / 8;
+  const int blocks = (int)(blocks64 < 148 * 8 ? blocks64 : 148 * 8);
+  const bool flat = n_sh_b == row_bytes && c_sh_b == row_bytes;
+#define UBX_APPEND(VB, FL)                                                                                      \
+  kv_append_kernel<VB, FL><<<blocks, threads, 0, stream>>>(                                                     \
       static_cast<const uint8_t*>(k_new), static_cast<const uint8_t*>(v_new), n_stok_b, n_sh_b,                 \
       static_cast<uint8_t*>(k_cache), static_cast<uint8_t*>(v_cache), c_sblk_b, c_stok_b, c_sh_b, slots,        \
       num_tokens, num_kv_heads, row_bytes, block_size, num_blocks, error_word)
   switch (vec_bytes) {
-    case 16: UBX_APPEND(16); break;
-    case 8: UBX_APPEND(8); break;
-    case 4: UBX_APPEND(4); break;
-    case 2: UBX_APPEND(2); break;
+    case 16: if (flat) UBX_APPEND(16, true); else UBX_APPEND(16, false); break;
+    case 8: if (flat) UBX_APPEND(8, true); else UBX_APPEND(8, false); break;
+    case 4: if (flat) UBX_APPEND(4, true); else UBX_APPEND(4, false); break;
+    case 2: if (flat) UBX_APPEND(2, true); else UBX_APPEND(2, false); break;
     default: return cudaErrorInvalidValue;
   }
 #undef UBX_APPEND
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_append(const void* k_new, const void* v_new, int64_t n_stok_b, int64_t n_sh_b,
+                                  void* k_cache, void* v_cache, int64_t c_sblk_b, int64_t c_stok_b, int64_t c_sh_b,
+                                  const int32_t* bt_row, int max_blocks, int64_t start_pos, int64_t num_tokens,
+                                  int num_kv_heads, int row_bytes, int block_size, int64_t num_blocks, int vec_bytes,
+                                  int64_t* slots_out, int32_t* error_word, cudaStream_t stream) {
+  const int64_t rows = num_tokens * 2;
+  if (rows == 0) return cudaSuccess;
+  const int threads = 256;
+  const int64_t blocks64 = (rows + 7) / 8;
+  const int blocks = (int)(blocks64 < 148 * 8 ? blocks64 : 148 * 8);
+  const bool flat = n_sh_b == row_bytes && c_sh_b == row_bytes;
+#define UBX_PREFILL(VB, FL)                                                                                     \
+  prefill_append_kernel<VB, FL><<<blocks, threads, 0, stream>>>(                                                \
+      static_cast<const uint8_t*>(k_new), static_cast<const uint8_t*>(v_new), n_stok_b, n_sh_b,                 \
+      static_cast<uint8_t*>(k_cache), static_cast<uint8_t*>(v_cache), c_sblk_b, c_stok_b, c_sh_b, bt_row,       \
+      max_blocks, start_pos, num_tokens, num_kv_heads, row_bytes, block_size, num_blocks, slots_out, error_word)
+  switch (vec_bytes) {
+    case 16: if (flat) UBX_PREFILL(16, true); else UBX_PREFILL(16, false); break;
+    case 8: if (flat) UBX_PREFILL(8, true); else UBX_PREFILL(8, false); break;
+    case 4: if (flat) UBX_PREFILL(4, true); else UBX_PREFILL(4, false); break;
+    case 2: if (flat) UBX_PREFILL(2, true); else UBX_PREFILL(2, false); break;
+    default: return cudaErrorInvalidValue;
+  }
+#undef UBX_PREFILL
   return cudaGetLastError();
 }
 

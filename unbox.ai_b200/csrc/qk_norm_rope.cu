@@ -8,7 +8,8 @@
 //   per-sequence apply_rotary_emb at pos (.item())   engine.py:204-210 / :123
 //   per-token write_kv(layer, seq, pos, xk, xv)      engine.py:213-215 / :126-128
 // (RMSNorm: unbox_platform/model/model.py:19-27; rotary: model.py:30-48; the
-// write: kvcache.py:330-340). One warp handles one (token, head) row; the warps
+// write: kvcache.py:330-340). One warp handles one (token, head) row at a time (a
+// block per token, its warps over the heads); the warps
 // of K heads also store the token's K and V rows into the pool.
 #include "ubx_common.cuh"
 #include "ubx_internal.h"
@@ -64,14 +65,15 @@ template <typename T>
 __global__ void __launch_bounds__(kPrepWarps * 32) qk_norm_rope_kernel(const PrepParams p) {
   const int lane = threadIdx.x & 31;
   const int rows_per_token = p.num_heads + p.num_kv_heads;
-  const int64_t rows = p.num_tokens * rows_per_token;
   const int np = p.head_dim / 2;
   const float inv_d = 1.f / (float)p.head_dim;
   const int64_t limit = p.num_blocks * p.block_size;
-  for (int64_t r = (int64_t)blockIdx.x * kPrepWarps + (threadIdx.x >> 5); r < rows;
-       r += (int64_t)gridDim.x * kPrepWarps) {
-    const int64_t t = r / rows_per_token;
-    const int h = (int)(r % rows_per_token);
+  // the page size is a power of two in practice: a shift instead of a 64-bit division
+  const int bs_shift = (p.block_size & (p.block_size - 1)) == 0 ? __ffs(p.block_size) - 1 : -1;
+  // a block per token (grid-stride), its warps over the token's q and k rows:
+  // no division to find a row's token and head
+  for (int64_t t = blockIdx.x; t < p.num_tokens; t += gridDim.x)
+  for (int h = threadIdx.x >> 5; h < rows_per_token; h += kPrepWarps) {
     const bool is_q = h < p.num_heads;
     const int hk = h - p.num_heads;
     const T* x = is_q ? static_cast<const T*>(p.q_in) + t * p.q_st + (int64_t)h * p.q_sh
@@ -105,7 +107,8 @@ __global__ void __launch_bounds__(kPrepWarps * 32) qk_norm_rope_kernel(const Pre
         if (slot >= limit) {
           if (lane == 0 && hk == 0) set_error(p.error, kErrBadSlot);
         } else if (slot >= 0) {
-          const int64_t off = (slot / p.block_size) * p.c_sblk + (slot % p.block_size) * p.c_stok + (int64_t)hk * p.c_sh;
+          const int64_t blk = bs_shift >= 0 ? slot >> bs_shift : slot / p.block_size;
+          const int64_t off = blk * p.c_sblk + (slot - blk * p.block_size) * p.c_stok + (int64_t)hk * p.c_sh;
           dst_cache = static_cast<T*>(p.k_cache) + off;
           dst_v = static_cast<T*>(p.v_cache) + off;
           src_v = static_cast<const T*>(p.v_in) + t * p.v_st + (int64_t)hk * p.v_sh;
@@ -134,10 +137,8 @@ __global__ void __launch_bounds__(kPrepWarps * 32) qk_norm_rope_kernel(const Pre
 }  // namespace
 
 cudaError_t launch_qk_norm_rope(int dtype, const PrepParams& p, cudaStream_t stream) {
-  const int64_t rows = p.num_tokens * (p.num_heads + p.num_kv_heads);
-  if (rows == 0) return cudaSuccess;
-  const int64_t want = (rows + kPrepWarps - 1) / kPrepWarps;
-  const int blocks = (int)(want < 148 * 32 ? want : 148 * 32);
+  if (p.num_tokens == 0) return cudaSuccess;
+  const int blocks = (int)(p.num_tokens < 148 * 32 ? p.num_tokens : 148 * 32);  // a block per token
   switch (dtype) {
     case 0: qk_norm_rope_kernel<float><<<blocks, kPrepWarps * 32, 0, stream>>>(p); break;
     case 1: qk_norm_rope_kernel<__nv_bfloat16><<<blocks, kPrepWarps * 32, 0, stream>>>(p); break;

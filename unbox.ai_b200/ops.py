@@ -485,12 +485,37 @@ def prefill_kv_write(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_
                      block_table_row: torch.Tensor, start_pos: int) -> torch.Tensor:
     """Write the K/V rows of a prefill chunk (T tokens of one sequence starting at
     ``start_pos``) into the pool: the per-token write_kv loop of prefill_step
-    (engine.py:126-128) as one slot computation and one append launch. Returns the
-    slots (T,) int64."""
-    if k.dim() != 3:
-        raise ValueError("k must be (T, KVH, D)")
-    slots = prefill_slots(block_table_row, start_pos, k.shape[0], k_cache.shape[1])
-    kv_append(k, v, k_cache, v_cache, slots)
+    (engine.py:126-128) as one launch that computes each token's slot from the
+    block-table row and copies its rows. Returns the slots (T,) int64."""
+    dev = _require_cuda(k, v, k_cache, v_cache, block_table_row)
+    if k.dim() != 3 or v.shape != k.shape or k_cache.dim() != 4 or v_cache.shape != k_cache.shape:
+        raise ValueError("expected k/v (T, KVH, D) and caches (NB, bs, KVH, D)")
+    if k.dtype != k_cache.dtype or v.dtype != k_cache.dtype or v_cache.dtype != k_cache.dtype:
+        raise TypeError("chunk rows and caches must share one dtype")
+    if k_cache.dtype not in _DTYPES:
+        raise TypeError(f"unsupported dtype {k_cache.dtype}")
+    if k.stride() != v.stride() or k_cache.stride() != v_cache.stride():
+        raise ValueError("K and V tensors must have matching strides")
+    T, KVH, D = k.shape
+    NB, bs, KVH2, D2 = k_cache.shape
+    if (KVH2, D2) != (KVH, D):
+        raise ValueError(f"row shape {(KVH, D)} does not match cache {(KVH2, D2)}")
+    if k.stride(-1) != 1 or k_cache.stride(-1) != 1:
+        raise ValueError("the head_dim dimension must be contiguous")
+    row = _int32(block_table_row, "block_table_row").contiguous()
+    if row.dim() != 1:
+        raise ValueError("block_table_row must be 1-D")
+    if start_pos < 0:
+        raise ValueError("start_pos must be >= 0")
+    slots = torch.empty(T, dtype=torch.int64, device=dev)
+    if T == 0:
+        return slots
+    ws = workspace_for(dev)
+    st = _L.load().ubx_prefill_kv_write(k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), k_cache.data_ptr(),
+                                        v_cache.data_ptr(), k_cache.stride(0), k_cache.stride(1), k_cache.stride(2),
+                                        row.data_ptr(), row.shape[0], int(start_pos), T, KVH, D, bs, NB,
+                                        _DTYPES[k_cache.dtype], slots.data_ptr(), ws.error_word_ptr(), _stream(dev))
+    _L.check(st, "prefill_kv_write")
     return slots
 
 
