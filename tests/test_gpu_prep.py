@@ -221,6 +221,45 @@ def test_prefill_kv_write_bit_exact(dtype, pkg, oracle):
     assert torch.equal(c["k_cache"].cpu(), kc) and torch.equal(c["v_cache"].cpu(), vc)
 
 
+def test_prefill_kv_write_edges(pkg, oracle):
+    """The one-launch prefill write: a chunk that runs past its block-table row
+    (no slot, nothing written), a -1 page inside the row (padding), K/V given as
+    head-strided views (the copy path without contiguous head rows), and a page
+    outside the pool (flagged, not written)."""
+    T, start, NB, KVH, D = 50, 5, 10, 8, 112                     # positions 5 .. 54
+    g = torch.Generator().manual_seed(31)
+    kc = torch.randn((NB, 16, KVH, D), generator=g).to(torch.bfloat16)
+    vc = torch.randn((NB, 16, KVH, D), generator=g).to(torch.bfloat16)
+    big_k = torch.randn((T, KVH, 128), generator=g).to(torch.bfloat16)
+    big_v = torch.randn((T, KVH, 128), generator=g).to(torch.bfloat16)
+    k, v = big_k[:, :, :D], big_v[:, :, :D]                       # head stride 128, not D
+    row = np.array([3, -1, 7], dtype=np.int32)                     # 3 pages: positions 0..47 only
+    dkc, dvc = kc.to(DEV), vc.to(DEV)
+    dk, dv = big_k.to(DEV)[:, :, :D], big_v.to(DEV)[:, :, :D]
+    assert dk.stride(1) == 128
+    slots = pkg.prefill_kv_write(dk, dv, dkc, dvc, torch.from_numpy(row).to(DEV), start)
+    torch.cuda.synchronize()
+    pos = np.arange(start, start + T)
+    want = np.full(T, -1, dtype=np.int64)
+    inside = pos // 16 < len(row)
+    pages = np.where(inside, row[np.minimum(pos // 16, len(row) - 1)], -1)
+    ok = inside & (pages >= 0)
+    want[ok] = pages[ok] * 16 + pos[ok] % 16
+    assert np.array_equal(slots.cpu().numpy(), want)
+    ek, ev = kc.clone(), vc.clone()
+    assert oracle.kv_append(k.contiguous(), v.contiguous(), ek, ev, torch.from_numpy(want)) == 0
+    assert torch.equal(dkc.cpu(), ek) and torch.equal(dvc.cpu(), ev)
+    pkg.check_device_errors()
+    # a page id past the pool: reported, the pool left as it was
+    bad = torch.tensor([NB + 2], dtype=torch.int32, device=DEV)
+    before = dkc.clone()
+    pkg.prefill_kv_write(dk[:4], dv[:4], dkc, dvc, bad, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(dkc, before)
+    with pytest.raises(RuntimeError, match="slot outside"):
+        pkg.check_device_errors()
+
+
 def test_prefill_prep_golden(pkg):
     z, lay, x, caches, rope = load_prep_golden("prep_prefill_fp32")
     d, c = dev(x), dev(caches)
