@@ -512,7 +512,7 @@ def bench_prefill(args):
         if args.prep:
             outs[l] = pkg.prefill_prep(q, k, v, dqw[l], dkw[l], rope, kcs[l], vcs[l], row, 0)
         else:
-            outs[l] = pkg.prefill_kv_write(k, v, kcs[l], vcs[l], row, 0)
+            outs[l] = pkg.prefill_kv_write(k, v, kcs[l], vcs[l], row, 0, overlap_previous=args.overlap)
 
     def step():
         for l in range(L):

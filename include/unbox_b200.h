@@ -99,13 +99,16 @@ int ubx_kv_append(const void* k_new, const void* v_new, int64_t new_s_tok, int64
  * kernel; slots_out (num_tokens,) int64 receives them when not NULL.
  * Replaces: the per-token PagedKVCache.write_kv loop of prefill_step
  * (unbox_platform/infer/engine.py:126-128, kvcache.py:330-340).
- * Strides as in ubx_kv_append (k, v share s_tok / s_head).
+ * Strides as in ubx_kv_append (k, v share s_tok / s_head). flags:
+ * UBX_FLAG_OVERLAP_PREVIOUS = programmatic dependent launch (the kernel may
+ * start while the previous kernel on the stream drains; it reads and writes
+ * nothing before that kernel has completed).
  */
 int ubx_prefill_kv_write(const void* k, const void* v, int64_t s_tok, int64_t s_head, void* k_cache, void* v_cache,
                          int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head, const int32_t* block_table_row,
                          int max_blocks_per_seq, int64_t start_pos, int64_t num_tokens, int num_kv_heads, int head_dim,
                          int block_size, int64_t num_blocks, int dtype, int64_t* slots_out, int32_t* error_word,
-                         void* stream);
+                         int flags, void* stream);
 
 /*
  * Slot mapping of one decode step: slot[b] = block_table[b, pos // bs] * bs + pos % bs

@@ -249,8 +249,9 @@ int ubx_prefill_kv_write(const void* k, const void* v, int64_t s_tok, int64_t s_
                          int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head, const int32_t* block_table_row,
                          int max_blocks_per_seq, int64_t start_pos, int64_t num_tokens, int num_kv_heads, int head_dim,
                          int block_size, int64_t num_blocks, int dtype, int64_t* slots_out, int32_t* error_word,
-                         void* stream) {
+                         int flags, void* stream) {
   g_last_error.clear();
+  if (flags & ~UBX_FLAG_OVERLAP_PREVIOUS) return fail(UBX_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
   if (dtype != UBX_DTYPE_F32 && dtype != UBX_DTYPE_BF16 && dtype != UBX_DTYPE_F16)
     return fail(UBX_ERR_INVALID_ARGUMENT, "unknown dtype code %d", dtype);
   if (num_tokens < 0 || num_kv_heads <= 0 || head_dim <= 0 || block_size <= 0 || num_blocks <= 0 ||
@@ -272,7 +273,7 @@ int ubx_prefill_kv_write(const void* k, const void* v, int64_t s_tok, int64_t s_
   cudaError_t e = launch_prefill_append(k, v, s_tok * es, s_head * es, k_cache, v_cache, c_s_block * es, c_s_tok * es,
                                         c_s_head * es, block_table_row, max_blocks_per_seq, start_pos, num_tokens,
                                         num_kv_heads, row, block_size, num_blocks, vec, slots_out, error_word,
-                                        static_cast<cudaStream_t>(stream));
+                                        (flags & UBX_FLAG_OVERLAP_PREVIOUS) != 0, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "prefill_kv_write launch");
   return UBX_OK;
 }

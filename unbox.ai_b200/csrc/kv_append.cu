@@ -98,6 +98,10 @@ __global__ void __launch_bounds__(256) prefill_append_kernel(const uint8_t* __re
   const int64_t limit = num_blocks * block_size;
   const int lane = threadIdx.x & 31;
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  // launched with programmatic overlap: the next kernel may launch now, and
+  // nothing is read or written before the previous kernel has completed
+  griddep_launch_dependents();
+  griddep_wait();
   for (int64_t r = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; r < 2 * num_tokens; r += nwarps) {
     const int64_t t = r >> 1;
     const int which = (int)(r & 1);
@@ -168,18 +172,29 @@ cudaError_t launch_prefill_append(const void* k_new, const void* v_new, int64_t 
                                   void* k_cache, void* v_cache, int64_t c_sblk_b, int64_t c_stok_b, int64_t c_sh_b,
                                   const int32_t* bt_row, int max_blocks, int64_t start_pos, int64_t num_tokens,
                                   int num_kv_heads, int row_bytes, int block_size, int64_t num_blocks, int vec_bytes,
-                                  int64_t* slots_out, int32_t* error_word, cudaStream_t stream) {
+                                  int64_t* slots_out, int32_t* error_word, bool overlap, cudaStream_t stream) {
   const int64_t rows = num_tokens * 2;
   if (rows == 0) return cudaSuccess;
   const int threads = 256;
   const int64_t blocks64 = (rows + 7) / 8;
   const int blocks = (int)(blocks64 < 148 * 8 ? blocks64 : 148 * 8);
   const bool flat = n_sh_b == row_bytes && c_sh_b == row_bytes;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(threads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = overlap ? 1 : 0;
+  cudaError_t e = cudaSuccess;
 #define UBX_PREFILL(VB, FL)                                                                                     \
-  prefill_append_kernel<VB, FL><<<blocks, threads, 0, stream>>>(                                                \
-      static_cast<const uint8_t*>(k_new), static_cast<const uint8_t*>(v_new), n_stok_b, n_sh_b,                 \
-      static_cast<uint8_t*>(k_cache), static_cast<uint8_t*>(v_cache), c_sblk_b, c_stok_b, c_sh_b, bt_row,       \
-      max_blocks, start_pos, num_tokens, num_kv_heads, row_bytes, block_size, num_blocks, slots_out, error_word)
+  e = cudaLaunchKernelEx(&cfg, prefill_append_kernel<VB, FL>, static_cast<const uint8_t*>(k_new),               \
+                         static_cast<const uint8_t*>(v_new), n_stok_b, n_sh_b, static_cast<uint8_t*>(k_cache),   \
+                         static_cast<uint8_t*>(v_cache), c_sblk_b, c_stok_b, c_sh_b, bt_row, max_blocks,         \
+                         start_pos, num_tokens, num_kv_heads, row_bytes, block_size, num_blocks, slots_out,       \
+                         error_word)
   switch (vec_bytes) {
     case 16: if (flat) UBX_PREFILL(16, true); else UBX_PREFILL(16, false); break;
     case 8: if (flat) UBX_PREFILL(8, true); else UBX_PREFILL(8, false); break;
@@ -188,6 +203,7 @@ cudaError_t launch_prefill_append(const void* k_new, const void* v_new, int64_t 
     default: return cudaErrorInvalidValue;
   }
 #undef UBX_PREFILL
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

@@ -161,7 +161,7 @@ cudaError_t launch_prefill_append(const void* k_new, const void* v_new, int64_t 
                                   void* k_cache, void* v_cache, int64_t c_sblk_b, int64_t c_stok_b, int64_t c_sh_b,
                                   const int32_t* bt_row, int max_blocks, int64_t start_pos, int64_t num_tokens,
                                   int num_kv_heads, int row_bytes, int block_size, int64_t num_blocks, int vec_bytes,
-                                  int64_t* slots_out, int32_t* error_word, cudaStream_t stream);
+                                  int64_t* slots_out, int32_t* error_word, bool overlap, cudaStream_t stream);
 
 cudaError_t launch_qk_norm_rope(int dtype, const PrepParams& p, cudaStream_t stream);
 

@@ -32,7 +32,7 @@ SIGNATURES = {
                              _i32, _vp, _vp]),
     "ubx_slot_mapping": (_i32, [_vp, _i64, _vp, _vp, _i32, _i32, _i32, _vp]),
     "ubx_prefill_kv_write": (_i32, [_vp, _vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _vp, _i32, _i64, _i64, _i32,
-                                    _i32, _i32, _i64, _i32, _vp, _vp, _vp]),
+                                    _i32, _i32, _i64, _i32, _vp, _vp, _i32, _vp]),
     "ubx_paged_decode_workspace_size": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _i32, ctypes.POINTER(_sz)]),
     "ubx_workspace_init": (_i32, [_vp, _sz, _vp]),
     "ubx_paged_decode_attention": (_i32, [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _i64,

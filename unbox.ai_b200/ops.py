@@ -482,11 +482,13 @@ def prefill_slots(block_table_row: torch.Tensor, start_pos: int, num_tokens: int
 
 
 def prefill_kv_write(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
-                     block_table_row: torch.Tensor, start_pos: int) -> torch.Tensor:
+                     block_table_row: torch.Tensor, start_pos: int, *, overlap_previous: bool = False) -> torch.Tensor:
     """Write the K/V rows of a prefill chunk (T tokens of one sequence starting at
     ``start_pos``) into the pool: the per-token write_kv loop of prefill_step
     (engine.py:126-128) as one launch that computes each token's slot from the
-    block-table row and copies its rows. Returns the slots (T,) int64."""
+    block-table row and copies its rows. Returns the slots (T,) int64.
+    ``overlap_previous``: programmatic dependent launch (the launch overlaps the
+    previous kernel's drain; nothing is touched before that kernel completes)."""
     dev = _require_cuda(k, v, k_cache, v_cache, block_table_row)
     if k.dim() != 3 or v.shape != k.shape or k_cache.dim() != 4 or v_cache.shape != k_cache.shape:
         raise ValueError("expected k/v (T, KVH, D) and caches (NB, bs, KVH, D)")
@@ -514,7 +516,8 @@ def prefill_kv_write(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_
     st = _L.load().ubx_prefill_kv_write(k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), k_cache.data_ptr(),
                                         v_cache.data_ptr(), k_cache.stride(0), k_cache.stride(1), k_cache.stride(2),
                                         row.data_ptr(), row.shape[0], int(start_pos), T, KVH, D, bs, NB,
-                                        _DTYPES[k_cache.dtype], slots.data_ptr(), ws.error_word_ptr(), _stream(dev))
+                                        _DTYPES[k_cache.dtype], slots.data_ptr(), ws.error_word_ptr(),
+                                        _L.FLAG_OVERLAP_PREVIOUS if overlap_previous else 0, _stream(dev))
     _L.check(st, "prefill_kv_write")
     return slots
 
