@@ -36,6 +36,15 @@ def test_oracle_single_thread_equals_threaded(oracle):
     assert np.array_equal(a, b)
 
 
+def test_oracle_uses_every_core_on_request(oracle):
+    """The CPU baseline asks for every core the process may use, whatever
+    OMP_NUM_THREADS said (torchrun sets it to 1 for its ranks)."""
+    oracle.lib().oracle_set_num_threads(1)
+    assert oracle.num_threads() == 1
+    n = len(os.sched_getaffinity(0))
+    assert oracle.use_all_cores() == n == oracle.num_threads()
+
+
 def test_oracle_status_codes(oracle, pkg):
     lay = pkg.workloads.layout_uniform(5, 3, 1, 40, num_blocks=16)
     t = pkg.workloads.materialize_host(lay, 5)
