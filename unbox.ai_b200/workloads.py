@@ -57,7 +57,7 @@ def portable_uniform(seed: int, stream: int, n: int) -> np.ndarray:
 
 
 def portable_randint(seed: int, stream: int, n: int, lo: int, hi: int) -> np.ndarray:
-    """n integers uniform in [lo, hi] (inclusive, as BASELINE's U[lo, hi])."""
+    """n integers uniform in [lo, hi] (inclusive: the workloads' U[lo, hi] ranges)."""
     span = np.uint64(hi - lo + 1)
     return (lo + (_stream(seed, stream, n) % span).astype(np.int64)).astype(np.int64)
 
