@@ -18,6 +18,10 @@ copy streams that overlap the layer-calls (layer l waits for its own inputs).
 ``--impl reference`` times the CPU oracle (the reference algorithm restated in
 C, OpenMP over all host cores) on one layer-call of the same workload per step.
 
+``--op handoff`` and ``--op prefill`` measure the rows either side of the step
+(the KV page hand-off between workers, a prefill chunk's KV write); see
+bench_handoff and bench_prefill.
+
 Multi-GPU (torchrun): decode_760m runs one batch of 64 per GPU (weak scaling:
 requests partitioned across GPUs, no collective on the data path);
 ``--workload box_scale`` splits one batch of 1024 requests over the GPUs
