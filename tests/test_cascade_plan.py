@@ -110,6 +110,32 @@ def test_prefix_cut_before_another_requests_append_page():
     assert len(shared) == 7 and shared_page not in shared
 
 
+@pytest.mark.parametrize("heads", [(16, 8), (16, 2), (8, 8)])
+def test_member_blocks_fill_one_tensor_core_tile(heads):
+    """A large group is cut into member blocks of at most 128 / G members (one
+    128-row tile of (request, query head) rows per work item); every member of
+    every chunk is covered once, and the merge items list the members in
+    member-list order with the group's chunk count."""
+    H, KVH = heads
+    G = H // KVH
+    wl = PKG.workloads
+    lay = wl.layout_radix_prefix(9, batch=150, prefix_pages=19, suffix_lo=1, suffix_hi=40)
+    p = PKG.cascade.plan_cascade(lay.block_table, lay.context_lens, H, KVH, device="cpu")
+    cap = PKG.cascade.TILE_ROWS // G
+    nch = -(-19 // PKG.cascade.MAX_CHUNK_PAGES)
+    work = p.work.numpy()
+    assert (work[:, 1] <= cap).all() and (work[:, 3] <= PKG.cascade.MAX_CHUNK_PAGES).all()
+    assert len(work) == nch * -(-150 // cap)
+    cover = {}
+    mlist = p.member_list.numpy()
+    for m_off, nm, _, _, chunk, _ in work:
+        for b in mlist[m_off:m_off + nm]:
+            cover[(int(b), int(chunk))] = cover.get((int(b), int(chunk)), 0) + 1
+    assert set(cover.values()) == {1} and len(cover) == 150 * nch
+    items = p.merge_items.numpy()
+    assert np.array_equal(items[:, 0], mlist) and (items[:, 1] == nch).all()
+
+
 @pytest.mark.parametrize("heads", [(16, 8, 112), (16, 2, 64), (8, 8, 64)])
 def test_merge_of_plan_pieces_equals_full_attention(heads, oracle):
     """Attention over the suffix table + attention over the shared pages, merged
