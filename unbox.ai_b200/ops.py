@@ -531,6 +531,10 @@ def prefill_prep(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_weight: to
     T = q.shape[0]
     dev = _require_cuda(q)
     positions = torch.arange(start_pos, start_pos + T, dtype=torch.int32, device=dev)
-    slots = prefill_slots(block_table_row, start_pos, T, k_cache.shape[1])
+    row = _int32(block_table_row, "block_table_row").contiguous()
+    if row.dim() != 1:
+        raise ValueError("block_table_row must be 1-D")
+    # the same positions feed the slot computation and the kernel (one arange)
+    slots = slot_mapping(row.unsqueeze(0).expand(T, -1), positions, k_cache.shape[1])
     return qk_norm_rope(q, k, q_weight, k_weight, rope, positions, eps, v=v, k_cache=k_cache, v_cache=v_cache,
                         slot_mapping=slots)
