@@ -75,6 +75,21 @@ def parse():
     return ap.parse_args()
 
 
+def host_info():
+    """The host the CPU baseline ran on: logical CPUs, the ones this process may
+    use, and the CPU model."""
+    model = None
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    usable = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    return {"cpu_count": os.cpu_count(), "usable_cpus": usable, "cpu_model": model}
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -276,7 +291,7 @@ def bench_handoff(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(times) / len(times),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": config,
-            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": 1, "kind": "port", **host_info(),
                              "sample": "one prompt's pages per step: numpy gather + scatter (the reference's "
                                        "serialize_blocks / deserialize_blocks without the socket)"},
             "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
@@ -408,7 +423,7 @@ def bench_handoff(args):
             n += 1
         el = time.perf_counter() - t0
         line["cpu_baseline"] = {"value": round(payload * n / el / 1e9, 3), "unit": "GB/s", "cores": 1,
-                                "kind": "port", "sample": f"{n} prompt(s): numpy gather + scatter of 128 pages x 24 "
+                                "kind": "port", **host_info(), "sample": f"{n} prompt(s): numpy gather + scatter of 128 pages x 24 "
                                                           f"layers, {el:.1f} s"}
     if rank == 0:
         print(json.dumps(line))
@@ -488,7 +503,7 @@ def bench_prefill(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(times) / len(times),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": config,
-            "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+            "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": "port", **host_info(),
                              "sample": "one layer of the 2048-token chunk per step: "
                                        + ("numpy q/k norm + rotary, then " if args.prep else "")
                                        + "the C oracle's slot write"},
@@ -659,7 +674,7 @@ def bench_prefill(args):
             if el >= min(args.cpu_seconds, 5.0) or calls >= 100000:
                 break
         line["cpu_baseline"] = {"value": round(lay_b * calls / el / 1e9, 4), "unit": "GB/s", "cores": cores,
-                                "kind": "port", "sample": f"{calls} layer write(s) of the 2048-token chunk, {el:.1f} s"}
+                                "kind": "port", **host_info(), "sample": f"{calls} layer write(s) of the 2048-token chunk, {el:.1f} s"}
     if rank == 0:
         print(json.dumps(line))
     if world > 1:
@@ -730,7 +745,7 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * tot / len(times),
             "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": dtype_tag,
             "data": "synthetic", "config": config, "layer_calls_per_s": len(times) / tot,
-            "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+            "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": "port", **host_info(),
                              "sample": sample},
             "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }))
@@ -1037,7 +1052,7 @@ def main():
                 break
         cpu_gbs = abs_[0]["layer_call"] * calls / el / 1e9
         line["cpu_baseline"] = {"value": round(cpu_gbs, 4), "unit": "GB/s", "cores": oracle.num_threads(),
-                                "kind": "port",
+                                "kind": "port", **host_info(),
                                 "sample": f"{calls} layer-call(s) ({'norm + rotary + ' if args.prep else ''}"
                                           f"append + attention) of layer 0 of this "
                                           f"workload, C oracle with OpenMP, {el:.1f} s"}
