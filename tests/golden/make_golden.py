@@ -2,7 +2,9 @@
 
 Run in a container that has the reference checked out (read-only is fine):
 
-    python tests/golden/make_golden.py --reference /root/reference
+    UNBOX_REFERENCE=<reference checkout> python tests/golden/make_golden.py
+
+(or ``--reference <checkout>``).
 
 The attention cases (CASES) cover the append and the attention call; the
 pre-attention cases (PREP_CASES) add the q/k RMSNorm and rotary steps before
@@ -259,9 +261,12 @@ def run_handoff_case(ref_root, wl, name, L, NB, KVH, D, src_pages, dst_pages, se
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("UNBOX_REFERENCE"),
+                    help="reference checkout (default: $UNBOX_REFERENCE)")
     ap.add_argument("--only", default=None)
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("name the reference checkout with --reference or UNBOX_REFERENCE")
     pkg = load_package()
     wl = pkg.workloads
     for name, (spec, dtype, vs, seed) in CASES.items():
