@@ -395,16 +395,22 @@ int ubx_ipc_close_handle(void* base);
  * as ubx_paged_decode_attention, minus the workspace: the scratch lives in a
  * fixed 8 MiB array inside the library (every GPU that loads the library holds
  * it until the process exits). Sizes whose scratch would exceed it are rejected
- * with UBX_ERR_WORKSPACE and a message naming the limit (on a 148-SM B200 the
- * balanced schedule needs about 2.6 MiB in all at 16 heads of 112; the split
- * schedule needs batch * ceil(max_blocks_per_seq / split_pages) * num_heads *
- * (4*head_dim + 8) bytes beyond the 520 KiB counter prefix). The call itself
- * allocates nothing.
+ * with UBX_ERR_WORKSPACE and a message naming the limit and the bytes the call
+ * needs (on a 148-SM B200 the balanced schedule needs about 2.6 MiB in all at
+ * 16 heads of 112; the split schedule needs roughly batch *
+ * ceil(max_blocks_per_seq / split_pages) * num_heads * (4*head_dim + 8) bytes
+ * beyond the 520 KiB counter prefix, plus 256-byte alignment of each region;
+ * the dynamic schedule adds its part lists and per-CTA partials). The call
+ * itself allocates nothing.
  * The first call on each device looks up the array's device address (with that
- * device current); make that first call before any stream capture. Every call
- * shares the one array per device and clears its counters and error word on
- * `stream` before launching, so calls that overlap on the GPU (other streams,
- * other host threads) race and must be serialised by the caller.
+ * device current) and caches it for the process; make that first call before
+ * any stream capture. The device's primary context is assumed: after
+ * cudaDeviceReset, or under another driver-API context, the cached address is
+ * stale, so neither is supported. Every call shares the one array per device;
+ * once its arguments pass every check it clears the counters and error word on
+ * `stream` and launches (a rejected call touches nothing), so calls that
+ * overlap on the GPU (other streams, other host threads) race and must be
+ * serialised by the caller.
  *   error_word: optional device int32 that receives the call's UBX_DEVERR_* bits.
  */
 int ubx_paged_decode_attention_noalloc(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache,

@@ -63,3 +63,35 @@ def test_noalloc_rejects_sizes_beyond_its_scratch(pkg):
     st = call_noalloc(lib, d, out, err, schedule=2, split_pages=1, max_blocks=1 << 20)
     assert st == pkg.library.ERR_WORKSPACE
     assert b"fixed" in lib.ubx_last_error() and b"8388608" in lib.ubx_last_error()
+
+
+@pytest.mark.parametrize("schedule,heads", [(2, (16, 8, 112)), (3, (4, 4, 64))])
+def test_noalloc_split_and_dynamic_schedules_twice(schedule, heads, pkg, oracle):
+    """The split schedule (partials + log-sum-exp combine) and the dynamic one
+    (part lists, per-CTA partials, owner words) keep all their scratch in the
+    fixed array; the second call runs on what the first one left there."""
+    lib = pkg.library.load()
+    wl = pkg.workloads
+    H, KVH, D = heads
+    lay = wl.layout_uniform(43 + schedule, 48, 1, 2500, num_heads=H, num_kv_heads=KVH, head_dim=D)
+    host = wl.materialize_host(lay, 43 + schedule, dtype="bfloat16", value_scale=0.5)
+    d = {k: v.to(DEV) for k, v in host.items()}
+    g = torch.Generator().manual_seed(6)
+    q2_host = (torch.randn(host["q"].shape, generator=g) * 0.5).to(torch.bfloat16)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    name = {2: "split", 3: "dynamic"}[schedule]
+    for q_host in (host["q"], q2_host):
+        q = q_host.to(DEV)
+        out = torch.empty_like(q)
+        st = call_noalloc(lib, dict(d, q=q), out, err, schedule=schedule, split_pages=32)
+        assert st == 0, lib.ubx_last_error()
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        ref = pkg.paged_attention(q, d["k_cache"], d["v_cache"], d["block_table"], d["context_lens"],
+                                  schedule=name, split_pages=32)
+        e = (out.float() - ref.float()).abs()
+        assert e.max().item() <= 2e-2 and e.mean().item() <= 2e-3
+        exact, _ = oracle.paged_decode_attention(q_host, host["k_cache"], host["v_cache"], host["block_table"],
+                                                 host["context_lens"])
+        e = np.abs(out.float().cpu().numpy().astype(np.float64) - exact)
+        assert e.max() <= 2e-2 and e.mean() <= 2e-3

@@ -425,7 +425,8 @@ int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache
                 const int32_t* context_lens, void* out, int64_t o_s_b, int64_t o_s_h, int batch, int num_heads,
                 int num_kv_heads, int head_dim, int block_size, int64_t num_blocks, int max_blocks_per_seq,
                 float scale, int dtype, int schedule, int split_pages, int flags, void* workspace,
-                size_t workspace_bytes, const AppendArgs* app, const PrepArgs* prep, float* lse, void* stream) {
+                size_t workspace_bytes, const AppendArgs* app, const PrepArgs* prep, float* lse, void* stream,
+                size_t clear_bytes = 0) {
   g_last_error.clear();
   int st = check_shape(num_heads, num_kv_heads, head_dim, block_size, dtype);
   if (st != UBX_OK) return st;
@@ -554,6 +555,13 @@ int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache
 
   LaunchShape shape{pl.grid, pl.block, pl.smem, (flags & UBX_FLAG_OVERLAP_PREVIOUS) != 0};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (clear_bytes > 0) {
+    // a workspace shared between calls (the allocation-free entry point) is
+    // cleared only once the call has passed every check, so a rejected call
+    // leaves the state of a call still running elsewhere alone
+    cudaError_t ce = cudaMemsetAsync(workspace, 0, std::min(clear_bytes, workspace_bytes), s);
+    if (ce != cudaSuccess) return cuda_fail(ce, "workspace clear");
+  }
   cudaError_t e = pl.dynamic ? launch_paged_decode_dyn(dtype, head_dim, p, shape, s)
                              : launch_paged_decode(dtype, head_dim, pl.gw, pl.balanced, p, shape, s);
   if (e != cudaSuccess) return cuda_fail(e, "paged_decode launch");
@@ -565,6 +573,23 @@ int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache
 }
 
 }  // namespace
+
+namespace ubx {
+
+int paged_decode_attention_cleared(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache,
+                                   const void* v_cache, int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head,
+                                   const int32_t* block_table, int64_t bt_s_row, const int32_t* context_lens,
+                                   void* out, int64_t o_s_b, int64_t o_s_h, int batch, int num_heads, int num_kv_heads,
+                                   int head_dim, int block_size, int64_t num_blocks, int max_blocks_per_seq,
+                                   float scale, int dtype, int schedule, int split_pages, void* workspace,
+                                   size_t workspace_bytes, size_t clear_bytes, void* stream) {
+  return decode_impl(q, q_s_b, q_s_h, k_cache, v_cache, c_s_block, c_s_tok, c_s_head, block_table, bt_s_row,
+                     context_lens, out, o_s_b, o_s_h, batch, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
+                     max_blocks_per_seq, scale, dtype, schedule, split_pages, 0, workspace, workspace_bytes, nullptr,
+                     nullptr, nullptr, stream, clear_bytes);
+}
+
+}  // namespace ubx
 
 extern "C" {
 

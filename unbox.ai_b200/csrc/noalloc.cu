@@ -13,7 +13,11 @@
 // host code is only a stand-in for the symbol, never a device address, so the
 // address is looked up once per device with cudaGetSymbolAddress (with that
 // device current) and cached; the first call on each device performs that
-// lookup, so make the first call on a device before any stream capture.
+// lookup, so make the first call on a device before any stream capture. The
+// cache is keyed by device ordinal for the life of the process: it assumes the
+// device's primary context, so cudaDeviceReset (which unloads the module) and
+// calls made under another driver-API context of the same device are not
+// supported.
 #include <cstdio>
 #include <mutex>
 #include <string>
@@ -69,16 +73,15 @@ int ubx_paged_decode_attention_noalloc(const void* q, int64_t q_s_b, int64_t q_s
   void* scratch = nullptr;
   cudaError_t e = scratch_for_current_device(&scratch);
   if (e != cudaSuccess) return cuda_status(e, "scratch address lookup (cudaGetSymbolAddress)");
-  // The array keeps whatever the previous call left: re-zero the error word and
-  // the counters (the whole zero-initialised prefix of the workspace) before launching.
-  if (batch > 0) {
-    e = cudaMemsetAsync(scratch, 0, ubx::kWsZeroBytes, s);
-    if (e != cudaSuccess) return cuda_status(e, "scratch clear");
-  }
-  int st = ubx_paged_decode_attention(q, q_s_b, q_s_h, k_cache, v_cache, c_s_block, c_s_tok, c_s_head, block_table,
-                                      bt_s_row, context_lens, out, o_s_b, o_s_h, batch, num_heads, num_kv_heads,
-                                      head_dim, block_size, num_blocks, max_blocks_per_seq, scale, dtype, schedule,
-                                      split_pages, scratch, kNoAllocScratchBytes, stream);
+  // The array keeps whatever the previous call left: the error word and the
+  // counters (the whole zero-initialised prefix of the workspace) are re-zeroed
+  // on `stream` once the arguments have passed every check, just before the
+  // launch; a rejected call leaves the array untouched.
+  int st = ubx::paged_decode_attention_cleared(q, q_s_b, q_s_h, k_cache, v_cache, c_s_block, c_s_tok, c_s_head,
+                                               block_table, bt_s_row, context_lens, out, o_s_b, o_s_h, batch,
+                                               num_heads, num_kv_heads, head_dim, block_size, num_blocks,
+                                               max_blocks_per_seq, scale, dtype, schedule, split_pages, scratch,
+                                               kNoAllocScratchBytes, ubx::kWsZeroBytes, stream);
   if (st == UBX_ERR_WORKSPACE) {
     // the only workspace here is the fixed array: say so, with its limit
     char msg[512];

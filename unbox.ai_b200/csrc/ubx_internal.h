@@ -132,6 +132,17 @@ struct PrepParams {
 void set_last_error(const char* msg);
 const char* last_error();
 
+// ubx_paged_decode_attention that first zeroes the first `clear_bytes` of the
+// workspace on `stream`, after every argument check has passed and right
+// before the launch (capi.cu; the allocation-free entry point's shared scratch).
+int paged_decode_attention_cleared(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache,
+                                   const void* v_cache, int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head,
+                                   const int32_t* block_table, int64_t bt_s_row, const int32_t* context_lens,
+                                   void* out, int64_t o_s_b, int64_t o_s_h, int batch, int num_heads, int num_kv_heads,
+                                   int head_dim, int block_size, int64_t num_blocks, int max_blocks_per_seq,
+                                   float scale, int dtype, int schedule, int split_pages, void* workspace,
+                                   size_t workspace_bytes, size_t clear_bytes, void* stream);
+
 struct LaunchShape {
   dim3 grid;
   dim3 block;
@@ -179,7 +190,7 @@ struct KvCopyParams {
   int64_t page_bytes;
   unsigned long long* checksum;  // null: none
   int32_t* error;
-  bool dst_is_peer;  // destination outside this GPU's memory: no TMA stores to it
+  bool cross_gpu;  // source or destination outside this GPU's memory: plain loads and stores, no TMA
 };
 
 cudaError_t launch_kv_pages_copy(const KvCopyParams& p, cudaStream_t stream);
