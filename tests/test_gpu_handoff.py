@@ -152,6 +152,24 @@ def test_transfer_pages_across_gpus_over_nvlink(pkg, oracle):
     assert torch.equal(dst.cpu(), ref)
 
 
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_pull_pages_from_peer_gpu(pkg, oracle):
+    """The decode worker's GPU runs the copy and reads the prefill pool on the
+    other GPU (a peer source: plain loads over NVLink, no TMA load)."""
+    wl, ho = pkg.workloads, pkg.handoff
+    src_h = wl.materialize_pool_host(72, 3, 30, 16, 8, 112, "bfloat16")
+    dst_h = wl.materialize_pool_host(73, 3, 20, 16, 8, 112, "bfloat16", stream=31)
+    src, dst = src_h.to("cuda:0"), dst_h.to("cuda:1")
+    sp, dp = [1, 29, 7, 12, 3], [0, 19, 4, 8, 11]
+    ho.transfer_pages(src, sp, dst, dp, on="destination")
+    torch.cuda.synchronize("cuda:1")
+    ref = dst_h.clone()
+    oracle.scatter_pages(oracle.gather_pages(src_h, sp), ref, dp)
+    assert torch.equal(dst.cpu(), ref)
+    with torch.cuda.device("cuda:1"):
+        pkg.check_device_errors(torch.device("cuda:1"))
+
+
 def _ipc_rank(rank, port, result_path):
     """Two worker processes, one GPU each (worker.py:47-51): the decode worker
     (rank 1) exports its pool over CUDA IPC, the prefill worker (rank 0) writes

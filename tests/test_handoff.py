@@ -161,3 +161,12 @@ def test_invariant_divisor_identity():
         for n in [0, 1, d - 1, d, d + 1, 2 ** 31 - 1, 2 ** 32 - 1] + [rng.getrandbits(32) for _ in range(5000)]:
             if 0 <= n < 2 ** 32:
                 assert (((n * m) >> 32) + n) >> s == n // d, (d, n)
+
+
+def test_transfer_direction_is_checked(pkg):
+    """transfer_pages runs its kernel on the source (push) or the destination
+    (pull) GPU; anything else is rejected before any device work."""
+    import torch
+    pool = torch.zeros((1, 2, 4, 16, 8, 112), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="on must be"):
+        pkg.handoff.transfer_pages(pool, [0], pool, [1], on="sideways")

@@ -135,15 +135,20 @@ int ubx_kv_pages_copy(const void* src, int64_t src_s_layer, int64_t src_s_kv, in
   p.checksum = reinterpret_cast<unsigned long long*>(checksum);
   p.error = error_word;
   {
-    // local destinations take the TMA bulk path; another GPU's memory (peer
-    // access, IPC mapping) gets plain stores
+    // copies between two buffers of this GPU take the TMA bulk path; when
+    // either side is another GPU's memory (peer access, IPC mapping) the copy
+    // runs as plain 16-byte loads and stores: a peer destination never gets a
+    // TMA store, a peer source (a decode worker pulling pages) never a TMA load
     int dev = 0;
-    cudaPointerAttributes a;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return hcuda(e, "cudaGetDevice");
-    e = cudaPointerGetAttributes(&a, dst);
-    if (e != cudaSuccess) cudaGetLastError();
-    p.dst_is_peer = !(e == cudaSuccess && a.type == cudaMemoryTypeDevice && a.device == dev);
+    auto on_this_gpu = [&](const void* ptr) {
+      cudaPointerAttributes a;
+      cudaError_t pe = cudaPointerGetAttributes(&a, ptr);
+      if (pe != cudaSuccess) cudaGetLastError();
+      return pe == cudaSuccess && a.type == cudaMemoryTypeDevice && a.device == dev;
+    };
+    p.cross_gpu = !on_this_gpu(dst) || !on_this_gpu(src);
   }
   cudaError_t e = ubx::launch_kv_pages_copy(p, s);
   if (e != cudaSuccess) return hcuda(e, "kv_pages_copy launch");

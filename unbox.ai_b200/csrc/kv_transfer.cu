@@ -8,9 +8,10 @@
 // any two page layouts on the device:
 //   * pool -> packed wire payload (serialize), with the payload checksum fused;
 //   * packed payload -> pool pages (deserialize) at the receiver's own page ids;
-//   * pool -> pool directly, where the destination may be another GPU's memory
-//     (peer access or an IPC mapping): the rows cross NVLink as plain stores,
-//     with no staging buffer and no host round trip.
+//   * pool -> pool directly, where the destination (a prefill worker pushing)
+//     or the source (a decode worker pulling) may be another GPU's memory (peer
+//     access or an IPC mapping): the rows cross NVLink as plain loads and
+//     stores, with no staging buffer and no host round trip.
 // The packed payload has the reference's byte order: (layer, K|V, page, row).
 //
 // A page unit (one layer, K or V, one page) is page_bytes contiguous bytes in
@@ -254,7 +255,7 @@ cudaError_t launch_kv_pages_copy(const KvCopyParams& p, cudaStream_t stream) {
                      p.src_s_block, p.src_pages, p.src_num_blocks};
   const PageSide dst{static_cast<uint8_t*>(p.dst), p.dst_s_layer, p.dst_s_kv, p.dst_s_block, p.dst_pages,
                      p.dst_num_blocks};
-  if (!p.dst_is_peer) {
+  if (!p.cross_gpu) {
     // TMA bulk path: pieces of equal size (a multiple of 16 bytes), at most 16 KB
     const uint32_t ppu = (uint32_t)((p.page_bytes + kMaxPieceBytes - 1) / kMaxPieceBytes);
     const uint32_t piece = (uint32_t)(((p.page_bytes + ppu - 1) / ppu + 15) / 16 * 16);
@@ -278,7 +279,7 @@ cudaError_t launch_kv_pages_copy(const KvCopyParams& p, cudaStream_t stream) {
           src, dst, (uint32_t)p.num_pages, (uint64_t)p.page_bytes, ppu, piece, pieces, nullptr, p.error);
     return cudaGetLastError();
   }
-  // destination in another GPU's memory: plain 16-byte stores over NVLink
+  // a side in another GPU's memory: plain 16-byte loads and stores over NVLink
   const FastDiv vpu_div = make_fast_div((uint32_t)(p.page_bytes / 16));
   const FastDiv np_div = make_fast_div((uint32_t)p.num_pages);
   if (p.checksum)

@@ -173,28 +173,34 @@ def deserialize_blocks(pool: torch.Tensor, data: Union[bytes, bytearray, memoryv
         raise RuntimeError(f"KV page message checksum mismatch: {_u64(ck):#x} != header {int(h.checksum):#x}")
 
 
-def transfer_pages(src_pool: torch.Tensor, src_pages, dst_pool: torch.Tensor, dst_pages) -> None:
+def transfer_pages(src_pool: torch.Tensor, src_pages, dst_pool: torch.Tensor, dst_pages, on: str = "source") -> None:
     """Copy ``src_pages`` of every layer of ``src_pool`` into ``dst_pages`` of
-    ``dst_pool`` with one kernel on the source device (torch's current stream
-    there). When the pools sit on different GPUs the source GPU writes into the
-    destination's memory over NVLink (peer access is enabled on first use); the
-    caller orders later reads on the destination after this stream (e.g. an event)."""
-    sdev = _require_cuda(src_pool)
+    ``dst_pool`` with one kernel, on the source device (``on="source"``: a
+    prefill worker pushing) or on the destination device (``on="destination"``:
+    a decode worker pulling), on torch's current stream there. When the pools
+    sit on different GPUs that kernel reaches the other pool over NVLink with
+    plain loads or stores (peer access is enabled on first use); the caller
+    orders later use of the pages on the other GPU after this stream (e.g. an
+    event)."""
+    if on not in ("source", "destination"):
+        raise ValueError("on must be 'source' or 'destination'")
+    _require_cuda(src_pool)
     if dst_pool.device.type != "cuda":
         raise ValueError("dst_pool must be a CUDA tensor")
     g1, g2 = _geometry(src_pool), _geometry(dst_pool)
     if g1[0] != g2[0] or g1[2:] != g2[2:] or src_pool.dtype != dst_pool.dtype:
         raise ValueError("source and destination pools differ in dtype or page geometry")
     L, NB, bs, KVH, D = g1
-    si, di = _pages(src_pages, sdev), _pages(dst_pages, sdev)
+    run, other = (src_pool.device, dst_pool.device) if on == "source" else (dst_pool.device, src_pool.device)
+    si, di = _pages(src_pages, run), _pages(dst_pages, run)
     if si.numel() != di.numel():
         raise ValueError("as many destination pages as source pages")
-    with torch.cuda.device(sdev):
-        if dst_pool.device != sdev:
-            _L.check(_L.load().ubx_enable_peer_access(dst_pool.device.index), "enable peer access")
+    with torch.cuda.device(run):
+        if other != run:
+            _L.check(_L.load().ubx_enable_peer_access(other.index), "enable peer access")
         _copy(src_pool, (src_pool.stride(0), src_pool.stride(1), src_pool.stride(2)), si, NB,
               dst_pool, (dst_pool.stride(0), dst_pool.stride(1), dst_pool.stride(2)), di, g2[1], L, si.numel(),
-              bs * KVH * D, src_pool.dtype, None, sdev)
+              bs * KVH * D, src_pool.dtype, None, run)
 
 
 # ---------------------------------------------------------------------------
