@@ -42,9 +42,32 @@ def sha(t) -> str:
 
 
 _ALL_GOLDEN = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
-GOLDEN_NAMES = [n for n in _ALL_GOLDEN if not n.startswith(("prep_", "handoff_"))]  # append + attention
+GOLDEN_NAMES = [n for n in _ALL_GOLDEN if not n.startswith(("prep_", "handoff_", "engine_"))]  # append + attention
 PREP_GOLDEN_NAMES = [n for n in _ALL_GOLDEN if n.startswith("prep_")]  # norm + rotary (+ append, attention)
 HANDOFF_GOLDEN_NAMES = [n for n in _ALL_GOLDEN if n.startswith("handoff_")]  # serialize / deserialize
+ENGINE_GOLDEN_NAMES = [n for n in _ALL_GOLDEN if n.startswith("engine_")]  # the engine's decode flow
+
+
+def load_engine_golden(name: str):
+    """Engine-flow fixture (tests/golden/make_engine_golden.py): the record and
+    the KV pool as prefill left it, (L, 2, NB, bs, KVH, D) in the case's dtype
+    (checked by SHA-256)."""
+    import torch
+    z = dict(np.load(os.path.join(GOLDEN_DIR, name + ".npz")))
+    td = {"float32": torch.float32, "bfloat16": torch.bfloat16}[str(z["dtype"])]
+    pool0 = torch.from_numpy(z["pool0"]).to(td)
+    assert sha(pool0) == str(z["sha_pool0"]), f"{name}: stored pool differs from the engine's"
+    return z, pool0
+
+
+def engine_block_table(blocks_of_step) -> "np.ndarray":
+    """The decode step's block table as engine.py:179-185 builds it: int32,
+    (batch, longest block list), padded with -1."""
+    rows = [[int(x) for x in r if x >= 0] for r in blocks_of_step]
+    bt = np.full((len(rows), max(len(r) for r in rows)), -1, dtype=np.int32)
+    for i, r in enumerate(rows):
+        bt[i, :len(r)] = r
+    return bt
 
 
 def load_golden(name: str):
