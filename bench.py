@@ -15,8 +15,16 @@ step's per-token inputs (q, new K/V rows, block table, context lengths) copied
 from pinned host memory and the outputs copied back inside the timed region, on
 copy streams that overlap the layer-calls (layer l waits for its own inputs).
 
+``e2e_eager`` is the same end-to-end step launched from Python every step,
+with no CUDA graph and no events between launches, as the engine's eager
+decode loop calls the ops.
+
 ``--impl reference`` times the CPU oracle (the reference algorithm restated in
 C, OpenMP over all host cores) on one layer-call of the same workload per step.
+``cpu_baseline_ref`` reports the reference's own Python path
+(paged_decode_attention_ref + PagedKVCache.write_kv), timed where the
+reference is importable on a subsample and extrapolated
+(oracle/reference_cpu_path.json, made by oracle/time_reference_cpu.py).
 
 ``--op handoff`` and ``--op prefill`` measure the rows either side of the step
 (the KV page hand-off between workers, a prefill chunk's KV write); see
@@ -26,7 +34,12 @@ Multi-GPU (torchrun): decode_760m runs one batch of 64 per GPU (weak scaling:
 requests partitioned across GPUs, no collective on the data path);
 ``--workload box_scale`` splits one batch of 1024 requests over the GPUs
 (strong scaling, LPT placement, KV-head split of contexts over 2048 tokens).
-value = all ranks' bytes / the slowest rank's time.
+value = all ranks' bytes / the slowest rank's time. Every default line also
+carries ``box_scale``: that strong-scaling split measured in the same run at
+this N, with the whole batch timed on rank 0's GPU alone for its efficiency.
+
+The default 200 timed steps keep the timed region long enough (about 0.25 s
+on one GPU) for a few dozen NVML clock samples.
 """
 from __future__ import annotations
 
@@ -47,7 +60,7 @@ METRIC = "decode-attn HBM GB/s (% of peak) and layer-calls/s at 1/2/4/8 B200 vs 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="decode_760m",
@@ -72,6 +85,10 @@ def parse():
                          "shared-prefix pass and merge (plan built on the host once per step)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-box-scale", dest="box_scale", action="store_false",
+                    help="skip the box-scale strong-scaling sub-record of the default decode_760m line")
+    ap.add_argument("--box-scale-layers", type=int, default=12,
+                    help="per-layer caches of the box-scale sub-record (4.5 GB each on one GPU, > L2)")
     return ap.parse_args()
 
 
@@ -682,6 +699,120 @@ def bench_prefill(args):
         dist.destroy_process_group()
 
 
+def box_scale_record(args, pkg, rank: int, world: int, device, reduce_max, barrier):
+    """Strong-scaling sub-record carried by every default line: the box-scale
+    batch (1024 requests, contexts log-normal with median 1024, clipped to
+    [128, 4096]) split over the N GPUs of this run by ``plan_shards`` (LPT
+    placement, KV-head split of contexts over 2048 tokens; no collective on the
+    data path), each layer-call its KV append + attention launch(es), timed like
+    the main step (CUDA-graph replay, device events, max over ranks). Rank 0
+    then runs the whole batch alone (the one-GPU plan) in the same process, the
+    baseline of the efficiency value_N / (N * value_1). ``--box-scale-layers``
+    per-layer caches rotate (4.5 GB each on one GPU: every layer-call streams
+    from HBM)."""
+    import torch
+    wl = pkg.workloads
+    spec = wl.NAMED["box_scale"]
+    L = args.box_scale_layers
+
+    def timed(parts, seed0):
+        devs = [wl.materialize_device(lay, seed0 + i, spec["dtype"], spec["scale_values"], L)
+                for i, (_, lay) in enumerate(parts)]
+        outs = [[torch.empty_like(d["q"][l]) for l in range(L)] for d in devs]
+
+        def step():
+            for l in range(L):
+                for i, d in enumerate(devs):
+                    pkg.paged_attention(d["q"][l], d["k_caches"][l], d["v_caches"][l], d["block_table"],
+                                        d["context_lens"], out=outs[i][l], k_new=d["k_new"][l], v_new=d["v_new"][l],
+                                        overlap_previous=True)
+
+        for _ in range(max(3, args.warmup)):
+            step()
+        torch.cuda.synchronize()
+        pkg.check_device_errors(device)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            step()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step()
+        for _ in range(max(3, args.warmup)):
+            g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(args.steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        del g
+        pkg.check_device_errors(device)
+        step_bytes = L * sum(wl.algorithmic_bytes(lay, 2)["layer_call"] for _, lay in parts)
+        launches = L * len(parts)
+        del devs, outs
+        torch.cuda.empty_cache()
+        return e0.elapsed_time(e1), step_bytes, launches
+
+    parts, _, glay = build_parts(pkg, "box_scale", rank, world)
+    barrier()
+    ms, step_bytes, launches = timed(parts, 5000 + 31 * rank)
+    barrier()
+    ms_max = reduce_max(ms)
+    bytes_all = float(step_bytes)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([bytes_all], device=device, dtype=torch.float64)
+        dist.all_reduce(t)
+        bytes_all = float(t.item())
+    value = bytes_all * args.steps / (ms_max / 1e3) / 1e9
+    peak, _ = peaks()
+    rec = {"workload": "box_scale", "requests": int(glay.batch), "sigma": 0.6, "layers": L,
+           "value": round(value, 2), "unit": "GB/s", "ms_per_step": round(ms_max / args.steps, 4),
+           "frac_per_gpu": round(value / world / peak, 4), "gpu_launches_per_rank_step": launches,
+           "timing": "graph replay, device events, max over ranks",
+           "plan": "plan_shards: LPT on KV bytes, KV heads of contexts > 2048 split across GPUs"}
+    if world == 1:
+        rec.update(value_1gpu=rec["value"], efficiency=1.0)
+    else:
+        v1 = None
+        if rank == 0:
+            p1, _, _ = build_parts(pkg, "box_scale", 0, 1)
+            ms1, b1, _ = timed(p1, 7000)
+            v1 = b1 * args.steps / (ms1 / 1e3) / 1e9
+        barrier()
+        if rank == 0:
+            rec.update(value_1gpu=round(v1, 2), efficiency=round(value / (world * v1), 4),
+                       value_1gpu_source="the whole batch on rank 0's GPU alone, same process, after the N-GPU run")
+    return rec
+
+
+def reference_cpu_path(workload: str):
+    """The reference's own Python path (paged_decode_attention_ref + write_kv)
+    timed where the reference is importable, on a subsample extrapolated per
+    (sequence, head, position): oracle/reference_cpu_path.json, written by
+    oracle/time_reference_cpu.py. None when absent."""
+    try:
+        with open(os.path.join(ROOT, "oracle", "reference_cpu_path.json")) as f:
+            rec = json.load(f)
+    except (OSError, ValueError):
+        return None
+    w = rec.get("workloads", {}).get(workload)
+    if w is None:
+        return None
+    return {"value": w["value"], "unit": w["unit"], "layer_calls_per_s": w["layer_calls_per_s"],
+            "cores": w["torch_threads"], "kind": "reference", "extrapolated": True,
+            "cpu_model": rec.get("cpu_model"), "cpu_count": rec.get("cpu_count"), "when": rec.get("when"),
+            "measured_on": "the build host, where the reference is importable (it does not travel to the GPU host)",
+            "sample": (f"reference paged_decode_attention_ref + PagedKVCache.write_kv, unmodified, on sequences "
+                       f"{w['sample']['sequences']} (contexts {w['sample']['context_lens']}), all heads, one layer: "
+                       f"{w['per_seq_head_pos_us']} us per (sequence, head, position), extrapolated to the whole "
+                       f"layer-call ({w['extrapolated_layer_call_s']} s)")}
+
+
 def main():
     args = parse()
     if args.op == "handoff":
@@ -985,6 +1116,21 @@ def main():
     torch.cuda.synchronize()
     barrier()
     e2e_ms = reduce(e0.elapsed_time(e1), dist.ReduceOp.MAX)
+    # the same end-to-end step launched from Python every step, as the engine's
+    # eager decode loop calls the ops (engine.py:157-234): no CUDA graph and no
+    # events between launches
+    e2e_eager_ms = None
+    if eg is not None:
+        for _ in range(3):
+            e2e_step()
+        barrier()
+        e0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        e2e_eager_ms = reduce(e0.elapsed_time(e1), dist.ReduceOp.MAX)
     h2d = sum(stg.nbytes for _, _, stg in hosts)
     if args.cascade:
         h2d += sum(t.numel() * t.element_size() for h, _, _ in hosts for t in h["plan"].values())
@@ -1023,6 +1169,12 @@ def main():
                      "shared_tokens": sum(d["plan"].shared_tokens for d in devs)} if args.cascade else None),
         "overlap_previous": bool(args.overlap and not args.separate),
     }
+    if e2e_eager_ms is not None:
+        line["e2e_eager"] = {"value": round(step_bytes_all * args.steps / (e2e_eager_ms / 1e3) / 1e9, 2),
+                             "unit": "GB/s", "ms_per_step": round(e2e_eager_ms / args.steps, 4),
+                             "vs_e2e": round(e2e_ms / e2e_eager_ms, 4),
+                             "launch": "the e2e step launched from Python every step: no CUDA graph, no events "
+                                       "between launches (the engine's eager loop)"}
     achieved = kernel_bytes / (kernel_avg_ms / 1e3) / 1e9
     line["roofline"] = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                         "frac": round(achieved / peak, 4), "traffic": profiled_traffic(args.workload),
@@ -1056,9 +1208,17 @@ def main():
                                 "sample": f"{calls} layer-call(s) ({'norm + rotary + ' if args.prep else ''}"
                                           f"append + attention) of layer 0 of this "
                                           f"workload, C oracle with OpenMP, {el:.1f} s"}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        ref_cpu = reference_cpu_path(args.workload)
+        if ref_cpu is not None:
+            line["cpu_baseline_ref"] = ref_cpu
+    del graph
+    if (args.box_scale and args.workload == "decode_760m" and not (args.cascade or args.prep or args.separate)
+            and args.graph):
+        line["box_scale"] = box_scale_record(args, pkg, rank, world, device,
+                                             lambda x: reduce(x, dist.ReduceOp.MAX), barrier)
     if rank == 0:
         print(json.dumps(line))
-    del graph
     if world > 1:
         dist.destroy_process_group()
 
