@@ -31,18 +31,24 @@ _SCHEDULES = {"auto": _L.SCHEDULE_AUTO, "balanced": _L.SCHEDULE_BALANCED, "split
               "dynamic": _L.SCHEDULE_DYNAMIC}
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(device: torch.device) -> int:
+    """Handle of torch's current CUDA stream on ``device`` (what every op launches on)."""
+    if _raw_stream is not None and device.index is not None:
+        return _raw_stream(device.index)  # the same handle, without building a Stream object per call
     return torch.cuda.current_stream(device).cuda_stream
 
 
 def _require_cuda(*ts):
-    dev = ts[0].device
+    idx = ts[0].get_device()  # -1 for host memory
     for t in ts:
-        if t.device.type != "cuda":
+        if not t.is_cuda:
             raise ValueError("unbox_b200 ops run on CUDA tensors only (no CPU fallback)")
-        if t.device != dev:
-            raise ValueError(f"tensors on different devices: {dev} vs {t.device}")
-    return dev
+        if t.get_device() != idx:
+            raise ValueError(f"tensors on different devices: {ts[0].device} vs {t.device}")
+    return ts[0].device
 
 
 class DecodeWorkspace:
@@ -57,6 +63,7 @@ class DecodeWorkspace:
     def __init__(self, device: torch.device):
         self.device = torch.device(device)
         self.buf: Optional[torch.Tensor] = None
+        self._sized: set = set()  # call sizes already known to fit the current buffer
 
     @property
     def nbytes(self) -> int:
@@ -66,6 +73,9 @@ class DecodeWorkspace:
                num_kv_heads: int = 0, dtype: Optional[torch.dtype] = None):
         """Grow to what a call with these sizes needs (``num_kv_heads`` and a 16-bit
         ``dtype`` add room for the dynamic schedule)."""
+        key = (batch, num_heads, head_dim, max_blocks, split_pages, num_kv_heads, dtype)
+        if key in self._sized:  # the decode loop asks the same sizes every layer: answer from the cache
+            return self.buf
         lib = _L.load()
         need = ctypes.c_size_t(0)
         with torch.cuda.device(self.device):
@@ -77,6 +87,8 @@ class DecodeWorkspace:
             self.buf = torch.zeros(n, dtype=torch.uint8, device=self.device)
             _L.check(lib.ubx_workspace_init(self.buf.data_ptr(), self.buf.numel(), _stream(self.device)),
                      "workspace init")
+            self._sized.clear()
+        self._sized.add(key)
         return self.buf
 
     def error_word_ptr(self) -> int:
@@ -159,24 +171,29 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
     if q.dtype not in _DTYPES or k_cache.dtype != q.dtype or v_cache.dtype != q.dtype:
         raise TypeError(f"q, k_cache, v_cache must share one of {list(_DTYPES)}; got {q.dtype}, "
                         f"{k_cache.dtype}, {v_cache.dtype}")
-    if k_cache.stride() != v_cache.stride():
+    q_st, c_st = q.stride(), k_cache.stride()
+    if c_st != v_cache.stride():
         raise ValueError("k_cache and v_cache must have the same strides")
     B, H, D = q.shape
     NB, bs, KVH, D2 = k_cache.shape
     if D2 != D:
         raise ValueError(f"head_dim mismatch: q {D} vs cache {D2}")
-    if q.stride(-1) != 1 or k_cache.stride(-1) != 1:
+    if q_st[2] != 1 or c_st[3] != 1:
         raise ValueError("the head_dim dimension must be contiguous")
     block_table = _int32(block_table, "block_table")
     context_lens = _int32(context_lens, "context_lens")
-    if block_table.dim() != 2 or block_table.shape[0] != B or block_table.stride(-1) != 1:
+    bt_st = block_table.stride()
+    if block_table.dim() != 2 or block_table.shape[0] != B or bt_st[1] != 1:
         raise ValueError(f"block_table must be (B, max_blocks) with contiguous rows; got {tuple(block_table.shape)}")
     if context_lens.shape != (B,) or not context_lens.is_contiguous():
         raise ValueError(f"context_lens must be a contiguous ({B},) tensor")
     if out is None:
         out = torch.empty((B, H, D), dtype=q.dtype, device=dev)
-    elif out.shape != (B, H, D) or out.dtype != q.dtype or out.stride(-1) != 1:
-        raise ValueError("out must be (B, H, D) in q's dtype with a contiguous last dimension")
+        o_st = out.stride()
+    else:
+        o_st = out.stride()
+        if out.shape != (B, H, D) or out.dtype != q.dtype or o_st[2] != 1:
+            raise ValueError("out must be (B, H, D) in q's dtype with a contiguous last dimension")
     if B == 0:
         return out
     if scale is None:
@@ -185,15 +202,14 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
     ws = workspace or workspace_for(dev)
     buf = ws.ensure(B, H, D, max_blocks, split_pages, KVH, q.dtype)
     lib = _L.load()
-    tail = (block_table.data_ptr(), block_table.stride(0), context_lens.data_ptr(), out.data_ptr(), out.stride(0),
-            out.stride(1), B, H, KVH, D, bs, NB, max_blocks, float(scale), _DTYPES[q.dtype], _SCHEDULES[schedule],
+    tail = (block_table.data_ptr(), bt_st[0], context_lens.data_ptr(), out.data_ptr(), o_st[0], o_st[1],
+            B, H, KVH, D, bs, NB, max_blocks, float(scale), _DTYPES[q.dtype], _SCHEDULES[schedule],
             int(split_pages), buf.data_ptr(), buf.numel(), _stream(dev))
     if k_new is None:
         if overlap_previous:
             raise ValueError("overlap_previous applies to the fused append + attention call")
         st = lib.ubx_paged_decode_attention(
-            q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(),
-            k_cache.stride(0), k_cache.stride(1), k_cache.stride(2), *tail)
+            q.data_ptr(), q_st[0], q_st[1], k_cache.data_ptr(), v_cache.data_ptr(), c_st[0], c_st[1], c_st[2], *tail)
         _L.check(st, "paged_decode_attention")
     else:
         _require_cuda(q, k_new, v_new)
@@ -201,13 +217,13 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
             raise ValueError(f"k_new / v_new must be ({B}, {KVH}, {D})")
         if k_new.dtype != q.dtype or v_new.dtype != q.dtype:
             raise TypeError("k_new / v_new must have the cache dtype")
-        if k_new.stride() != v_new.stride() or k_new.stride(-1) != 1:
+        n_st = k_new.stride()
+        if n_st != v_new.stride() or n_st[2] != 1:
             raise ValueError("k_new and v_new need equal strides and a contiguous last dimension")
         st = lib.ubx_paged_decode_append_attention(
-            k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0), k_new.stride(1),
-            q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(),
-            k_cache.stride(0), k_cache.stride(1), k_cache.stride(2), *tail[:-3],
-            _L.FLAG_OVERLAP_PREVIOUS if overlap_previous else 0, *tail[-3:])
+            k_new.data_ptr(), v_new.data_ptr(), n_st[0], n_st[1],
+            q.data_ptr(), q_st[0], q_st[1], k_cache.data_ptr(), v_cache.data_ptr(), c_st[0], c_st[1], c_st[2],
+            *tail[:-3], _L.FLAG_OVERLAP_PREVIOUS if overlap_previous else 0, *tail[-3:])
         _L.check(st, "paged_decode_append_attention")
     return out
 
