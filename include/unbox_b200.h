@@ -49,13 +49,11 @@ extern "C" {
 #define UBX_DEVERR_BAD_SLOT 16     /* kv_append slot >= num_blocks * block_size: row skipped */
 #define UBX_DEVERR_BAD_POSITION 32 /* rotary position outside [0, rope_positions): row left unrotated */
 #define UBX_DEVERR_BAD_WORK 64     /* cascade work or merge item out of range: item skipped */
-#define UBX_DEVERR_CAPACITY 128    /* dynamic schedule: partial-result storage exhausted; output undefined */
 
 /* work schedules of the attention kernel */
 #define UBX_SCHEDULE_AUTO 0     /* library picks */
 #define UBX_SCHEDULE_BALANCED 1 /* persistent grid, equal pages per CTA, in-kernel LSE merge */
 #define UBX_SCHEDULE_SPLIT 2    /* fixed split-KV chunks per sequence + LSE combine kernel */
-#define UBX_SCHEDULE_DYNAMIC 3  /* bf16/f16: balanced ranges taken in grabs, idle CTAs steal the others' pages */
 
 /* call flags (ubx_paged_decode_append_attention) */
 #define UBX_FLAG_OVERLAP_PREVIOUS 1 /* launch with programmatic dependent launch: the kernel may start, and
@@ -123,9 +121,9 @@ int ubx_slot_mapping(const int32_t* block_table, int64_t bt_s_row, const int32_t
 /*
  * Bytes of device workspace the attention entry points need for these sizes on
  * the current device (partial results of split sequences, merge counters, the
- * error word; sized for up to 4 CTAs per SM and, for bf16/f16, for the dynamic
- * schedule). The workspace must be zeroed once with ubx_workspace_init before
- * its first use; the kernels leave it ready for the next call.
+ * error word; sized for up to 4 CTAs per SM). The workspace must be zeroed once
+ * with ubx_workspace_init before its first use; the kernels leave it ready for
+ * the next call.
  */
 int ubx_paged_decode_workspace_size(int batch, int num_heads, int num_kv_heads, int head_dim, int max_blocks_per_seq,
                                     int split_pages, int dtype, size_t* bytes);
@@ -399,8 +397,8 @@ int ubx_ipc_close_handle(void* base);
  * needs (on a 148-SM B200 the balanced schedule needs about 2.6 MiB in all at
  * 16 heads of 112; the split schedule needs roughly batch *
  * ceil(max_blocks_per_seq / split_pages) * num_heads * (4*head_dim + 8) bytes
- * beyond the 520 KiB counter prefix, plus 256-byte alignment of each region;
- * the dynamic schedule adds its part lists and per-CTA partials). The call
+ * beyond the 256 KiB counter prefix, plus 256-byte alignment of each region).
+ * The call
  * itself allocates nothing.
  * The first call on each device looks up the array's device address (with that
  * device current) and caches it for the process; make that first call before

@@ -354,6 +354,9 @@ def test_overlap_previous_layers_match(graph, pkg):
     torch.cuda.synchronize()
     pkg.check_device_errors()
     for l in range(L):
-        assert torch.equal(outs_ref[l], outs_ovl[l])
+        # with overlap the last CTA's range is shorter, so sequences are cut at other
+        # pages and the partial sums merge in another order: equal within the tolerance
+        e = (outs_ref[l].float() - outs_ovl[l].float()).abs()
+        assert e.max().item() <= 2e-2 and e.mean().item() <= 2e-3, (e.max().item(), e.mean().item())
         assert torch.equal(ref_dev["k_caches"][l], ovl_dev["k_caches"][l])
         assert torch.equal(ref_dev["v_caches"][l], ovl_dev["v_caches"][l])

@@ -280,12 +280,14 @@ def test_prep_graph_capture(pkg):
     tab = rope.to(DEV)
     args = (d["q_raw"], d["k_raw"], d["v_new"], d["q_weight"], d["k_weight"], tab, c["k_cache"], c["v_cache"],
             c["block_table"], c["context_lens"], 1e-6)
-    out_eager = pkg.paged_decode_prep_attention(*args).clone()
+    # both with programmatic overlap: the flag also shapes the work split (the last
+    # CTA's range is shorter), so eager and replayed calls use the same one
+    out_eager = pkg.paged_decode_prep_attention(*args, overlap_previous=True).clone()
     out = torch.empty_like(out_eager)
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
-        pkg.paged_decode_prep_attention(*args, out=out)
+        pkg.paged_decode_prep_attention(*args, out=out, overlap_previous=True)
     torch.cuda.current_stream().wait_stream(s)
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):

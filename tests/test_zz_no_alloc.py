@@ -65,10 +65,10 @@ def test_noalloc_rejects_sizes_beyond_its_scratch(pkg):
     assert b"fixed" in lib.ubx_last_error() and b"8388608" in lib.ubx_last_error()
 
 
-@pytest.mark.parametrize("schedule,heads", [(2, (16, 8, 112)), (3, (4, 4, 64))])
-def test_noalloc_split_and_dynamic_schedules_twice(schedule, heads, pkg, oracle):
-    """The split schedule (partials + log-sum-exp combine) and the dynamic one
-    (part lists, per-CTA partials, owner words) keep all their scratch in the
+@pytest.mark.parametrize("schedule,heads", [(1, (16, 8, 112)), (2, (16, 8, 112)), (2, (4, 4, 64))])
+def test_noalloc_balanced_and_split_schedules_twice(schedule, heads, pkg, oracle):
+    """The balanced schedule (merge counters, partials of cut sequences) and the
+    split one (partials + log-sum-exp combine) keep all their scratch in the
     fixed array; the second call runs on what the first one left there."""
     lib = pkg.library.load()
     wl = pkg.workloads
@@ -79,7 +79,7 @@ def test_noalloc_split_and_dynamic_schedules_twice(schedule, heads, pkg, oracle)
     g = torch.Generator().manual_seed(6)
     q2_host = (torch.randn(host["q"].shape, generator=g) * 0.5).to(torch.bfloat16)
     err = torch.zeros(1, dtype=torch.int32, device=DEV)
-    name = {2: "split", 3: "dynamic"}[schedule]
+    name = {1: "balanced", 2: "split"}[schedule]
     for q_host in (host["q"], q2_host):
         q = q_host.to(DEV)
         out = torch.empty_like(q)

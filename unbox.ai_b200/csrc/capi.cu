@@ -38,31 +38,20 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 constexpr size_t kHeaderBytes = kWsHeaderBytes;        // error word + reserved
 constexpr size_t kCounterEntries = kWsCounterEntries;  // merge counters, re-armed by the kernel
 constexpr int kDefaultSplitPages = 32;                 // 512-token split-KV chunks
-// Whether UBX_SCHEDULE_AUTO picks the dynamic (work-sharing) variant for the
-// bf16/f16 batches the balanced schedule can take. Off: on the measured
-// workloads the dynamic kernel streams each page more slowly than the balanced
-// one gains by evening out the CTAs' end times.
-constexpr bool kAutoDynamic = false;
-
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct WsLayout {
   size_t ml_off, o_off, total;
-  size_t dyn_list_off, dyn_ml_off, dyn_o_off;  // dynamic schedule regions (total includes them when used)
   int64_t slots;
 };
 
-// [zeroed prefix | static partials (ml, o) | dynamic part lists | dynamic partials (ml, o)]
-WsLayout ws_layout(int64_t slots, int num_heads, int head_dim, int64_t dyn_list_entries = 0, int64_t dyn_rows = 0) {
+// [zeroed prefix | partials (max, sum) | partial outputs]
+WsLayout ws_layout(int64_t slots, int num_heads, int head_dim) {
   WsLayout w;
   w.slots = slots;
   w.ml_off = kWsZeroBytes;
   w.o_off = w.ml_off + align256((size_t)slots * num_heads * sizeof(float2));
   w.total = w.o_off + (size_t)slots * num_heads * head_dim * sizeof(float);
-  w.dyn_list_off = align256(w.total);
-  w.dyn_ml_off = w.dyn_list_off + align256((size_t)dyn_list_entries * sizeof(int32_t));
-  w.dyn_o_off = w.dyn_ml_off + align256((size_t)dyn_rows * sizeof(float2));
-  if (dyn_rows > 0) w.total = w.dyn_o_off + (size_t)dyn_rows * head_dim * sizeof(float);
   return w;
 }
 
@@ -86,9 +75,6 @@ int num_sms_current_device(int* n) {
 struct Plan {
   int gw, wpk, hg, n_hg, stages, smem, row, pitch, tile, pbuf, ctas_per_sm;
   bool balanced;
-  bool dynamic;             // balanced ranges with grabs and steals (bf16/f16)
-  int64_t dyn_list_entries; // [batch][num_kv_heads][kDynMaxParts]
-  int64_t dyn_rows;         // partial rows: CTAs * kDynSlotsPerCta * heads per CTA
   int split_pages, max_chunks;
   dim3 grid, block;
   int64_t slots;
@@ -116,12 +102,9 @@ int make_plan(int batch, int num_heads, int num_kv_heads, int head_dim, int dtyp
   pl->pitch = tile_row_pitch(pl->row);   // its shared-memory pitch
   pl->n_hg = num_kv_heads / pl->hg;
   const bool can_balance = batch <= kMaxBatchSmem && (int64_t)batch * num_kv_heads * pl->wpk <= (int64_t)kCounterEntries;
-  if ((schedule == UBX_SCHEDULE_BALANCED || schedule == UBX_SCHEDULE_DYNAMIC) && !can_balance)
-    return fail(UBX_ERR_UNSUPPORTED, "balanced and dynamic schedules need batch <= %d (got %d)", kMaxBatchSmem, batch);
-  if (schedule == UBX_SCHEDULE_DYNAMIC && !mma)
-    return fail(UBX_ERR_UNSUPPORTED, "the dynamic schedule is built for bf16/f16");
-  pl->dynamic = mma && can_balance && (schedule == UBX_SCHEDULE_DYNAMIC || (schedule == UBX_SCHEDULE_AUTO && kAutoDynamic));
-  pl->balanced = pl->dynamic || schedule == UBX_SCHEDULE_BALANCED || (schedule == UBX_SCHEDULE_AUTO && can_balance);
+  if (schedule == UBX_SCHEDULE_BALANCED && !can_balance)
+    return fail(UBX_ERR_UNSUPPORTED, "the balanced schedule needs batch <= %d (got %d)", kMaxBatchSmem, batch);
+  pl->balanced = schedule == UBX_SCHEDULE_BALANCED || (schedule == UBX_SCHEDULE_AUTO && can_balance);
   pl->split_pages = split_pages > 0 ? split_pages : kDefaultSplitPages;
   pl->max_chunks = (max_blocks + pl->split_pages - 1) / pl->split_pages;
   pl->tile = kBlockSize * pl->pitch;
@@ -141,19 +124,9 @@ int make_plan(int batch, int num_heads, int num_kv_heads, int head_dim, int dtyp
   pl->ctas_per_sm = ctas;
   pl->smem = decode_smem_bytes(pl->tile, pl->pbuf, pl->stages, prefix);
   pl->block = dim3((pl->hg * pl->wpk + 1) * 32);
-  pl->dyn_list_entries = pl->dyn_rows = 0;
   if (pl->balanced) {
     pl->grid = dim3(std::max(1, num_sms * ctas / pl->n_hg), pl->n_hg);
     pl->slots = 2 * (int64_t)pl->grid.x;
-    if (pl->dynamic && (int64_t)pl->grid.x * pl->grid.y > kMaxCtasTotal) {
-      if (schedule == UBX_SCHEDULE_DYNAMIC)
-        return fail(UBX_ERR_UNSUPPORTED, "dynamic schedule: more than %d CTAs", kMaxCtasTotal);
-      pl->dynamic = false;
-    }
-    if (pl->dynamic) {
-      pl->dyn_list_entries = (int64_t)batch * num_kv_heads * kDynMaxParts;
-      pl->dyn_rows = (int64_t)pl->grid.x * pl->grid.y * kDynSlotsPerCta * pl->hg * G;
-    }
   } else {
     pl->grid = dim3((unsigned)((int64_t)batch * pl->max_chunks), pl->n_hg);
     pl->slots = (int64_t)batch * pl->max_chunks;
@@ -368,16 +341,7 @@ int ubx_paged_decode_workspace_size(int batch, int num_heads, int num_kv_heads, 
   const int sp = split_pages > 0 ? split_pages : kDefaultSplitPages;
   const int64_t chunks = (max_blocks_per_seq + sp - 1) / sp;
   const int64_t slots = std::max<int64_t>(2 * (int64_t)sms * kMaxCtasPerSm, (int64_t)batch * chunks);
-  size_t total = ws_layout(slots, num_heads, head_dim).total;
-  // room for the dynamic schedule too, where it applies to these sizes
-  Plan pl;
-  if ((dtype == UBX_DTYPE_BF16 || dtype == UBX_DTYPE_F16) && batch > 0 &&
-      check_shape(num_heads, num_kv_heads, head_dim, kBlockSize, dtype) == UBX_OK &&
-      make_plan(batch, num_heads, num_kv_heads, head_dim, dtype, std::max(1, max_blocks_per_seq),
-                UBX_SCHEDULE_DYNAMIC, split_pages, sms, &pl) == UBX_OK)
-    total = std::max(total, ws_layout(slots, num_heads, head_dim, pl.dyn_list_entries, pl.dyn_rows).total);
-  g_last_error.clear();
-  *bytes = total;
+  *bytes = ws_layout(slots, num_heads, head_dim).total;
   return UBX_OK;
 }
 
@@ -432,8 +396,7 @@ int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache
   if (st != UBX_OK) return st;
   if (batch < 0) return fail(UBX_ERR_INVALID_ARGUMENT, "negative batch");
   if (batch == 0) return UBX_OK;
-  if (schedule != UBX_SCHEDULE_AUTO && schedule != UBX_SCHEDULE_BALANCED && schedule != UBX_SCHEDULE_SPLIT &&
-      schedule != UBX_SCHEDULE_DYNAMIC)
+  if (schedule != UBX_SCHEDULE_AUTO && schedule != UBX_SCHEDULE_BALANCED && schedule != UBX_SCHEDULE_SPLIT)
     return fail(UBX_ERR_INVALID_ARGUMENT, "unknown schedule %d", schedule);
   if (!q || !k_cache || !v_cache || !block_table || !context_lens || !out)
     return fail(UBX_ERR_INVALID_ARGUMENT, "null pointer");
@@ -483,20 +446,7 @@ int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache
   st = make_plan(batch, num_heads, num_kv_heads, head_dim, dtype, max_blocks_per_seq, schedule, split_pages, sms, &pl,
                  reserve);
   if (st != UBX_OK) return st;
-  if (pl.dynamic) {
-    // the producer copies the appended token's heads as one row: they must be contiguous in k_new / v_new
-    const bool rows_ok = !app || app->s_head == head_dim;
-    const bool fits = ws_layout(pl.slots, num_heads, head_dim, pl.dyn_list_entries, pl.dyn_rows).total <= workspace_bytes;
-    if (schedule == UBX_SCHEDULE_DYNAMIC && !rows_ok)
-      return fail(UBX_ERR_UNSUPPORTED, "dynamic schedule: k_new / v_new heads must be contiguous (head stride %d)",
-                  head_dim);
-    if (schedule == UBX_SCHEDULE_AUTO && (!rows_ok || !fits)) {
-      st = make_plan(batch, num_heads, num_kv_heads, head_dim, dtype, max_blocks_per_seq, UBX_SCHEDULE_BALANCED,
-                     split_pages, sms, &pl, reserve);
-      if (st != UBX_OK) return st;
-    }
-  }
-  const WsLayout wl = ws_layout(pl.slots, num_heads, head_dim, pl.dyn_list_entries, pl.dyn_rows);
+  const WsLayout wl = ws_layout(pl.slots, num_heads, head_dim);
   if (workspace_bytes < wl.total)
     return fail(UBX_ERR_WORKSPACE, "workspace of %zu bytes, this call needs %zu", workspace_bytes, wl.total);
 
@@ -526,15 +476,12 @@ int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache
   p.stages = pl.stages;
   p.split_pages = pl.split_pages;
   p.max_chunks = pl.max_chunks;
+  p.tail_trim = ((flags & UBX_FLAG_OVERLAP_PREVIOUS) && pl.balanced && pl.ctas_per_sm == 1 &&
+                 pl.grid.y == 1)
+                    ? kTailTrimPages : 0;
   p.part_o = reinterpret_cast<float*>(ws + wl.o_off);
   p.part_ml = reinterpret_cast<float2*>(ws + wl.ml_off);
   p.counters = reinterpret_cast<int32_t*>(ws + kHeaderBytes);
-  p.dyn_own = reinterpret_cast<unsigned long long*>(ws + kWsDynOwnOff);
-  p.dyn_ctas_done = reinterpret_cast<int32_t*>(ws + kWsDynDoneOff);
-  p.dyn_nparts = reinterpret_cast<int32_t*>(ws + kWsDynNpartsOff);
-  p.dyn_part_list = pl.dynamic ? reinterpret_cast<int32_t*>(ws + wl.dyn_list_off) : nullptr;
-  p.dyn_part_ml = pl.dynamic ? reinterpret_cast<float2*>(ws + wl.dyn_ml_off) : nullptr;
-  p.dyn_part_o = pl.dynamic ? reinterpret_cast<float*>(ws + wl.dyn_o_off) : nullptr;
   p.error = reinterpret_cast<int32_t*>(ws);
   p.k_cache = k_cache;
   p.v_cache = v_cache;
@@ -562,8 +509,7 @@ int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache
     cudaError_t ce = cudaMemsetAsync(workspace, 0, std::min(clear_bytes, workspace_bytes), s);
     if (ce != cudaSuccess) return cuda_fail(ce, "workspace clear");
   }
-  cudaError_t e = pl.dynamic ? launch_paged_decode_dyn(dtype, head_dim, p, shape, s)
-                             : launch_paged_decode(dtype, head_dim, pl.gw, pl.balanced, p, shape, s);
+  cudaError_t e = launch_paged_decode(dtype, head_dim, pl.gw, pl.balanced, p, shape, s);
   if (e != cudaSuccess) return cuda_fail(e, "paged_decode launch");
   if (!pl.balanced) {
     e = launch_lse_combine(dtype, head_dim, p, s);

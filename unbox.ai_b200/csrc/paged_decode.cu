@@ -314,8 +314,22 @@ __device__ __forceinline__ void page_update(const T* __restrict__ kt, const T* _
 // ---------------------------------------------------------------- shared CTA plumbing
 
 struct Work {
-  int g_begin, g_end, b_first, w_eff, total, chunk, n_split;
+  int g_begin, g_end, b_first, w_eff, total, chunk, n_split, trim;
 };
+
+// Balanced ranges: CTA x streams flattened pages [range_begin(x),
+// range_begin(x + 1)). The shares are equal, except that with `trim` > 0 the
+// last CTA takes `trim` pages fewer than the others: under programmatic overlap
+// it is the CTA the hardware dispatches last, onto the SM that the previous
+// grid's last CTA frees, so it starts after every other CTA has prefetched.
+__device__ __forceinline__ int range_begin(const Work& w, int x) {
+  return x >= w.w_eff ? w.total : (int)((int64_t)(w.total + w.trim) * x / w.w_eff);
+}
+
+// The CTA whose range holds flattened page gp.
+__device__ __forceinline__ int cta_of(const Work& w, int gp) {
+  return min(w.w_eff - 1, (int)(((int64_t)(gp + 1) * w.w_eff - 1) / (w.total + w.trim)));
+}
 
 struct Seg {
   int b, s0, s1, lp0, lp1;
@@ -347,11 +361,10 @@ struct Smem {
   float* p_buf;
   uint64_t* full_bar;
   uint64_t* empty_bar;
-  int4* info;  // dynamic schedule: (sequence, page index, page id) of each stage; sequence -1 = end
   int32_t* prefix;
 };
 
-// Layout: [stages][p_buf][full x stages][empty x stages][info x stages][prefix]
+// Layout: [stages][p_buf][full x stages][empty x stages][prefix]
 // (per-stage slots sized by the launch's stage count: every byte counts toward
 // fitting one more stage)
 __device__ __forceinline__ Smem carve_smem(uint8_t* smem, const DecodeParams& p) {
@@ -361,8 +374,7 @@ __device__ __forceinline__ Smem carve_smem(uint8_t* smem, const DecodeParams& p)
   s.p_buf = reinterpret_cast<float*>(smem + p.stages * stage_bytes);
   s.full_bar = reinterpret_cast<uint64_t*>(smem + p.stages * stage_bytes + p.pbuf_bytes);
   s.empty_bar = s.full_bar + p.stages;
-  s.info = reinterpret_cast<int4*>(s.empty_bar + p.stages);  // 16-byte aligned: 2 x stages x 8 bytes before
-  s.prefix = reinterpret_cast<int32_t*>(s.info + p.stages);
+  s.prefix = reinterpret_cast<int32_t*>(s.empty_bar + p.stages);
   return s;
 }
 
@@ -371,15 +383,17 @@ __device__ __forceinline__ Smem carve_smem(uint8_t* smem, const DecodeParams& p)
 // context_lens. Ends with a CTA barrier (publishes mbarrier init).
 template <typename T, int D, bool BAL>
 __device__ Work setup_work(const DecodeParams& p, const Smem& sm, int32_t* warp_tot) {
-  Work w{0, 0, 0, 1, 0, 0, 0};
+  Work w{0, 0, 0, 1, 0, 0, 0, 0};
   const int B = p.batch;
   if constexpr (BAL) {
     build_page_prefix(p, sm.prefix, warp_tot);
     w.total = sm.prefix[B];
     w.w_eff = min((int)gridDim.x, w.total);
+    // the last range keeps at least half of an even share
+    if (w.w_eff > 1) w.trim = max(0, min(p.tail_trim, w.total / (2 * w.w_eff)));
     if ((int)blockIdx.x < w.w_eff) {
-      w.g_begin = (int)((int64_t)w.total * blockIdx.x / w.w_eff);
-      w.g_end = (int)((int64_t)w.total * (blockIdx.x + 1) / w.w_eff);
+      w.g_begin = range_begin(w, blockIdx.x);
+      w.g_end = range_begin(w, blockIdx.x + 1);
       int lo = 0, hi = B;  // last b with prefix[b] <= g_begin
       while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
@@ -478,6 +492,7 @@ __device__ void produce(const DecodeParams& p, const Work& w, const Smem& sm, in
                      (int64_t)head0 * p.c_sh * (int64_t)sizeof(T);
   const int t = lane & 15;
   const int dst_off = (lane >> 4) * tile + t * p.smem_row_bytes;
+  const uint64_t stream_policy = l2_policy_evict_first();  // pages are read once: keep the metadata in L2
   uint32_t it = 0;
   RingPos pos{0, 0};
   bool ok = true;
@@ -508,8 +523,9 @@ __device__ void produce(const DecodeParams& p, const Work& w, const Smem& sm, in
         }
         uint8_t* dst = sm.stages + st * stage_bytes;
         if (in_pool) {
-          bulk_copy_g2s(dst + dst_off, base + ((int64_t)page * p.c_sblk + (int64_t)t * p.c_stok) * (int64_t)sizeof(T),
-                        p.row_bytes, &sm.full_bar[st]);
+          bulk_copy_g2s_hint(dst + dst_off,
+                             base + ((int64_t)page * p.c_sblk + (int64_t)t * p.c_stok) * (int64_t)sizeof(T),
+                             p.row_bytes, &sm.full_bar[st], stream_policy);
         } else {
           // a page outside the pool (reported above) reads as zeros
           for (int i = lane * 16; i < stage_bytes; i += 32 * 16)
@@ -548,26 +564,24 @@ __device__ __forceinline__ int64_t partial_slot(const DecodeParams& p, const Wor
 template <typename T, int D>
 __device__ void publish_and_merge(const DecodeParams& p, const Work& w, const Seg& s, int64_t ctr_index, int head0,
                                   int nh, int lane) {
-  __threadfence();
+  // the lanes' partial stores are ordered before lane 0's release by the warp
+  // barrier; the counter's acquire-release add publishes them and, for the
+  // warp that completes the count, orders the other parts' stores before its loads
   __syncwarp();
-  auto wid = [&](int gp) { return (int)(((int64_t)(gp + 1) * w.w_eff - 1) / w.total); };
-  const int w_first = wid(s.s0), w_last = wid(s.s1 - 1);
+  const int w_first = cta_of(w, s.s0), w_last = cta_of(w, s.s1 - 1);
   const int nparts = w_last - w_first + 1;
   int last = 0;
-  if (lane == 0) {
-    const int old = atomicAdd(&p.counters[ctr_index], 1);
-    last = old == nparts - 1;
-    if (last) atomicExch(&p.counters[ctr_index], 0);
-  }
+  if (lane == 0) last = atom_add_acq_rel_gpu(&p.counters[ctr_index], 1) == nparts - 1;
   if (__shfl_sync(kFull, last, 0)) {
-    __threadfence();
     const int sb0 = s.s0;
     auto slot_of = [&](int i) -> int64_t {
       const int wi = w_first + i;
-      const int sw = (int)((int64_t)w.total * wi / w.w_eff);
-      return 2 * (int64_t)wi + (sw < sb0 ? 1 : 0);
+      return 2 * (int64_t)wi + (range_begin(w, wi) < sb0 ? 1 : 0);
     };
     merge_rows<T, D>(p, s.b, head0, nh, nparts, slot_of, lane);
+    // re-armed for the next launch: every part has counted, and the next grid
+    // reads the counter only after this one has completed
+    if (lane == 0) st_relaxed_gpu(&p.counters[ctr_index], 0);
   }
 }
 
@@ -942,451 +956,6 @@ __device__ void consume_mma(const DecodeParams& p, const Work& w, const Smem& sm
   }
 }
 
-// ---------------------------------------------------------------- dynamic (work-sharing) schedule
-//
-// Every CTA starts from its balanced static range of the flattened (sequence,
-// page) list but takes its pages in grabs, through a per-CTA word in the
-// workspace (low half: pages its owner took from the front; high half: pages
-// other CTAs took from the back). A CTA whose range is used up steals from the
-// back of the CTA with the most pages left, so all CTAs finish within a few
-// pages of one another whatever their start time or streaming rate. The
-// producer records in shared memory which (sequence, page) each stage holds;
-// a consumer warp keeps one accumulator per run of pages of one sequence, and
-// the partial runs of a sequence are merged by the warp that completes its page
-// count (an atomic counter, no waiting).
-
-struct DynRange {
-  int begin, end, fixed;  // static range; its first `fixed` pages are streamed before any grab
-};
-
-__device__ __forceinline__ DynRange dyn_range(int total, int w_eff, int stages, int c) {
-  DynRange r{total, total, 0};
-  if (c < w_eff) {
-    r.begin = (int)((int64_t)total * c / w_eff);
-    r.end = (int)((int64_t)total * (c + 1) / w_eff);
-    r.fixed = min(stages, r.end - r.begin);
-  }
-  return r;
-}
-
-// Sequence holding flattened page g: the last b with prefix[b] <= g.
-__device__ __forceinline__ int seq_of(const int32_t* prefix, int B, int g) {
-  int lo = 0, hi = B - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (lds_int(prefix + mid) <= g) lo = mid; else hi = mid - 1;
-  }
-  return lo;
-}
-
-// Pages left in CTA v's range (negative once used up).
-__device__ __forceinline__ int dyn_left(unsigned long long word, const DynRange& r) {
-  return (r.end - (int)(word >> 32)) - (r.begin + max((int)(uint32_t)word, r.fixed));
-}
-
-template <typename T, int D>
-__device__ void produce_dyn(const DecodeParams& p, const Work& w, const Smem& sm, int head0, int lane) {
-  const int STAGES = p.stages;
-  const int tile = p.tile_bytes, stage_bytes = 2 * tile;
-  const int B = p.batch;
-  const char* base = reinterpret_cast<const char*>(lane < 16 ? p.k_cache : p.v_cache) +
-                     (int64_t)head0 * p.c_sh * (int64_t)sizeof(T);
-  // the token being decoded is copied from k_new / v_new (heads contiguous) in place of its pool row
-  const char* nbase = p.k_new == nullptr ? nullptr
-                                         : reinterpret_cast<const char*>(lane < 16 ? p.k_new : p.v_new) +
-                                               (int64_t)head0 * p.n_sh * (int64_t)sizeof(T);
-  const int t = lane & 15;
-  const int dst_off = (lane >> 4) * tile + t * p.smem_row_bytes;
-  unsigned long long* own = p.dyn_own + (int64_t)blockIdx.y * gridDim.x;
-  uint32_t it = 0;
-  RingPos pos{0, 0};
-  bool ok = true;
-
-  // Window of 32 consecutive flattened pages whose (sequence, page index, page
-  // id, appended-row slot) the lanes hold: one block-table read per 32 pages.
-  int win = -1, wb = 0, wlp = 0, wpage = 0, wslot = -1;
-  auto fill = [&](int g0) {
-    win = g0;
-    wslot = -1;
-    const int g = g0 + lane;
-    if (g < w.total) {
-      wb = seq_of(sm.prefix, B, g);
-      const int p0 = lds_int(sm.prefix + wb), p1 = lds_int(sm.prefix + wb + 1);
-      wlp = g - p0;
-      wpage = __ldg(p.block_table + (int64_t)wb * p.bt_sb + wlp);
-      if (nbase != nullptr && wlp == p1 - p0 - 1) {
-        const int ctx = __ldg(&p.context_lens[wb]);
-        if (ctx >= 1 && (ctx - 1) / kBlockSize < p.max_blocks) wslot = (ctx - 1) & (kBlockSize - 1);
-      }
-    }
-  };
-  // page g of the flattened list into the next stage
-  auto issue_one = [&](int g) {
-    if (win < 0 || g < win || g >= win + 32) fill(g);
-    const int i = g - win;
-    const int b = __shfl_sync(kFull, wb, i), lp = __shfl_sync(kFull, wlp, i);
-    const int page = __shfl_sync(kFull, wpage, i), a_slot = __shfl_sync(kFull, wslot, i);
-    const bool in_pool = page >= 0 && (int64_t)page < p.num_blocks;
-    if (!in_pool && lane == 0) set_error(p.error, kErrBadPage);
-    const int st = pos.st;
-    int good = 1;
-    if (lane == 0) {
-      if (!mbar_wait_bounded(&sm.empty_bar[st], pos.ph ^ 1u)) {
-        good = 0;
-      } else {
-        sts_int4(sm.info + st, make_int4(b, lp, page, in_pool ? a_slot : -1));
-        if (in_pool) mbar_arrive_expect_tx(&sm.full_bar[st], 2 * kBlockSize * p.row_bytes);
-      }
-    }
-    if (!__shfl_sync(kFull, good, 0)) {
-      ok = false;
-      return;
-    }
-    uint8_t* dst = sm.stages + st * stage_bytes;
-    if (in_pool) {
-      const char* src = t == a_slot ? nbase + (int64_t)b * p.n_stok * (int64_t)sizeof(T)
-                                    : base + ((int64_t)page * p.c_sblk + (int64_t)t * p.c_stok) * (int64_t)sizeof(T);
-      bulk_copy_g2s(dst + dst_off, src, p.row_bytes, &sm.full_bar[st]);
-    } else {
-      // a page outside the pool (reported above) reads as zeros
-      for (int i2 = lane * 16; i2 < stage_bytes; i2 += 32 * 16)
-        *reinterpret_cast<uint4*>(dst + i2) = make_uint4(0, 0, 0, 0);
-      fence_proxy_async_smem();  // before later bulk copies refill this stage
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.full_bar[st]);
-    }
-    ++it;
-    pos.next(STAGES);
-  };
-
-  // the head of the own range needs no grab: stream it at once
-  const DynRange me = dyn_range(w.total, w.w_eff, STAGES, blockIdx.x);
-  for (int g = me.begin; g < me.begin + me.fixed && ok; ++g) issue_one(g);
-  // the owner words are re-zeroed by the previous grid's last CTA: touch them only after it completed
-  griddep_wait();
-  // Own range in grabs from the front, each requested one grab ahead so its
-  // atomic round trip overlaps the streaming of the previous one. Grabs shrink
-  // with the pages left, so little of the range is reserved near its end.
-  auto grab_size = [&](int left) { return min(kDynOwnerPages, max(2, left / 4)); };
-  uint32_t inc = (uint32_t)(grab_size(me.end - me.begin - me.fixed) + me.fixed);
-  unsigned long long pend = 0;
-  if (lane == 0) pend = atomicAdd(own + blockIdx.x, (unsigned long long)inc);
-  for (bool first = true; ok;) {
-    const unsigned long long old = __shfl_sync(kFull, pend, 0);
-    const int lo = (int)(uint32_t)old, hi = (int)(old >> 32);
-    const int from = me.begin + (first ? me.fixed : lo);
-    const int to = min(me.begin + lo + (int)inc, me.end - hi);
-    first = false;
-    if (from >= to) break;
-    inc = (uint32_t)grab_size(me.end - hi - to);
-    if (lane == 0) pend = atomicAdd(own + blockIdx.x, (unsigned long long)inc);
-    for (int g = from; g < to && ok; ++g) issue_one(g);
-  }
-  // steal from the back of the CTA with the most pages left (worth it from 4 pages)
-  for (int runs = 0; ok && runs < kDynMaxStealRuns;) {
-    int best = 0, victim = -1;
-    for (int v = lane; v < w.w_eff; v += 32) {
-      const int left = dyn_left(__ldcg(own + v), dyn_range(w.total, w.w_eff, STAGES, v));
-      if (left > best) {
-        best = left;
-        victim = v;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const int ob = __shfl_xor_sync(kFull, best, o), ov = __shfl_xor_sync(kFull, victim, o);
-      if (ob > best) {
-        best = ob;
-        victim = ov;
-      }
-    }
-    best = __shfl_sync(kFull, best, 0);
-    victim = __shfl_sync(kFull, victim, 0);
-    if (best < 4 || victim < 0) break;
-    const int k = min(kDynMaxStealPages, best / 2);
-    unsigned long long old = 0;
-    if (lane == 0) old = atomicAdd(own + victim, (unsigned long long)k << 32);
-    old = __shfl_sync(kFull, old, 0);
-    const DynRange r = dyn_range(w.total, w.w_eff, STAGES, victim);
-    const int back = r.end - (int)(old >> 32);
-    const int from = max(back - k, r.begin + max((int)(uint32_t)old, r.fixed));
-    if (from < back) {
-      for (int g = from; g < back && ok; ++g) issue_one(g);
-      ++runs;
-    }
-  }
-  // end marker for the consumers
-  if (ok) {
-    const int st = pos.st;
-    int good = 1;
-    if (lane == 0) {
-      if (!mbar_wait_bounded(&sm.empty_bar[st], pos.ph ^ 1u)) {
-        good = 0;
-      } else {
-        sts_int4(sm.info + st, make_int4(-1, 0, 0, -1));
-        mbar_arrive(&sm.full_bar[st]);
-      }
-    }
-    if (__shfl_sync(kFull, good, 0)) {
-      ++it;
-      pos.next(STAGES);
-    } else {
-      ok = false;
-    }
-  }
-  if (!ok && lane == 0) set_error(p.error, kErrTimeout);
-  // the CTA must not retire with bulk copies still writing its shared memory
-  if (lane == 0) {
-    const uint32_t n = it < (uint32_t)STAGES ? it : (uint32_t)STAGES;
-    RingPos back = pos;
-    for (uint32_t k = 1; k <= n; ++k) {
-      back.prev(STAGES);
-      if (!mbar_wait_bounded(&sm.full_bar[back.st], back.ph)) set_error(p.error, kErrTimeout);
-    }
-  }
-}
-
-// Merge of the partial runs of (sequence b, KV head kvh) into the rows of heads
-// head0 .. head0 + G - 1. Lanes are (head, 16-byte output chunk); part i's rows
-// start at row index list[i] of the dynamic partial store.
-template <typename T, int D>
-__device__ void merge_dyn(const DecodeParams& p, int b, int kvh, int head0, int G, int nparts, int lane) {
-  constexpr int EPC = Elem<T>::kPerChunk;
-  constexpr int DCH = D / EPC;
-  constexpr int HPW = 32 / DCH;
-  const int32_t* list = p.dyn_part_list + ((int64_t)b * p.num_kv_heads + kvh) * kDynMaxParts;
-  for (int hb = 0; hb < G; hb += HPW) {
-    const int g = hb + lane / DCH, c = lane % DCH;
-    if (lane >= HPW * DCH || g >= G) continue;  // no warp collectives below
-    float M = -INFINITY, L = 0.f, o[EPC];
-#pragma unroll
-    for (int e = 0; e < EPC; ++e) o[e] = 0.f;
-#pragma unroll 4
-    for (int i = 0; i < nparts; ++i) {
-      const int64_t row = (int64_t)__ldcg(&list[i]) + g;
-      const float2 ml = __ldcg(&p.dyn_part_ml[row]);
-      const float4* src = reinterpret_cast<const float4*>(p.dyn_part_o + row * D + c * EPC);
-      float4 v[EPC / 4];
-#pragma unroll
-      for (int e4 = 0; e4 < EPC / 4; ++e4) v[e4] = __ldcg(src + e4);
-      if (ml.x > M) {
-        const float sc = exp2f(M - ml.x);  // M = -inf at first: sc = 0
-        L *= sc;
-#pragma unroll
-        for (int e = 0; e < EPC; ++e) o[e] *= sc;
-        M = ml.x;
-      }
-      const float wgt = exp2f(ml.x - M);
-      L = fmaf(ml.y, wgt, L);
-#pragma unroll
-      for (int e4 = 0; e4 < EPC / 4; ++e4) {
-        o[4 * e4 + 0] = fmaf(wgt, v[e4].x, o[4 * e4 + 0]);
-        o[4 * e4 + 1] = fmaf(wgt, v[e4].y, o[4 * e4 + 1]);
-        o[4 * e4 + 2] = fmaf(wgt, v[e4].z, o[4 * e4 + 2]);
-        o[4 * e4 + 3] = fmaf(wgt, v[e4].w, o[4 * e4 + 3]);
-      }
-    }
-    const float inv = 1.f / L;
-#pragma unroll
-    for (int e = 0; e < EPC; ++e) o[e] *= inv;
-    const int head = head0 + g;
-    T* dst = reinterpret_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)head * p.o_sh + c * EPC;
-    *reinterpret_cast<uint4*>(dst) = Elem<T>::pack(o);
-    if (p.lse && c == 0) p.lse[(int64_t)b * p.num_heads + head] = M + log2f(L);
-  }
-}
-
-// Tensor-core consumer of the dynamic schedule: the same page math as
-// consume_mma, with the runs of consecutive stages of one sequence (read from
-// the stage records) as its segments.
-template <typename T, int D>
-__device__ void consume_dyn(const DecodeParams& p, const Smem& sm, int kh, int kvh, int lane) {
-  constexpr int KS = D / 16;
-  constexpr int NT = D / 8;
-  constexpr int RC = D / 8;  // 16-byte chunks of one head row
-  const int G = p.num_heads / p.num_kv_heads;
-  const int head0 = kvh * G;
-  const int qr = lane >> 2, qc = lane & 3;
-  const bool real_row = qr < G;
-  const float c = p.scale_log2;
-  const int STAGES = p.stages, stage_bytes = 2 * p.tile_bytes;
-  const int rs = p.smem_row_bytes / (int)sizeof(T);
-  const int k_row = (((lane >> 4) & 1) * 8 + (lane & 7)) * rs + ((lane >> 3) & 1) * 8;
-  const int v_row = (((lane >> 3) & 1) * 8 + (lane & 7)) * rs + ((lane >> 4) & 1) * 8;
-  const int a_which = lane / RC, a_chunk = lane % RC;
-  const int hgg = p.heads_per_cta * G;  // query heads of the CTA: the rows of one partial slot
-  const int64_t slot0 = ((int64_t)blockIdx.y * gridDim.x + blockIdx.x) * kDynSlotsPerCta;
-  int used = 0;  // partial slots used (the same count in every consumer warp of the CTA)
-
-  RingPos pos{0, 0};
-  int cur = -1, n_b = 0, ctx = 0, ctx_raw = 0, run = 0;
-  uint32_t qa[KS][2];
-  float m = -INFINITY, l = 0.f;
-  float o[NT][2];
-#pragma unroll
-  for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = 0.f;
-
-  auto close_run = [&]() {
-    l += __shfl_xor_sync(kFull, l, 1);
-    l += __shfl_xor_sync(kFull, l, 2);
-    if (run == n_b) {  // the whole sequence went through this CTA
-      if (real_row) {
-        const float inv = 1.f / l;
-        uint32_t* dst = reinterpret_cast<uint32_t*>(reinterpret_cast<T*>(p.out) + (int64_t)cur * p.o_sb +
-                                                    (int64_t)(head0 + qr) * p.o_sh + 2 * qc);
-#pragma unroll
-        for (int n = 0; n < NT; ++n) dst[4 * n] = Elem<T>::pack2(o[n][0] * inv, o[n][1] * inv);
-        if (p.lse && qc == 0) p.lse[(int64_t)cur * p.num_heads + head0 + qr] = fmaf(m, c, log2f(l));
-      }
-      return;
-    }
-    if (used >= kDynSlotsPerCta) {
-      if (lane == 0) set_error(p.error, kErrCapacity);
-      return;
-    }
-    const int64_t row0 = (slot0 + used) * hgg + (int64_t)kh * G;
-    ++used;
-    if (real_row) {
-      float2* dst = reinterpret_cast<float2*>(p.dyn_part_o + (row0 + qr) * D + 2 * qc);
-#pragma unroll
-      for (int n = 0; n < NT; ++n) dst[4 * n] = make_float2(o[n][0], o[n][1]);
-      if (qc == 0) p.dyn_part_ml[row0 + qr] = make_float2(m * c, l);
-    }
-    __threadfence();
-    __syncwarp();
-    const int64_t idx = (int64_t)cur * p.num_kv_heads + kvh;
-    int last = 0, np = 0;
-    if (lane == 0) {
-      const int k = atomicAdd(&p.dyn_nparts[idx], 1);
-      if (k < kDynMaxParts)
-        p.dyn_part_list[idx * kDynMaxParts + k] = (int32_t)row0;
-      else
-        set_error(p.error, kErrCapacity);
-      __threadfence();
-      const int old = atomicAdd(&p.counters[idx], run);
-      last = old + run == n_b;
-      if (last) {
-        np = min(atomicExch(&p.dyn_nparts[idx], 0), kDynMaxParts);
-        atomicExch(&p.counters[idx], 0);  // re-armed for the next call
-      }
-    }
-    if (__shfl_sync(kFull, last, 0)) {
-      __threadfence();
-      merge_dyn<T, D>(p, cur, kvh, head0, G, __shfl_sync(kFull, np, 0), lane);
-    }
-  };
-
-  bool ok = true;
-  for (;; pos.next(STAGES)) {
-    const int st = pos.st;
-    if (!mbar_wait_bounded(&sm.full_bar[st], pos.ph)) {
-      ok = false;
-      break;
-    }
-    const int4 inf = lds_int4(sm.info + st);  // (sequence, page index, page id, appended-row slot or -1)
-    if (inf.x < 0) {  // end marker (may be the first stage: a CTA that found no pages)
-      if (cur >= 0) close_run();
-      break;
-    }
-    if (inf.x != cur) {
-      if (cur >= 0) close_run();
-      cur = inf.x;
-      n_b = lds_int(sm.prefix + cur + 1) - lds_int(sm.prefix + cur);
-      ctx_raw = __ldg(&p.context_lens[cur]);
-      ctx = min(max(ctx_raw, 0), n_b * kBlockSize);
-      run = 0;
-      const T* qrow = reinterpret_cast<const T*>(p.q) + (int64_t)cur * p.q_sb + (int64_t)(head0 + qr) * p.q_sh;
-#pragma unroll
-      for (int ks = 0; ks < KS; ++ks) {
-        qa[ks][0] = real_row ? __ldg(reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 2 * qc)) : 0u;
-        qa[ks][1] = real_row ? __ldg(reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 8 + 2 * qc)) : 0u;
-      }
-      if (p.rope) prep_q<T, D>(p, ctx_raw - 1, real_row, qc, lane, qa);
-      m = -INFINITY;
-      l = 0.f;
-#pragma unroll
-      for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = 0.f;
-    }
-    const int lp = inf.y;
-    T* kt = reinterpret_cast<T*>(sm.stages + st * stage_bytes) + kh * D;
-    T* vt = reinterpret_cast<T*>(sm.stages + st * stage_bytes + p.tile_bytes) + kh * D;
-    const int valid = ctx - lp * kBlockSize;
-    if (inf.w >= 0 || valid < kBlockSize) {
-      if (inf.w >= 0) {
-        // the appended token: the producer copied its k_new / v_new rows into
-        // tile row inf.w; (normalise and rotate k,) store both to the pool
-        uint4 a_row = make_uint4(0, 0, 0, 0);
-        if (lane < 2 * RC) a_row = *reinterpret_cast<const uint4*>((a_which ? vt : kt) + inf.w * rs + a_chunk * 8);
-        if (p.rope) {
-          prep_k<T, D>(p, ctx_raw - 1, lane, a_row);
-          if (lane < RC) *reinterpret_cast<uint4*>(kt + inf.w * rs + a_chunk * 8) = a_row;
-        }
-        if (lane < 2 * RC)
-          *(reinterpret_cast<uint4*>(const_cast<T*>(reinterpret_cast<const T*>(a_which ? p.v_cache : p.k_cache)) +
-                                     (int64_t)inf.z * p.c_sblk + (int64_t)inf.w * p.c_stok + (int64_t)kvh * p.c_sh) +
-            a_chunk) = a_row;
-      }
-      // slots past the context may hold anything: zero their V rows (P is 0
-      // there, but 0 * NaN would not be)
-      for (int i = lane; i < (kBlockSize - valid) * RC; i += 32)
-        *reinterpret_cast<uint4*>(vt + (valid + i / RC) * rs + (i % RC) * 8) = make_uint4(0, 0, 0, 0);
-      // order these generic-proxy writes before the bulk copy that later refills the stage
-      fence_proxy_async_smem();
-      __syncwarp();
-    }
-
-    // ---- scores
-    float sa[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-#pragma unroll
-    for (int ks = 0; ks < KS; ++ks) {
-      uint32_t r0, r1, r2, r3;
-      ldsm_x4(kt + k_row + 16 * ks, r0, r1, r2, r3);
-      mma16816_top<T>(sa[0], qa[ks][0], qa[ks][1], r0, r1);
-      mma16816_top<T>(sa[1], qa[ks][0], qa[ks][1], r2, r3);
-    }
-    float sv[4] = {sa[0][0], sa[0][1], sa[1][0], sa[1][1]};
-    if (valid < kBlockSize) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if ((i >> 1) * 8 + 2 * qc + (i & 1) >= valid) sv[i] = -INFINITY;
-    }
-    float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
-    mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 2));
-    const float m_new = fmaxf(m, mx);
-    if (__any_sync(kFull, m_new != m)) {
-      const float alpha = exp2f((m - m_new) * c);
-      l *= alpha;
-#pragma unroll
-      for (int n = 0; n < NT; ++n) {
-        o[n][0] *= alpha;
-        o[n][1] *= alpha;
-      }
-      m = m_new;
-    }
-    const float mc = m * c;
-    float pv[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      pv[i] = exp2f(fmaf(sv[i], c, -mc));
-      l += pv[i];
-    }
-    const uint32_t pa0 = Elem<T>::pack2(pv[0], pv[1]);
-    const uint32_t pa2 = Elem<T>::pack2(pv[2], pv[3]);
-#pragma unroll
-    for (int np2 = 0; np2 < NT / 2; ++np2) {
-      uint32_t r0, r1, r2, r3;
-      ldsm_x4_trans(vt + v_row + 16 * np2, r0, r1, r2, r3);
-      mma16816_top<T>(o[2 * np2], pa0, pa2, r0, r1);
-      mma16816_top<T>(o[2 * np2 + 1], pa0, pa2, r2, r3);
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.empty_bar[st]);
-    ++run;
-  }
-  if (!__all_sync(kFull, ok) && lane == 0) set_error(p.error, kErrTimeout);
-}
-
 }  // namespace
 
 // ---------------------------------------------------------------- kernels
@@ -1464,48 +1033,6 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
   consume_mma<T, D, BAL>(p, w, sm, warp, blockIdx.y * HG + warp, lane);
 }
 
-// Dynamic (work-sharing) schedule, bf16 / fp16: same CTA layout as the
-// balanced tensor-core kernel; every CTA takes part (no early exit), and the
-// last CTA to finish re-zeroes the owner words for the next launch.
-template <typename T, int D>
-__global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
-    paged_decode_dyn_kernel(const DecodeParams p) {
-  extern __shared__ __align__(128) uint8_t smem_raw[];
-  __shared__ int32_t warp_tot[32];
-  const Smem sm = carve_smem(smem_raw, p);
-  const int HG = p.heads_per_cta, NCW = HG;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = p.num_heads / p.num_kv_heads;
-  if (threadIdx.x == 0) {
-    griddep_launch_dependents();  // the next grid may start on SMs this one frees
-    for (int s = 0; s < p.stages; ++s) {
-      mbar_init(&sm.full_bar[s], 1);
-      mbar_init(&sm.empty_bar[s], NCW);
-    }
-    fence_mbar_init();
-  }
-  const Work w = setup_work<T, D, true>(p, sm, warp_tot);
-  if (warp < NCW) {
-    griddep_wait();  // everything below may touch memory the previous grid wrote
-    write_zero_rows<T, D, true>(p, w, sm.prefix, blockIdx.y * HG * G, (blockIdx.y + 1) * HG * G, threadIdx.x,
-                                NCW * 32);
-    consume_dyn<T, D>(p, sm, warp, blockIdx.y * HG + warp, lane);
-  } else if (warp == NCW) {
-    produce_dyn<T, D>(p, w, sm, blockIdx.y * HG, lane);
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const int ctas = (int)(gridDim.x * gridDim.y);
-    if (atomicAdd(p.dyn_ctas_done, 1) == ctas - 1) {
-      // every CTA has finished its grabs and steals: re-zero for the next launch
-      for (int i = 0; i < ctas; ++i) p.dyn_own[i] = 0ull;
-      *p.dyn_ctas_done = 0;
-      __threadfence();
-    }
-  }
-}
-
 // Split schedule: merge the chunks of every sequence that has more than one.
 // One warp per (sequence, query head).
 template <typename T, int D>
@@ -1569,22 +1096,6 @@ static cudaError_t launch_mma(const DecodeParams& p, const LaunchShape& s, cudaS
 }
 
 template <typename T, int D>
-static cudaError_t launch_dyn(const DecodeParams& p, const LaunchShape& s, cudaStream_t st) {
-  static int granted[64] = {0};
-  return launch_with_smem(paged_decode_dyn_kernel<T, D>, granted, p, s, st);
-}
-
-template <typename T>
-static cudaError_t launch_dyn_t(int head_dim, const DecodeParams& p, const LaunchShape& s, cudaStream_t st) {
-  switch (head_dim) {
-    case 64: return launch_dyn<T, 64>(p, s, st);
-    case 112: return launch_dyn<T, 112>(p, s, st);
-    case 128: return launch_dyn<T, 128>(p, s, st);
-    default: return cudaErrorInvalidValue;
-  }
-}
-
-template <typename T, int D>
 static cudaError_t launch_d(int gw, bool bal, const DecodeParams& p, const LaunchShape& s, cudaStream_t st) {
   if constexpr (sizeof(T) == 2) {
     return bal ? launch_mma<T, D, true>(p, s, st) : launch_mma<T, D, false>(p, s, st);
@@ -1601,15 +1112,6 @@ static cudaError_t launch_t(int head_dim, int gw, bool bal, const DecodeParams& 
     case 64: return launch_d<T, 64>(gw, bal, p, s, st);
     case 112: return launch_d<T, 112>(gw, bal, p, s, st);
     case 128: return launch_d<T, 128>(gw, bal, p, s, st);
-    default: return cudaErrorInvalidValue;
-  }
-}
-
-cudaError_t launch_paged_decode_dyn(int dtype, int head_dim, const DecodeParams& p, const LaunchShape& shape,
-                                    cudaStream_t stream) {
-  switch (dtype) {
-    case UBX_DTYPE_BF16: return launch_dyn_t<__nv_bfloat16>(head_dim, p, shape, stream);
-    case UBX_DTYPE_F16: return launch_dyn_t<__half>(head_dim, p, shape, stream);
     default: return cudaErrorInvalidValue;
   }
 }

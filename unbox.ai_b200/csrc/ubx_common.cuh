@@ -26,7 +26,6 @@ enum : int32_t {
   kErrBadSlot = UBX_DEVERR_BAD_SLOT,          // append slot >= num_blocks * block_size
   kErrBadPosition = UBX_DEVERR_BAD_POSITION,  // rotary position outside the table
   kErrBadWork = UBX_DEVERR_BAD_WORK,          // a cascade work or merge item out of range
-  kErrCapacity = UBX_DEVERR_CAPACITY,         // dynamic schedule: partial-result storage exhausted
 };
 
 __device__ __forceinline__ void set_error(int32_t* err, int32_t bit) {
@@ -107,6 +106,41 @@ __device__ __forceinline__ void bulk_copy_g2s(void* smem_dst, const void* gmem_s
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
       ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(gmem_src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Atomic add with acquire-release semantics at GPU scope: the writes that
+// precede it (in this thread, or in threads ordered before it by a barrier)
+// are visible to whoever observes the new value, and whatever this thread does
+// after it sees the writes that preceded the values it observed. One round trip
+// in place of a fence and an atomic.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int32_t* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+// Relaxed store at GPU scope (no ordering, no round trip to wait for).
+__device__ __forceinline__ void st_relaxed_gpu(int32_t* p, int v) {
+  asm volatile("st.relaxed.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// L2 eviction policy for data read once per launch (KV pages streamed from
+// HBM): the lines it fills are evicted first, so the small data every launch
+// re-reads (block tables, context lengths, queries, partial results) stays in L2.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  return policy;
+}
+
+// bulk_copy_g2s with an L2 cache policy (l2_policy_evict_first) for the source lines.
+__device__ __forceinline__ void bulk_copy_g2s_hint(void* smem_dst, const void* gmem_src, uint32_t bytes,
+                                                   uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+      ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(gmem_src)), "r"(bytes), "r"(smem_u32(bar)),
+        "l"(policy)
       : "memory");
 }
 

@@ -9,7 +9,7 @@ namespace ubx {
 
 constexpr int kBlockSize = 16;          // tokens per page (configs/infer/serve.yaml block_size)
 constexpr int kMaxStages = 8;           // pipeline depth limit
-constexpr int kStageSlotBytes = 2 * 8 + 16;  // per stage: full and empty mbarriers, stage record
+constexpr int kStageSlotBytes = 2 * 8;  // per stage: full and empty mbarriers
 constexpr int kMaxConsumerWarps = 8;    // consumer warps per CTA
 constexpr int kMaxBatchSmem = 2048;     // balanced schedule keeps a (B+1) page prefix in smem
 constexpr int kMaxTileBytes = 36864;    // one K (or V) page tile of a head group
@@ -18,24 +18,19 @@ constexpr int kSmemPerSm = 228 * 1024;        // shared memory of one SM
 constexpr int kSmemReservedPerCta = 1024 + 512;  // per-CTA reservation + static smem
 constexpr int kMaxCtasPerSm = 4;              // CTAs of one balanced launch per SM (small head groups)
 constexpr int kCascadeFollowerSmem = 4096;     // per SM, left by the cascade's suffix pass to the merge CTAs
-
-// Dynamic (work-sharing) schedule.
-constexpr int kDynOwnerPages = 16;    // most pages a CTA takes from its own range per grab
-constexpr int kDynMaxStealPages = 8;  // most pages one steal takes
-constexpr int kDynMaxStealRuns = 6;   // steals per CTA (bounds its partial results)
-constexpr int kDynSlotsPerCta = 16;   // partial-result slots per CTA (3 + 2 per steal suffice)
-constexpr int kDynMaxParts = 256;     // partial results one (sequence, KV head) may collect
-constexpr int kMaxCtasTotal = 1024;   // CTAs of one launch (owner words in the workspace)
+#ifndef UBX_TAIL_TRIM_PAGES
+#define UBX_TAIL_TRIM_PAGES 4
+#endif
+// Balanced schedule under programmatic overlap, one CTA per SM: pages fewer
+// for the last CTA, which starts only once the previous grid's last CTA has
+// left its SM (the others start as their SMs free and prefetch meanwhile).
+constexpr int kTailTrimPages = UBX_TAIL_TRIM_PAGES;
 
 // Workspace layout prefix: [error word + reserved | merge counters | partials].
 constexpr size_t kWsHeaderBytes = 256;                      // error word at offset 0
 constexpr size_t kWsCounterEntries = 65536;                 // balanced-schedule merge counters
 constexpr size_t kWsCounterBytes = kWsCounterEntries * 4;   // must be zero before a call
-// dynamic schedule: per-(sequence, KV head) partial counts, per-CTA owner words, CTAs-done count
-constexpr size_t kWsDynNpartsOff = kWsHeaderBytes + kWsCounterBytes;
-constexpr size_t kWsDynOwnOff = kWsDynNpartsOff + kWsCounterBytes;
-constexpr size_t kWsDynDoneOff = kWsDynOwnOff + 1024 * 8;  // kMaxCtasTotal owner words
-constexpr size_t kWsZeroBytes = kWsDynDoneOff + 256;       // the prefix ubx_workspace_init zeroes
+constexpr size_t kWsZeroBytes = kWsHeaderBytes + kWsCounterBytes;  // the prefix ubx_workspace_init zeroes
 
 // Shared-memory row pitch of a page tile: one token row of the CTA's heads
 // (heads * head_dim elements, contiguous in the KVPool layout) plus 16 bytes
@@ -66,6 +61,7 @@ struct DecodeParams {
   int stages;            // pipeline depth
   int split_pages;       // split schedule: pages per chunk
   int max_chunks;        // split schedule: chunk slots per sequence
+  int tail_trim;         // balanced schedule: pages fewer for the last CTA's range (0: equal shares)
   float* part_o;         // [slots][num_heads][D] unnormalised partial outputs
   float2* part_ml;       // [slots][num_heads] (running max in log2 units, denominator)
   int32_t* counters;     // [batch][num_kv_heads * warps_per_kv] merge counters (balanced)
@@ -91,13 +87,6 @@ struct DecodeParams {
   // optional (batch, num_heads) output: log2 of the softmax denominator in the
   // exp2 domain, m * scale * log2(e) + log2(sum), -inf for an empty context
   float* lse;
-  // dynamic schedule (workspace regions; zero between launches where noted)
-  unsigned long long* dyn_own;  // [grid.y][grid.x]: pages the owner took | pages thieves took << 32 (zero)
-  int32_t* dyn_ctas_done;       // CTAs finished; the last re-zeroes dyn_own and this (zero)
-  int32_t* dyn_nparts;          // [batch][num_kv_heads] partials listed (zero, re-armed by the merger)
-  int32_t* dyn_part_list;       // [batch][num_kv_heads][kDynMaxParts] head-row index of each partial
-  float* dyn_part_o;            // [CTAs * kDynSlotsPerCta * HG * G][D] partial rows
-  float2* dyn_part_ml;          // [same] (max in log2 units, sum)
 };
 
 // Standalone pre-attention step (qk_norm_rope.cu); strides in elements.
@@ -153,10 +142,6 @@ struct LaunchShape {
 // Shared-memory bytes the decode kernel needs (stage ring + softmax buffers +
 // barriers + optional page prefix).
 int decode_smem_bytes(int tile_bytes, int pbuf_bytes, int stages, int prefix_entries);
-
-// Dynamic schedule launch (bf16/f16, tensor-core consumers).
-cudaError_t launch_paged_decode_dyn(int dtype, int head_dim, const DecodeParams& p, const LaunchShape& shape,
-                                    cudaStream_t stream);
 
 cudaError_t launch_paged_decode(int dtype, int head_dim, int gw, bool balanced, const DecodeParams& p,
                                 const LaunchShape& shape, cudaStream_t stream);

@@ -14,13 +14,12 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libunbox_b200.so")
 
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
-SCHEDULE_AUTO, SCHEDULE_BALANCED, SCHEDULE_SPLIT, SCHEDULE_DYNAMIC = 0, 1, 2, 3
+SCHEDULE_AUTO, SCHEDULE_BALANCED, SCHEDULE_SPLIT = 0, 1, 2
 FLAG_OVERLAP_PREVIOUS = 1
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_WORKSPACE, ERR_CUDA = 0, 1, 2, 3, 4
 DEVERR = {1: "page id outside the pool", 2: "context longer than its block-table row",
           4: "negative context length", 8: "pipeline wait timed out", 16: "append slot outside the pool",
-          32: "rotary position outside the rope table", 64: "cascade work or merge item out of range",
-          128: "dynamic schedule ran out of partial-result storage"}
+          32: "rotary position outside the rope table", 64: "cascade work or merge item out of range"}
 
 # exported symbol -> (restype, argtypes); the test suite checks this list against the header
 _i32, _i64, _vp, _f32, _sz = ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_float, ctypes.c_size_t

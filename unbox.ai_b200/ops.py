@@ -27,8 +27,7 @@ import torch
 from . import library as _L
 
 _DTYPES = {torch.float32: _L.DTYPE_F32, torch.bfloat16: _L.DTYPE_BF16, torch.float16: _L.DTYPE_F16}
-_SCHEDULES = {"auto": _L.SCHEDULE_AUTO, "balanced": _L.SCHEDULE_BALANCED, "split": _L.SCHEDULE_SPLIT,
-              "dynamic": _L.SCHEDULE_DYNAMIC}
+_SCHEDULES = {"auto": _L.SCHEDULE_AUTO, "balanced": _L.SCHEDULE_BALANCED, "split": _L.SCHEDULE_SPLIT}
 
 
 _raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
@@ -71,8 +70,7 @@ class DecodeWorkspace:
 
     def ensure(self, batch: int, num_heads: int, head_dim: int, max_blocks: int, split_pages: int = 0,
                num_kv_heads: int = 0, dtype: Optional[torch.dtype] = None):
-        """Grow to what a call with these sizes needs (``num_kv_heads`` and a 16-bit
-        ``dtype`` add room for the dynamic schedule)."""
+        """Grow to what a call with these sizes needs."""
         key = (batch, num_heads, head_dim, max_blocks, split_pages, num_kv_heads, dtype)
         if key in self._sized:  # the decode loop asks the same sizes every layer: answer from the cache
             return self.buf
