@@ -744,22 +744,23 @@ def box_scale_record(args, pkg, rank: int, world: int, device, reduce_max, barri
             g.replay()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
-        e0.record()
-        for _ in range(args.steps):
-            g.replay()
-        e1.record()
-        torch.cuda.synchronize()
+        with ClockSampler(device.index) as clocks:
+            e0.record()
+            for _ in range(args.steps):
+                g.replay()
+            e1.record()
+            torch.cuda.synchronize()
         del g
         pkg.check_device_errors(device)
         step_bytes = L * sum(wl.algorithmic_bytes(lay, 2)["layer_call"] for _, lay in parts)
         launches = L * len(parts)
         del devs, outs
         torch.cuda.empty_cache()
-        return e0.elapsed_time(e1), step_bytes, launches
+        return e0.elapsed_time(e1), step_bytes, launches, clocks.summary()
 
     parts, _, glay = build_parts(pkg, "box_scale", rank, world)
     barrier()
-    ms, step_bytes, launches = timed(parts, 5000 + 31 * rank)
+    ms, step_bytes, launches, clk = timed(parts, 5000 + 31 * rank)
     barrier()
     ms_max = reduce_max(ms)
     bytes_all = float(step_bytes)
@@ -773,7 +774,7 @@ def box_scale_record(args, pkg, rank: int, world: int, device, reduce_max, barri
     rec = {"workload": "box_scale", "requests": int(glay.batch), "sigma": 0.6, "layers": L,
            "value": round(value, 2), "unit": "GB/s", "ms_per_step": round(ms_max / args.steps, 4),
            "frac_per_gpu": round(value / world / peak, 4), "gpu_launches_per_rank_step": launches,
-           "timing": "graph replay, device events, max over ranks",
+           "timing": "graph replay, device events, max over ranks", "clocks": clk,
            "plan": "plan_shards: LPT on KV bytes, KV heads of contexts > 2048 split across GPUs"}
     if world == 1:
         rec.update(value_1gpu=rec["value"], efficiency=1.0)
@@ -781,7 +782,7 @@ def box_scale_record(args, pkg, rank: int, world: int, device, reduce_max, barri
         v1 = None
         if rank == 0:
             p1, _, _ = build_parts(pkg, "box_scale", 0, 1)
-            ms1, b1, _ = timed(p1, 7000)
+            ms1, b1, _, _ = timed(p1, 7000)
             v1 = b1 * args.steps / (ms1 / 1e3) / 1e9
         barrier()
         if rank == 0:

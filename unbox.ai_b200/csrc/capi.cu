@@ -38,6 +38,35 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 constexpr size_t kHeaderBytes = kWsHeaderBytes;        // error word + reserved
 constexpr size_t kCounterEntries = kWsCounterEntries;  // merge counters, re-armed by the kernel
 constexpr int kDefaultSplitPages = 32;                 // 512-token split-KV chunks
+
+// UBX_SCHEDULE_AUTO for a few long sequences: the balanced schedule cuts each
+// of them over many CTAs, and the last part's warp merges every part (one
+// sequence of 32k tokens: 148 parts, 92 us on a B200), while split-KV chunks of
+// about (batch * max_blocks / SMs) pages, merged by the parallel combine
+// kernel, take 31 us. Measured crossover (B200, GQA 16/8, head_dim 112, bf16):
+// split wins for batch <= 4 with contexts of 8k-32k tokens (27-88 us against
+// 42-96 us), ties at batch 6 and loses from batch 8 (157 against 168-176 us at
+// 32k tokens) and on the 760M batch (54 against 74-88 us).
+constexpr int kAutoSplitMaxBatch = 4;
+constexpr int kAutoSplitMinBlocks = 64;
+
+bool auto_prefers_split(int batch, int max_blocks) {
+  return batch <= kAutoSplitMaxBatch && max_blocks >= kAutoSplitMinBlocks;
+}
+
+// Pages per chunk for the split schedule: the caller's choice, else about one
+// wave of chunks (batch * max_blocks / SMs pages, a power of two in [16, 64])
+// when AUTO picks split, else kDefaultSplitPages.
+int split_pages_for(int split_pages, int schedule, int batch, int max_blocks, int num_sms) {
+  if (split_pages > 0) return split_pages;
+  if (schedule == UBX_SCHEDULE_AUTO && auto_prefers_split(batch, max_blocks)) {
+    const int64_t want = ((int64_t)batch * max_blocks + num_sms - 1) / num_sms;
+    int sp = 16;
+    while (sp < want && sp < 64) sp *= 2;
+    return sp;
+  }
+  return kDefaultSplitPages;
+}
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct WsLayout {
@@ -104,8 +133,9 @@ int make_plan(int batch, int num_heads, int num_kv_heads, int head_dim, int dtyp
   const bool can_balance = batch <= kMaxBatchSmem && (int64_t)batch * num_kv_heads * pl->wpk <= (int64_t)kCounterEntries;
   if (schedule == UBX_SCHEDULE_BALANCED && !can_balance)
     return fail(UBX_ERR_UNSUPPORTED, "the balanced schedule needs batch <= %d (got %d)", kMaxBatchSmem, batch);
-  pl->balanced = schedule == UBX_SCHEDULE_BALANCED || (schedule == UBX_SCHEDULE_AUTO && can_balance);
-  pl->split_pages = split_pages > 0 ? split_pages : kDefaultSplitPages;
+  pl->balanced = schedule == UBX_SCHEDULE_BALANCED ||
+                 (schedule == UBX_SCHEDULE_AUTO && can_balance && !auto_prefers_split(batch, max_blocks));
+  pl->split_pages = split_pages_for(split_pages, schedule, batch, max_blocks, num_sms);
   pl->max_chunks = (max_blocks + pl->split_pages - 1) / pl->split_pages;
   pl->tile = kBlockSize * pl->pitch;
   pl->pbuf = mma ? 0 : ((pl->hg * pl->wpk * pl->gw * kBlockSize * 4 + 15) & ~15);
@@ -338,7 +368,9 @@ int ubx_paged_decode_workspace_size(int batch, int num_heads, int num_kv_heads, 
   int sms = 0;
   int st = num_sms_current_device(&sms);
   if (st != UBX_OK) return st;
-  const int sp = split_pages > 0 ? split_pages : kDefaultSplitPages;
+  // room for the chunk size AUTO would pick too
+  const int sp = std::min(split_pages_for(split_pages, UBX_SCHEDULE_AUTO, batch, max_blocks_per_seq, sms),
+                          split_pages > 0 ? split_pages : kDefaultSplitPages);
   const int64_t chunks = (max_blocks_per_seq + sp - 1) / sp;
   const int64_t slots = std::max<int64_t>(2 * (int64_t)sms * kMaxCtasPerSm, (int64_t)batch * chunks);
   *bytes = ws_layout(slots, num_heads, head_dim).total;

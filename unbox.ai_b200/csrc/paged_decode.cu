@@ -114,48 +114,6 @@ __device__ __forceinline__ void write_zero_row(const DecodeParams& p, int b, int
   }
 }
 
-// Merge `nparts` partial triples of one (sequence, query head) and write the
-// normalised output row. slot_of(i) gives the workspace slot of part i.
-template <typename T, int D, typename SlotFn>
-__device__ __forceinline__ void merge_parts(const DecodeParams& p, int b, int h, int nparts, SlotFn slot_of,
-                                            int lane) {
-  constexpr int EPC = Elem<T>::kPerChunk;
-  constexpr int DCH = D / EPC;
-  float M = -INFINITY;
-  for (int i = lane; i < nparts; i += 32) M = fmaxf(M, __ldcg(&p.part_ml[(int64_t)slot_of(i) * p.num_heads + h]).x);
-  M = warp_max(M);
-  float L = 0.f;
-  for (int i = lane; i < nparts; i += 32) {
-    const float2 ml = __ldcg(&p.part_ml[(int64_t)slot_of(i) * p.num_heads + h]);
-    L += ml.y * exp2f(ml.x - M);
-  }
-  L = warp_sum(L);
-  if (lane < DCH) {
-    float o[EPC];
-#pragma unroll
-    for (int e = 0; e < EPC; ++e) o[e] = 0.f;
-    for (int i = 0; i < nparts; ++i) {
-      const int64_t slot = slot_of(i);
-      const float w = exp2f(__ldcg(&p.part_ml[slot * p.num_heads + h]).x - M);
-      const float4* src = reinterpret_cast<const float4*>(p.part_o + (slot * p.num_heads + h) * D + lane * EPC);
-#pragma unroll
-      for (int e4 = 0; e4 < EPC / 4; ++e4) {
-        const float4 v = __ldcg(src + e4);
-        o[4 * e4 + 0] = fmaf(w, v.x, o[4 * e4 + 0]);
-        o[4 * e4 + 1] = fmaf(w, v.y, o[4 * e4 + 1]);
-        o[4 * e4 + 2] = fmaf(w, v.z, o[4 * e4 + 2]);
-        o[4 * e4 + 3] = fmaf(w, v.w, o[4 * e4 + 3]);
-      }
-    }
-    const float inv = 1.f / L;
-#pragma unroll
-    for (int e = 0; e < EPC; ++e) o[e] *= inv;
-    T* dst = reinterpret_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + lane * EPC;
-    *reinterpret_cast<uint4*>(dst) = Elem<T>::pack(o);
-    if (p.lse && lane == 0) p.lse[(int64_t)b * p.num_heads + h] = M + log2f(L);
-  }
-}
-
 // Merge the `nparts` partial (acc, max, sum) triples of heads head0 .. head0+nh-1
 // of sequence b into normalised output rows. Lanes are (head, 16-byte output
 // chunk) pairs, and the loads of several parts are in flight together, so a
@@ -175,11 +133,7 @@ __device__ void merge_rows(const DecodeParams& p, int b, int head0, int nh, int 
     float M = -INFINITY, L = 0.f, o[EPC];
 #pragma unroll
     for (int e = 0; e < EPC; ++e) o[e] = 0.f;
-#pragma unroll 4
-    for (int i = 0; i < nparts; ++i) {
-      const int64_t slot = slot_of(i);
-      const float2 ml = __ldcg(&p.part_ml[slot * H + head]);
-      const float4* src = reinterpret_cast<const float4*>(p.part_o + (slot * H + head) * D + c * EPC);
+    auto fold = [&](const float2 ml, const float4* src) {
       float4 v[EPC / 4];
 #pragma unroll
       for (int e4 = 0; e4 < EPC / 4; ++e4) v[e4] = __ldcg(src + e4);
@@ -199,6 +153,12 @@ __device__ void merge_rows(const DecodeParams& p, int b, int head0, int nh, int 
         o[4 * e4 + 2] = fmaf(wgt, v[e4].z, o[4 * e4 + 2]);
         o[4 * e4 + 3] = fmaf(wgt, v[e4].w, o[4 * e4 + 3]);
       }
+    };
+#pragma unroll 8
+    for (int i = 0; i < nparts; ++i) {
+      const int64_t slot = slot_of(i);
+      fold(__ldcg(&p.part_ml[slot * H + head]),
+           reinterpret_cast<const float4*>(p.part_o + (slot * H + head) * D + c * EPC));
     }
     const float inv = 1.f / L;
 #pragma unroll
@@ -1034,18 +994,85 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
 }
 
 // Split schedule: merge the chunks of every sequence that has more than one.
-// One warp per (sequence, query head).
+// One CTA per (sequence, query head). Thread (chunk c, group j) folds parts
+// j, j + PG, j + 2 PG, ... of 16-byte output chunk c with a running max, so
+// the loads of all parts are in flight at once across the CTA; the PG groups'
+// (max, sum, accumulator) are then combined through shared memory with
+// log-sum-exp weights.
+constexpr int kCombineThreads = 256;
+
 template <typename T, int D>
-__global__ void __launch_bounds__(128) lse_combine_kernel(const DecodeParams p) {
-  const int gw = blockIdx.x * 4 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (gw >= p.batch * p.num_heads) return;
-  const int b = gw / p.num_heads, h = gw % p.num_heads;
+__global__ void __launch_bounds__(kCombineThreads) lse_combine_kernel(const DecodeParams p) {
+  constexpr int EPC = Elem<T>::kPerChunk;
+  constexpr int DCH = D / EPC;                    // output chunks of one row
+  constexpr int PG = kCombineThreads / DCH;       // part groups
+  __shared__ float s_m[PG][DCH], s_l[PG][DCH];
+  __shared__ float4 s_o[PG][DCH][EPC / 4];
+  const int b = blockIdx.x / p.num_heads, h = blockIdx.x % p.num_heads;
   const int n_b = pages_of(p, b, false);
   const int nparts = (n_b + p.split_pages - 1) / p.split_pages;
   if (nparts <= 1) return;  // the decode kernel wrote the row directly
-  auto slot_of = [&](int i) -> int64_t { return (int64_t)b * p.max_chunks + i; };
-  merge_parts<T, D>(p, b, h, nparts, slot_of, lane);
+  const int c = threadIdx.x % DCH, j = threadIdx.x / DCH;
+  if (j < PG) {
+    float M = -INFINITY, L = 0.f, o[EPC];
+#pragma unroll
+    for (int e = 0; e < EPC; ++e) o[e] = 0.f;
+#pragma unroll 4
+    for (int i = j; i < nparts; i += PG) {
+      const int64_t slot = (int64_t)b * p.max_chunks + i;
+      const float2 ml = __ldcg(&p.part_ml[slot * p.num_heads + h]);
+      const float4* src = reinterpret_cast<const float4*>(p.part_o + (slot * p.num_heads + h) * D + c * EPC);
+      float4 v[EPC / 4];
+#pragma unroll
+      for (int e4 = 0; e4 < EPC / 4; ++e4) v[e4] = __ldcg(src + e4);
+      if (ml.x > M) {
+        const float sc = exp2f(M - ml.x);  // M = -inf at first: sc = 0
+        L *= sc;
+#pragma unroll
+        for (int e = 0; e < EPC; ++e) o[e] *= sc;
+        M = ml.x;
+      }
+      const float wgt = exp2f(ml.x - M);
+      L = fmaf(ml.y, wgt, L);
+#pragma unroll
+      for (int e4 = 0; e4 < EPC / 4; ++e4) {
+        o[4 * e4 + 0] = fmaf(wgt, v[e4].x, o[4 * e4 + 0]);
+        o[4 * e4 + 1] = fmaf(wgt, v[e4].y, o[4 * e4 + 1]);
+        o[4 * e4 + 2] = fmaf(wgt, v[e4].z, o[4 * e4 + 2]);
+        o[4 * e4 + 3] = fmaf(wgt, v[e4].w, o[4 * e4 + 3]);
+      }
+    }
+    s_m[j][c] = M;
+    s_l[j][c] = L;
+#pragma unroll
+    for (int e4 = 0; e4 < EPC / 4; ++e4)
+      s_o[j][c][e4] = make_float4(o[4 * e4], o[4 * e4 + 1], o[4 * e4 + 2], o[4 * e4 + 3]);
+  }
+  __syncthreads();
+  if (threadIdx.x >= DCH) return;
+  float M = -INFINITY;
+  for (int g = 0; g < PG; ++g) M = fmaxf(M, s_m[g][c]);  // groups without parts hold -inf, 0
+  float L = 0.f, o[EPC];
+#pragma unroll
+  for (int e = 0; e < EPC; ++e) o[e] = 0.f;
+  for (int g = 0; g < PG; ++g) {
+    const float wgt = s_m[g][c] == -INFINITY ? 0.f : exp2f(s_m[g][c] - M);
+    L = fmaf(s_l[g][c], wgt, L);
+#pragma unroll
+    for (int e4 = 0; e4 < EPC / 4; ++e4) {
+      const float4 v = s_o[g][c][e4];
+      o[4 * e4 + 0] = fmaf(wgt, v.x, o[4 * e4 + 0]);
+      o[4 * e4 + 1] = fmaf(wgt, v.y, o[4 * e4 + 1]);
+      o[4 * e4 + 2] = fmaf(wgt, v.z, o[4 * e4 + 2]);
+      o[4 * e4 + 3] = fmaf(wgt, v.w, o[4 * e4 + 3]);
+    }
+  }
+  const float inv = 1.f / L;
+#pragma unroll
+  for (int e = 0; e < EPC; ++e) o[e] *= inv;
+  T* dst = reinterpret_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + c * EPC;
+  *reinterpret_cast<uint4*>(dst) = Elem<T>::pack(o);
+  if (p.lse && c == 0) p.lse[(int64_t)b * p.num_heads + h] = M + log2f(L);
 }
 
 // ---------------------------------------------------------------- host side
@@ -1128,8 +1155,7 @@ cudaError_t launch_paged_decode(int dtype, int head_dim, int gw, bool balanced, 
 
 template <typename T>
 static cudaError_t combine_t(int head_dim, const DecodeParams& p, cudaStream_t st) {
-  const int warps = p.batch * p.num_heads;
-  const dim3 grid((warps + 3) / 4), block(128);
+  const dim3 grid((unsigned)p.batch * (unsigned)p.num_heads), block(kCombineThreads);
   switch (head_dim) {
     case 64: lse_combine_kernel<T, 64><<<grid, block, 0, st>>>(p); break;
     case 112: lse_combine_kernel<T, 112><<<grid, block, 0, st>>>(p); break;
