@@ -121,9 +121,9 @@ int ubx_slot_mapping(const int32_t* block_table, int64_t bt_s_row, const int32_t
 /*
  * Bytes of device workspace the attention entry points need for these sizes on
  * the current device (partial results of split sequences, merge counters, the
- * error word; sized for up to 4 CTAs per SM). The workspace must be zeroed once
- * with ubx_workspace_init before its first use; the kernels leave it ready for
- * the next call.
+ * error word; sized for up to 4 CTAs per SM). The workspace must be 16-byte
+ * aligned and zeroed once with ubx_workspace_init before its first use; the
+ * kernels leave it ready for the next call.
  */
 int ubx_paged_decode_workspace_size(int batch, int num_heads, int num_kv_heads, int head_dim, int max_blocks_per_seq,
                                     int split_pages, int dtype, size_t* bytes);
@@ -282,7 +282,7 @@ int ubx_paged_decode_attention_lse(const void* k_new, const void* v_new, int64_t
  *                offset, page count <= 8, chunk index < max_chunks, 0); member
  *                count * (num_heads / num_kv_heads) <= 128
  *   merge_items: int32 [num_merge_items][2] = (sequence, number of its prefix chunks)
- *   cascade_ws:  ubx_cascade_workspace_size bytes (no initialisation needed)
+ *   cascade_ws:  ubx_cascade_workspace_size bytes, 16-byte aligned (no initialisation needed)
  *   flags:       UBX_FLAG_OVERLAP_PREVIOUS = programmatic dependent launch: the
  *                kernel may start while the previous kernel on the stream drains.
  *                The prefix pass then loads its shared pages before waiting for

@@ -86,6 +86,12 @@ def test_validation_rejects_before_any_launch(pkg):
     st = lib.ubx_paged_decode_attention(None, 0, 0, None, None, 0, 0, 0, None, 0, None, None, 0, 0,
                                         0, 16, 8, 112, 16, 1, 1, 1.0, 1, 0, 0, None, 0, None)
     assert st == 0
+    # a workspace off a 16-byte boundary (the kernels read it 16 bytes at a time);
+    # the other pointers are never dereferenced on the host
+    st = lib.ubx_paged_decode_attention(0x10000, 16 * 112, 112, 0x20000, 0x30000, 16 * 8 * 112, 8 * 112, 112,
+                                        0x40000, 1, 0x50000, 0x60000, 16 * 112, 112,
+                                        1, 16, 8, 112, 16, 1, 1, 1.0, 1, 0, 0, 0x70008, 1 << 30, None)
+    assert st == pkg.library.ERR_WORKSPACE and b"16-byte aligned" in lib.ubx_last_error()
     st = lib.ubx_kv_append(None, None, 0, 0, None, None, 0, 0, 0, None, 0, 8, 112, 16, 4, 1, None, None)
     assert st == 0
 

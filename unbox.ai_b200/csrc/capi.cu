@@ -467,6 +467,7 @@ int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache
   if (!(scale > 0.f) && !(scale < 0.f)) return fail(UBX_ERR_INVALID_ARGUMENT, "scale must be finite and non-zero");
   if (flags & ~UBX_FLAG_OVERLAP_PREVIOUS) return fail(UBX_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
   if (!workspace) return fail(UBX_ERR_WORKSPACE, "workspace is required");
+  if (!aligned16(workspace)) return fail(UBX_ERR_WORKSPACE, "workspace must be 16-byte aligned");
 
   int sms = 0;
   st = num_sms_current_device(&sms);
@@ -661,6 +662,7 @@ int ubx_cascade_prefix_attention(const void* q, int64_t q_s_b, int64_t q_s_h, co
   ubx_cascade_workspace_size(batch, num_heads, head_dim, max_chunks, &need);
   if (cascade_ws_bytes < need)
     return fail(UBX_ERR_WORKSPACE, "cascade workspace of %zu bytes, this call needs %zu", cascade_ws_bytes, need);
+  if (!aligned16(cascade_ws)) return fail(UBX_ERR_WORKSPACE, "cascade workspace must be 16-byte aligned");
   if (!(scale > 0.f) && !(scale < 0.f)) return fail(UBX_ERR_INVALID_ARGUMENT, "scale must be finite and non-zero");
   CascadeParams p;
   p.q = q;
@@ -711,6 +713,7 @@ int ubx_cascade_merge(void* out, int64_t o_s_b, int64_t o_s_h, const float* lse,
   ubx_cascade_workspace_size(batch, num_heads, head_dim, max_chunks, &need);
   if (cascade_ws_bytes < need)
     return fail(UBX_ERR_WORKSPACE, "cascade workspace of %zu bytes, this call needs %zu", cascade_ws_bytes, need);
+  if (!aligned16(cascade_ws)) return fail(UBX_ERR_WORKSPACE, "cascade workspace must be 16-byte aligned");
   CascadeMergeParams p;
   p.out = out;
   p.o_sb = o_s_b;

@@ -533,11 +533,10 @@ __device__ void publish_and_merge(const DecodeParams& p, const Work& w, const Se
   int last = 0;
   if (lane == 0) last = atom_add_acq_rel_gpu(&p.counters[ctr_index], 1) == nparts - 1;
   if (__shfl_sync(kFull, last, 0)) {
-    const int sb0 = s.s0;
-    auto slot_of = [&](int i) -> int64_t {
-      const int wi = w_first + i;
-      return 2 * (int64_t)wi + (range_begin(w, wi) < sb0 ? 1 : 0);
-    };
+    // part 0's CTA may have begun its range before the sequence (its slot 1);
+    // the later parts are the first segments of their CTAs (slot 0)
+    const int64_t slot_first = 2 * (int64_t)w_first + (range_begin(w, w_first) < s.s0 ? 1 : 0);
+    auto slot_of = [&](int i) -> int64_t { return i == 0 ? slot_first : 2 * (int64_t)(w_first + i); };
     merge_rows<T, D>(p, s.b, head0, nh, nparts, slot_of, lane);
     // re-armed for the next launch: every part has counted, and the next grid
     // reads the counter only after this one has completed
