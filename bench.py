@@ -81,8 +81,11 @@ def parse():
                     help="layer-call = q/k RMSNorm + rotary embedding + KV append + attention in one launch "
                          "(the attention block between the QKV projection and o_proj)")
     ap.add_argument("--cascade", action="store_true",
-                    help="read pages shared by several requests (radix prefix) once per layer-call: suffix pass, "
-                         "shared-prefix pass and merge (plan built on the host once per step)")
+                    help="read pages shared by several requests (radix prefix) once per layer-call: suffix and "
+                         "shared-prefix passes in one launch, then a merge (plan built on the host once per step)")
+    ap.add_argument("--prefix-ctas", type=int, default=None,
+                    help="--cascade: CTAs of the one launch given to the shared-prefix pass (default: the plan's "
+                         "cost model; 0: the two passes as two launches)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-box-scale", dest="box_scale", action="store_false",
@@ -920,7 +923,9 @@ def main():
     kw = dict(schedule=args.schedule, split_pages=args.split_pages)
     launches_per_call = (2 if args.separate else 1) + (1 if args.schedule == "split" else 0)
     if args.cascade and any(d["plan"].num_work for d in devs):
-        launches_per_call += 2
+        one = pkg.cascade.one_launch_possible(glay.num_kv_heads, glay.head_dim) and args.schedule != "split" and \
+            (args.prefix_ctas is None or args.prefix_ctas > 0)
+        launches_per_call += 1 if one else 2
     calls_per_step = L * len(parts)
 
     def layer_call(d, l, q, k_new, v_new, block_table, context_lens, out, slots=None, timer=None):
@@ -933,7 +938,8 @@ def main():
             pkg.paged_attention(q, d["k_caches"][l], d["v_caches"][l], block_table, context_lens, out=out, **kw)
         elif args.cascade:
             pkg.paged_attention_cascade(q, d["k_caches"][l], d["v_caches"][l], d["plan"], out=out, k_new=k_new,
-                                        v_new=v_new, overlap_previous=args.overlap, schedule=args.schedule)
+                                        v_new=v_new, overlap_previous=args.overlap, schedule=args.schedule,
+                                        prefix_ctas=args.prefix_ctas)
         elif args.prep:
             pkg.paged_decode_prep_attention(q, k_new, v_new, d["q_w"][l], d["k_w"][l], rope, d["k_caches"][l],
                                             d["v_caches"][l], block_table, context_lens, 1e-6, out=out,
@@ -1175,8 +1181,8 @@ def main():
                         "frac": round(achieved / peak, 4), "traffic": profiled_traffic(args.workload),
                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                         else "fallback 6650 GB/s",
-                        "kernel": ("cascade layer-call: paged_decode_mma_kernel (suffix, KV append fused) + "
-                                   "cascade_prefix_kernel + cascade_merge_kernel" if args.cascade else
+                        "kernel": ("cascade layer-call: cascade_fused_kernel (suffix pages, KV append fused, and "
+                                   "shared-prefix tiles in one launch) + cascade_merge_kernel" if args.cascade else
                                    "paged_decode_mma_kernel" + ("" if args.separate else
                                                                 " (q/k RMSNorm, rotary, KV append fused)" if args.prep
                                                                 else " (KV append fused)")),

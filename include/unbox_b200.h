@@ -306,6 +306,28 @@ int ubx_cascade_merge(void* out, int64_t o_s_b, int64_t o_s_h, const float* lse,
                       void* stream);
 
 /*
+ * The whole cascade step in one call: steps 1-3 above with the arguments they
+ * take (suffix_block_table / suffix_context_lens are step 1's block_table /
+ * context_lens, schedule is step 1's; the device error word is the
+ * workspace's). With prefix_ctas > 0, and when the suffix pass runs the
+ * balanced schedule with one CTA per SM, steps 1 and 2 share one launch: its
+ * first prefix_ctas CTAs (at least 1, at most the grid less one) run the work
+ * items on the tensor cores while the others stream the suffix pages, on
+ * disjoint SMs. Otherwise (prefix_ctas = 0, the split schedule, several CTAs
+ * per SM) they are two launches. Step 3 follows.
+ */
+int ubx_cascade_attention(const void* k_new, const void* v_new, int64_t new_s_tok, int64_t new_s_head,
+                          const void* q, int64_t q_s_b, int64_t q_s_h, void* k_cache, void* v_cache,
+                          int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head, const int32_t* suffix_block_table,
+                          int64_t bt_s_row, const int32_t* suffix_context_lens, void* out, int64_t o_s_b,
+                          int64_t o_s_h, int batch, int num_heads, int num_kv_heads, int head_dim, int block_size,
+                          int64_t num_blocks, int max_blocks_per_seq, float scale, int dtype, int schedule,
+                          const int32_t* page_list, const int32_t* member_list, const int32_t* work_items,
+                          int num_work_items, const int32_t* merge_items, int num_merge_items, int max_chunks,
+                          int prefix_ctas, int flags, float* lse_out, void* workspace, size_t workspace_bytes,
+                          void* cascade_ws, size_t cascade_ws_bytes, void* stream);
+
+/*
  * KV hand-off between a prefill worker and a decode worker.
  * Replaces: KVPool.serialize_blocks / deserialize_blocks
  * (unbox_platform/infer/kvcache.py:268-277), used at worker.py:175-183 (prefill

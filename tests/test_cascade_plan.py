@@ -158,3 +158,29 @@ def test_merge_of_plan_pieces_equals_full_attention(heads, oracle):
         o_s, l_s = attend(q[b], kc, vc, sbt[b, :n], int(sctx[b]), scale)
         o_p, l_p = attend(q[b], kc, vc, shared, len(shared) * 16, scale)
         np.testing.assert_allclose(merge([(o_s, l_s), (o_p, l_p)]), full[b], atol=1e-9)
+
+
+@pytest.mark.parametrize("max_parts,run_pages", [(4, 24), (2, 48), (12, 8), (1, 64)])
+def test_long_prefix_in_runs_of_chunks(max_parts, run_pages):
+    """A 96-page shared prefix is cut into at most max_parts runs of whole 8-page
+    chunks, each at most 64 pages (one work item per run and member block,
+    folded on the device a chunk at a time); every (member, run) is covered once
+    and the runs tile the shared pages in order."""
+    wl = PKG.workloads
+    lay = wl.layout_radix_prefix(11, batch=40, prefix_pages=96, suffix_lo=1, suffix_hi=60)
+    p = PKG.cascade.plan_cascade(lay.block_table, lay.context_lens, 16, 8, max_parts=max_parts, device="cpu")
+    n_runs = -(-96 // run_pages)
+    assert p.max_chunks == n_runs
+    work = p.work.numpy()
+    assert (work[:, 3] <= min(run_pages, PKG.cascade.MAX_ITEM_PAGES)).all()
+    starts = sorted({(int(w[4]), int(w[2]), int(w[3])) for w in work})
+    assert [s[0] for s in starts] == list(range(n_runs))
+    assert starts[0][1] == 0 and all(a[1] + a[2] == b[1] for a, b in zip(starts, starts[1:]))
+    assert starts[-1][1] + starts[-1][2] == 96
+    cover = {}
+    mlist = p.member_list.numpy()
+    for m_off, nm, _, _, part, _ in work:
+        for b in mlist[m_off:m_off + nm]:
+            cover[(int(b), int(part))] = cover.get((int(b), int(part)), 0) + 1
+    assert set(cover.values()) == {1} and len(cover) == 40 * n_runs
+    assert (p.merge_items.numpy()[:, 1] == n_runs).all()

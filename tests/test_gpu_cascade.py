@@ -64,6 +64,30 @@ def test_cascade_random_vs_oracle(dtype, heads, schedule, pkg, oracle):
     close(out, ref)
 
 
+@pytest.mark.parametrize("prefix_ctas", [0, 1, 8, 40, 1000])
+def test_cascade_one_launch_split_of_sms(prefix_ctas, pkg, oracle):
+    """The suffix and prefix passes in one launch, with the SMs split between
+    them in several ways (0: two launches; 1000: clamped to all CTAs but one,
+    which then streams every suffix page), each with the append: the pools
+    bit-exact against the oracle's write, the output within tolerance."""
+    wl = pkg.workloads
+    lay = wl.layout_radix_prefix(91, batch=96, prefix_pages=37, suffix_lo=1, suffix_hi=400)
+    t = wl.materialize_host(lay, 91, dtype="bfloat16", value_scale=0.7)
+    d = to_dev(t)
+    plan = pkg.plan_cascade(lay.block_table, lay.context_lens, 16, 8, device=DEV)
+    assert plan.num_work > 0 and plan.suffix_pages > 0
+    out = pkg.paged_attention_cascade(d["q"], d["k_cache"], d["v_cache"], plan, k_new=d["k_new"],
+                                      v_new=d["v_new"], prefix_ctas=prefix_ctas)
+    torch.cuda.synchronize()
+    pkg.check_device_errors()
+    kc, vc = t["k_cache"].clone(), t["v_cache"].clone()
+    oracle.kv_append(t["k_new"], t["v_new"], kc, vc, t["slot_mapping"])
+    assert torch.equal(d["k_cache"].cpu(), kc) and torch.equal(d["v_cache"].cpu(), vc)
+    ref, st = oracle.paged_decode_attention(t["q"], kc, vc, t["block_table"], t["context_lens"])
+    assert st == 0
+    close(out, ref)
+
+
 def test_cascade_two_groups_and_unshared_requests(pkg, oracle):
     """Two prefix groups side by side with requests that share nothing: the
     unshared ones go through the suffix pass alone."""

@@ -11,12 +11,12 @@ groups of requests whose block-table rows start with the same pages, and
     out[b] = merge( attention of b over its own suffix pages,
                     attention of b over the group's shared pages )
 
-with one launch for every request's suffix (the balanced decode kernel, KV
-append fused, returning log-sum-exps), one launch for all groups' shared pages
-(each page chunk of a KV head loaded into shared memory once for up to 128
-(request, head) rows of the group, tcgen05 tensor-core MMAs with accumulators
-in tensor memory), and one merge launch. Softmax splits exactly over disjoint key sets, so the result is the
-attention over the whole context.
+with, in one launch, every request's suffix (the balanced decode kernel, KV
+append fused, returning log-sum-exps) on most SMs and all groups' shared pages
+on the others (each page chunk of a KV head loaded into shared memory once for
+up to 128 (request, head) rows of the group, tcgen05 tensor-core MMAs with
+accumulators in tensor memory), then one merge launch. Softmax splits exactly
+over disjoint key sets, so the result is the attention over the whole context.
 """
 from __future__ import annotations
 
@@ -30,9 +30,19 @@ import torch
 from . import library as _L
 from .ops import _DTYPES, _SCHEDULES, _require_cuda, _stream, workspace_for
 
-MAX_CHUNK_PAGES = 8     # shared pages one CTA holds (kCascadeMaxPages)
+MAX_CHUNK_PAGES = 8     # shared pages of one tensor-core chunk (kCascadeMaxPages)
+MAX_ITEM_PAGES = 64     # shared pages of one work item, taken a chunk at a time (kCascadeMaxItemPages)
 TILE_ROWS = 128         # (request, head) rows one CTA covers: the M of its tensor-core tile
 WORK_INTS = 6
+# Cost model that splits the SMs of the one-launch step between the two passes
+# (B200 measurements on the radix workload): a suffix CTA streams a page of all
+# KV heads in about PAGE_US after about SUFFIX_FIXED_US of start-up and merge; a
+# prefix pipeline (two per CTA, running side by side) takes a (work item, KV
+# head) pair in about ITEM_US plus CHUNK_US per 8-page chunk of the item.
+PAGE_US = 1.2
+SUFFIX_FIXED_US = 8.0
+ITEM_US = 4.0
+CHUNK_US = 8.0
 
 
 @dataclass
@@ -44,9 +54,11 @@ class CascadePlan:
     member_list: torch.Tensor          # int32: member sequences of every group
     work: torch.Tensor                 # (W, 6) int32
     merge_items: torch.Tensor          # (M, 2) int32: (sequence, prefix chunks)
-    max_chunks: int
+    max_chunks: int                    # partial rows per (member, head): work items along the prefix
     groups: list = field(default_factory=list)   # host: (members, shared pages) per group
     shared_tokens: int = 0             # tokens the shared pages hold, once per group
+    suffix_pages: int = 0              # pages of every request's suffix (host count)
+    prefix_chunks: int = 0             # 8-page chunks of all work items (host count)
     _lse: Optional[torch.Tensor] = None
     _ws: Optional[torch.Tensor] = None
 
@@ -60,7 +72,7 @@ class CascadePlan:
 
 
 def plan_cascade(block_table, context_lens, num_heads: int, num_kv_heads: int, block_size: int = 16,
-                 min_shared_pages: int = 4, device=None) -> CascadePlan:
+                 min_shared_pages: int = 4, max_parts: int = 4, device=None) -> CascadePlan:
     """Group the requests of one decode step by shared leading pages.
 
     A group is the requests whose rows start with the same page id; its shared
@@ -70,6 +82,9 @@ def plan_cascade(block_table, context_lens, num_heads: int, num_kv_heads: int, b
     request's append slot (the shared pages are read while the suffix pass
     appends). Groups with fewer than
     ``min_shared_pages`` shared pages, or a single member, stay on the plain path.
+    The shared pages are split into at most ``max_parts`` runs of whole 8-page
+    chunks (at most 64 pages each): one work item per run and block of up to
+    128 / G members, one partial row per (member, head) and run.
     ``block_table`` / ``context_lens`` are host arrays (or CPU tensors).
     """
     bt = np.asarray(block_table.cpu() if isinstance(block_table, torch.Tensor) else block_table, dtype=np.int32)
@@ -102,18 +117,23 @@ def plan_cascade(block_table, context_lens, num_heads: int, num_kv_heads: int, b
             P = int(np.argmax(hit))
         if P < min_shared_pages:
             continue
+        # the prefix in at most max_parts runs of whole chunks (one work item
+        # per run and member block; the item's chunks are folded in one after
+        # another on the device, each (member, head) gets one partial per run)
         n_chunks = (P + MAX_CHUNK_PAGES - 1) // MAX_CHUNK_PAGES
-        max_chunks = max(max_chunks, n_chunks)
+        run = min(MAX_ITEM_PAGES, -(-n_chunks // max(1, max_parts)) * MAX_CHUNK_PAGES)
+        n_parts = (P + run - 1) // run
+        max_chunks = max(max_chunks, n_parts)
         pg_off, m_off = len(pages), len(members)
         pages.extend(int(x) for x in rows[0, :P])
         members.extend(int(b) for b in mem)
-        for c in range(n_chunks):
-            p0 = c * MAX_CHUNK_PAGES
-            np_c = min(MAX_CHUNK_PAGES, P - p0)
+        for c in range(n_parts):
+            p0 = c * run
+            np_c = min(run, P - p0)
             for m0 in range(0, mem.size, max_members):
                 nm = min(max_members, mem.size - m0)
                 work.append((m_off + m0, nm, pg_off + p0, np_c, c, 0))
-        merge.extend((int(b), n_chunks) for b in mem)
+        merge.extend((int(b), n_parts) for b in mem)
         suffix_bt[mem, :MB - P] = bt[mem, P:]
         suffix_bt[mem, MB - P:] = -1
         suffix_ctx[mem] = (ctx[mem] - P * block_size).astype(np.int32)
@@ -132,16 +152,50 @@ def plan_cascade(block_table, context_lens, num_heads: int, num_kv_heads: int, b
         page_list=t(pages if pages else [0]), member_list=t(members if members else [0]),
         work=t(work if work else np.zeros((0, WORK_INTS)), (-1, WORK_INTS)),
         merge_items=t(merge if merge else np.zeros((0, 2)), (-1, 2)),
-        max_chunks=max_chunks, groups=groups, shared_tokens=shared_tokens)
+        max_chunks=max_chunks, groups=groups, shared_tokens=shared_tokens,
+        suffix_pages=int(((np.maximum(suffix_ctx, 0).astype(np.int64) + block_size - 1) // block_size).sum()),
+        prefix_chunks=sum(-(-int(w[3]) // MAX_CHUNK_PAGES) for w in work))
+
+
+def one_launch_possible(num_kv_heads: int, head_dim: int, elem_bytes: int = 2) -> bool:
+    """Whether the suffix pass of these head shapes runs one balanced CTA per SM
+    holding every KV head (the condition for sharing its launch with the
+    shared-prefix pass): the C library's plan puts all KV heads in one CTA when a
+    16-row page tile of them fits 36 KB, and one CTA per SM when that CTA has
+    8 or more consumer warps (one per KV head)."""
+    row = num_kv_heads * head_dim * elem_bytes
+    pitch = row if (row // 16) % 2 else row + 16
+    return num_kv_heads >= 8 and 16 * pitch <= 36864
+
+
+def prefix_ctas_for(plan: CascadePlan, num_kv_heads: int, num_sms: int) -> int:
+    """CTAs of the one-launch step that run the shared-prefix pairs: the
+    smallest count (at most half the SMs) that minimises the estimated time of
+    the slower pass -- the pairs go round-robin to two pipelines per CTA, the
+    suffix pages are shared evenly by the other CTAs. 0 when there is no
+    prefix work."""
+    if plan.num_work == 0 or num_sms < 2:
+        return 0
+    pairs = plan.num_work * num_kv_heads
+    pair_us = ITEM_US + CHUNK_US * plan.prefix_chunks / plan.num_work
+    best, best_t = 1, float("inf")
+    for n in range(1, num_sms // 2 + 1):
+        t = max(-(-pairs // (2 * n)) * pair_us, plan.suffix_pages * PAGE_US / (num_sms - n) + SUFFIX_FIXED_US)
+        if t < best_t - 1e-9:
+            best, best_t = n, t
+    return best
 
 
 def paged_attention_cascade(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, plan: CascadePlan,
                             scale: Optional[float] = None, *, k_new: Optional[torch.Tensor] = None,
                             v_new: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
-                            schedule: str = "auto", overlap_previous: bool = False) -> torch.Tensor:
+                            schedule: str = "auto", overlap_previous: bool = False,
+                            prefix_ctas: Optional[int] = None) -> torch.Tensor:
     """Paged decode attention (with the KV append when k_new/v_new are given) using
-    ``plan``: same result as ``paged_attention`` over the original block tables,
-    three launches (suffix, shared prefix, merge). bf16/f16."""
+    ``plan``: same result as ``paged_attention`` over the original block tables.
+    The suffix and shared-prefix passes share one launch (``prefix_ctas`` CTAs
+    for the prefix pairs, default from the plan's cost model; 0 runs them as two
+    launches), then a merge launch. bf16/f16."""
     dev = _require_cuda(q, k_cache, v_cache)
     if q.dtype not in (torch.bfloat16, torch.float16) or k_cache.dtype != q.dtype or v_cache.dtype != q.dtype:
         raise TypeError("the cascade path is built for bf16/f16 (use paged_attention for fp32)")
@@ -171,8 +225,8 @@ def paged_attention_cascade(q: torch.Tensor, k_cache: torch.Tensor, v_cache: tor
         plan._ws = torch.empty(max(int(need.value), 256), dtype=torch.uint8, device=dev)
     dws = workspace_for(dev)
     buf = dws.ensure(B, H, D, sbt.shape[1], 0, KVH, q.dtype)
-    st_ = _stream(dev)
-    dt = _DTYPES[q.dtype]
+    if prefix_ctas is None:
+        prefix_ctas = prefix_ctas_for(plan, KVH, dws.num_sms)
     if k_new is not None:
         _require_cuda(q, k_new, v_new)
         if k_new.shape != (B, KVH, D) or v_new.shape != k_new.shape or k_new.dtype != q.dtype or \
@@ -181,26 +235,13 @@ def paged_attention_cascade(q: torch.Tensor, k_cache: torch.Tensor, v_cache: tor
         kn, vn, ns0, ns1 = k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0), k_new.stride(1)
     else:
         kn, vn, ns0, ns1 = None, None, 0, 0
-    st = lib.ubx_paged_decode_attention_lse(
+    st = lib.ubx_cascade_attention(
         kn, vn, ns0, ns1, q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(),
         k_cache.stride(0), k_cache.stride(1), k_cache.stride(2), sbt.data_ptr(), sbt.stride(0), sctx.data_ptr(),
-        out.data_ptr(), out.stride(0), out.stride(1), B, H, KVH, D, bs, NB, sbt.shape[1], float(scale), dt,
-        _SCHEDULES[schedule], 0, _L.FLAG_OVERLAP_PREVIOUS if overlap_previous else 0, plan._lse.data_ptr(),
-        buf.data_ptr(), buf.numel(), st_)
-    _L.check(st, "cascade suffix pass")
-    if plan.num_work:
-        # Both follow a kernel of this call on the stream, so they start while it
-        # drains: the suffix pass writes no shared page (the plan keeps every
-        # request's append page private) and neither writes the plan arrays.
-        st = lib.ubx_cascade_prefix_attention(
-            q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0),
-            k_cache.stride(1), k_cache.stride(2), NB, plan.page_list.data_ptr(), plan.member_list.data_ptr(),
-            plan.work.data_ptr(), plan.num_work, plan.max_chunks, B, H, KVH, D, float(scale), dt,
-            plan._ws.data_ptr(), plan._ws.numel(), dws.error_word_ptr(), _L.FLAG_OVERLAP_PREVIOUS, st_)
-        _L.check(st, "cascade prefix pass")
-        st = lib.ubx_cascade_merge(out.data_ptr(), out.stride(0), out.stride(1), plan._lse.data_ptr(),
-                                   plan.merge_items.data_ptr(), plan.num_merge, plan.max_chunks, B, H, D, dt,
-                                   plan._ws.data_ptr(), plan._ws.numel(), dws.error_word_ptr(),
-                                   _L.FLAG_OVERLAP_PREVIOUS, st_)
-        _L.check(st, "cascade merge")
+        out.data_ptr(), out.stride(0), out.stride(1), B, H, KVH, D, bs, NB, sbt.shape[1], float(scale),
+        _DTYPES[q.dtype], _SCHEDULES[schedule], plan.page_list.data_ptr(), plan.member_list.data_ptr(),
+        plan.work.data_ptr(), plan.num_work, plan.merge_items.data_ptr(), plan.num_merge, plan.max_chunks,
+        int(prefix_ctas), _L.FLAG_OVERLAP_PREVIOUS if overlap_previous else 0, plan._lse.data_ptr(),
+        buf.data_ptr(), buf.numel(), plan._ws.data_ptr(), plan._ws.numel(), _stream(dev))
+    _L.check(st, "cascade attention")
     return out

@@ -422,7 +422,7 @@ int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache
                 int num_kv_heads, int head_dim, int block_size, int64_t num_blocks, int max_blocks_per_seq,
                 float scale, int dtype, int schedule, int split_pages, int flags, void* workspace,
                 size_t workspace_bytes, const AppendArgs* app, const PrepArgs* prep, float* lse, void* stream,
-                size_t clear_bytes = 0) {
+                size_t clear_bytes = 0, CascadeParams* fuse = nullptr, int prefix_ctas = 0) {
   g_last_error.clear();
   int st = check_shape(num_heads, num_kv_heads, head_dim, block_size, dtype);
   if (st != UBX_OK) return st;
@@ -512,6 +512,7 @@ int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache
   p.tail_trim = ((flags & UBX_FLAG_OVERLAP_PREVIOUS) && pl.balanced && pl.ctas_per_sm == 1 &&
                  pl.grid.y == 1)
                     ? kTailTrimPages : 0;
+  p.range_first = 0;
   p.part_o = reinterpret_cast<float*>(ws + wl.o_off);
   p.part_ml = reinterpret_cast<float2*>(ws + wl.ml_off);
   p.counters = reinterpret_cast<int32_t*>(ws + kHeaderBytes);
@@ -541,6 +542,33 @@ int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache
     // leaves the state of a call still running elsewhere alone
     cudaError_t ce = cudaMemsetAsync(workspace, 0, std::min(clear_bytes, workspace_bytes), s);
     if (ce != cudaSuccess) return cuda_fail(ce, "workspace clear");
+  }
+  if (fuse) {
+    // a cascade step: the shared-prefix pass shares the launch when the suffix
+    // pass runs one balanced CTA per SM (prefix CTAs first, on their own SMs);
+    // otherwise it follows as its own launch
+    fuse->error = p.error;
+    const int fused_smem = std::max(pl.smem, fused_prefix_smem_bytes(head_dim));
+    const bool fusable = pl.balanced && pl.ctas_per_sm == 1 && pl.grid.y == 1 && pl.grid.x >= 2 &&
+                         dtype != UBX_DTYPE_F32 && fused_smem <= kSmemLimit;
+    if (fusable && fuse->num_work > 0 && prefix_ctas > 0) {
+      p.range_first = std::min(std::max(prefix_ctas, 1), (int)pl.grid.x - 1);
+      LaunchShape fshape = shape;
+      fshape.smem_bytes = fused_smem;
+      cudaError_t e = launch_cascade_fused(dtype, head_dim, p, *fuse, fshape, s);
+      if (e != cudaSuccess) return cuda_fail(e, "cascade launch");
+      return UBX_OK;
+    }
+    cudaError_t e = launch_paged_decode(dtype, head_dim, pl.gw, pl.balanced, p, shape, s);
+    if (e != cudaSuccess) return cuda_fail(e, "paged_decode launch");
+    if (!pl.balanced) {
+      e = launch_lse_combine(dtype, head_dim, p, s);
+      if (e != cudaSuccess) return cuda_fail(e, "lse_combine launch");
+    }
+    fuse->overlap = true;  // follows a kernel of this call
+    e = launch_cascade_prefix(dtype, head_dim, *fuse, s);
+    if (e != cudaSuccess) return cuda_fail(e, "cascade prefix launch");
+    return UBX_OK;
   }
   cudaError_t e = launch_paged_decode(dtype, head_dim, pl.gw, pl.balanced, p, shape, s);
   if (e != cudaSuccess) return cuda_fail(e, "paged_decode launch");
@@ -635,21 +663,23 @@ int ubx_cascade_workspace_size(int batch, int num_heads, int head_dim, int max_c
   return UBX_OK;
 }
 
-int ubx_cascade_prefix_attention(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache,
-                                 const void* v_cache, int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head,
-                                 int64_t num_blocks, const int32_t* page_list, const int32_t* member_list,
-                                 const int32_t* work_items, int num_work_items, int max_chunks, int batch,
-                                 int num_heads, int num_kv_heads, int head_dim, float scale, int dtype,
-                                 void* cascade_ws, size_t cascade_ws_bytes, int32_t* error_word, int flags,
-                                 void* stream) {
-  g_last_error.clear();
-  if (flags & ~UBX_FLAG_OVERLAP_PREVIOUS) return fail(UBX_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
+}  // extern "C"
+
+namespace {
+
+// Checks the shared-prefix pass's arguments and fills its launch parameters
+// (error word and overlap flag left to the caller).
+int make_cascade_params(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache, const void* v_cache,
+                        int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head, int64_t num_blocks,
+                        const int32_t* page_list, const int32_t* member_list, const int32_t* work_items,
+                        int num_work_items, int max_chunks, int batch, int num_heads, int num_kv_heads, int head_dim,
+                        float scale, int dtype, void* cascade_ws, size_t cascade_ws_bytes, CascadeParams* out) {
   int st = check_shape(num_heads, num_kv_heads, head_dim, kBlockSize, dtype);
   if (st != UBX_OK) return st;
   if (dtype == UBX_DTYPE_F32) return fail(UBX_ERR_UNSUPPORTED, "the cascade pass is built for bf16/f16");
   if (num_work_items < 0 || max_chunks <= 0 || batch <= 0 || num_blocks <= 0)
     return fail(UBX_ERR_INVALID_ARGUMENT, "bad cascade sizes");
-  if (num_work_items == 0) return UBX_OK;
+  if (num_work_items == 0) return UBX_OK;  // nothing to launch: *out is not used
   if (!q || !k_cache || !v_cache || !page_list || !member_list || !work_items || !cascade_ws)
     return fail(UBX_ERR_INVALID_ARGUMENT, "null pointer");
   const int es = 2;
@@ -664,7 +694,7 @@ int ubx_cascade_prefix_attention(const void* q, int64_t q_s_b, int64_t q_s_h, co
     return fail(UBX_ERR_WORKSPACE, "cascade workspace of %zu bytes, this call needs %zu", cascade_ws_bytes, need);
   if (!aligned16(cascade_ws)) return fail(UBX_ERR_WORKSPACE, "cascade workspace must be 16-byte aligned");
   if (!(scale > 0.f) && !(scale < 0.f)) return fail(UBX_ERR_INVALID_ARGUMENT, "scale must be finite and non-zero");
-  CascadeParams p;
+  CascadeParams& p = *out;
   p.q = q;
   p.q_sb = q_s_b;
   p.q_sh = q_s_h;
@@ -686,6 +716,29 @@ int ubx_cascade_prefix_attention(const void* q, int64_t q_s_b, int64_t q_s_h, co
   uint8_t* ws = static_cast<uint8_t*>(cascade_ws);
   p.part_ml = reinterpret_cast<float2*>(ws);
   p.part_o = reinterpret_cast<float*>(ws + cascade_ml_bytes(batch, num_heads, max_chunks));
+  p.error = nullptr;
+  p.overlap = false;
+  return UBX_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ubx_cascade_prefix_attention(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache,
+                                 const void* v_cache, int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head,
+                                 int64_t num_blocks, const int32_t* page_list, const int32_t* member_list,
+                                 const int32_t* work_items, int num_work_items, int max_chunks, int batch,
+                                 int num_heads, int num_kv_heads, int head_dim, float scale, int dtype,
+                                 void* cascade_ws, size_t cascade_ws_bytes, int32_t* error_word, int flags,
+                                 void* stream) {
+  g_last_error.clear();
+  if (flags & ~UBX_FLAG_OVERLAP_PREVIOUS) return fail(UBX_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
+  CascadeParams p;
+  int st = make_cascade_params(q, q_s_b, q_s_h, k_cache, v_cache, c_s_block, c_s_tok, c_s_head, num_blocks,
+                               page_list, member_list, work_items, num_work_items, max_chunks, batch, num_heads,
+                               num_kv_heads, head_dim, scale, dtype, cascade_ws, cascade_ws_bytes, &p);
+  if (st != UBX_OK || num_work_items == 0) return st;
   p.error = error_word;
   p.overlap = (flags & UBX_FLAG_OVERLAP_PREVIOUS) != 0;
   cudaError_t e = launch_cascade_prefix(dtype, head_dim, p, static_cast<cudaStream_t>(stream));
@@ -732,6 +785,41 @@ int ubx_cascade_merge(void* out, int64_t o_s_b, int64_t o_s_h, const float* lse,
   cudaError_t e = launch_cascade_merge(dtype, head_dim, p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "cascade merge launch");
   return UBX_OK;
+}
+
+int ubx_cascade_attention(const void* k_new, const void* v_new, int64_t new_s_tok, int64_t new_s_head,
+                          const void* q, int64_t q_s_b, int64_t q_s_h, void* k_cache, void* v_cache,
+                          int64_t c_s_block, int64_t c_s_tok, int64_t c_s_head, const int32_t* suffix_block_table,
+                          int64_t bt_s_row, const int32_t* suffix_context_lens, void* out, int64_t o_s_b,
+                          int64_t o_s_h, int batch, int num_heads, int num_kv_heads, int head_dim, int block_size,
+                          int64_t num_blocks, int max_blocks_per_seq, float scale, int dtype, int schedule,
+                          const int32_t* page_list, const int32_t* member_list, const int32_t* work_items,
+                          int num_work_items, const int32_t* merge_items, int num_merge_items, int max_chunks,
+                          int prefix_ctas, int flags, float* lse_out, void* workspace, size_t workspace_bytes,
+                          void* cascade_ws, size_t cascade_ws_bytes, void* stream) {
+  g_last_error.clear();
+  if ((k_new == nullptr) != (v_new == nullptr)) return fail(UBX_ERR_INVALID_ARGUMENT, "pass both k_new and v_new, or neither");
+  if (!lse_out) return fail(UBX_ERR_INVALID_ARGUMENT, "lse_out is required");
+  if (flags & ~UBX_FLAG_OVERLAP_PREVIOUS) return fail(UBX_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
+  if (dtype == UBX_DTYPE_F32) return fail(UBX_ERR_UNSUPPORTED, "the cascade is built for bf16/f16");
+  if (num_merge_items < 0 || prefix_ctas < 0) return fail(UBX_ERR_INVALID_ARGUMENT, "bad cascade sizes");
+  if (batch == 0) return UBX_OK;
+  CascadeParams cp;
+  int st = make_cascade_params(q, q_s_b, q_s_h, k_cache, v_cache, c_s_block, c_s_tok, c_s_head, num_blocks,
+                               page_list, member_list, work_items, num_work_items, max_chunks, batch, num_heads,
+                               num_kv_heads, head_dim, scale, dtype, cascade_ws, cascade_ws_bytes, &cp);
+  if (st != UBX_OK) return st;
+  if (num_merge_items > 0 && !merge_items) return fail(UBX_ERR_INVALID_ARGUMENT, "null pointer");
+  const AppendArgs app{k_new, v_new, new_s_tok, new_s_head};
+  st = decode_impl(q, q_s_b, q_s_h, k_cache, v_cache, c_s_block, c_s_tok, c_s_head, suffix_block_table, bt_s_row,
+                   suffix_context_lens, out, o_s_b, o_s_h, batch, num_heads, num_kv_heads, head_dim, block_size,
+                   num_blocks, max_blocks_per_seq, scale, dtype, schedule, 0, flags, workspace,
+                   workspace_bytes, k_new ? &app : nullptr, nullptr, lse_out, stream, 0,
+                   num_work_items > 0 ? &cp : nullptr, prefix_ctas);
+  if (st != UBX_OK || num_work_items == 0 || num_merge_items == 0) return st;
+  return ubx_cascade_merge(out, o_s_b, o_s_h, lse_out, merge_items, num_merge_items, max_chunks, batch, num_heads,
+                           head_dim, dtype, cascade_ws, cascade_ws_bytes, static_cast<int32_t*>(workspace),
+                           UBX_FLAG_OVERLAP_PREVIOUS, stream);
 }
 
 int ubx_paged_decode_prep_attention(const void* q_raw, int64_t q_s_b, int64_t q_s_h, const void* k_raw,

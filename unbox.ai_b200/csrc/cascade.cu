@@ -6,19 +6,23 @@
 // those pages once per request. Here a decode step is split in three:
 //   1. the decode kernel attends each request over its private suffix pages
 //      (positions past the shared prefix) and also returns the log-sum-exp;
-//   2. cascade_prefix_kernel attends every request of a prefix group over the
-//      shared pages at once: a CTA loads a chunk of up to 8 shared pages of one
-//      KV head into shared memory once, with the q rows of up to 128 (request,
-//      query head) pairs of that group, and runs S = Q K^T and O = P V as two
-//      chains of 5th-generation tensor-core MMAs (tcgen05.mma, M = 128, fp32
-//      accumulators in tensor memory), the softmax in between on one thread per
-//      row; it writes unnormalised partial (acc, max, sum) rows per chunk;
-//   3. cascade_merge_kernel merges the suffix output with the chunks' partials by
+//   2. the shared-prefix pass attends every request of a prefix group over the
+//      shared pages at once: a work item is a run of up to 64 shared pages of
+//      one KV head and up to 128 (request, query head) rows of that group,
+//      taken 8 pages at a time through shared memory with S = Q K^T and
+//      O += P V on the 5th-generation tensor cores (tcgen05.mma, M = 128, fp32
+//      accumulators in tensor memory) and an online softmax in between, one
+//      thread per row (ubx_cascade_prefix.cuh); it writes one unnormalised
+//      partial (acc, max, sum) row per run. It runs here as its own kernel
+//      (cascade_prefix_kernel, one item per CTA) or inside the suffix pass's
+//      launch (cascade_fused_kernel, paged_decode.cu);
+//   3. cascade_merge_kernel merges the suffix output with the runs' partials by
 //      log-sum-exp weights (the same combination the split-KV path uses).
 // The result equals attention over the whole context (softmax is exactly
 // decomposable over disjoint key sets).
 #include <type_traits>
 
+#include "ubx_cascade_prefix.cuh"
 #include "ubx_common.cuh"
 #include "ubx_internal.h"
 #include "ubx_mma.cuh"
@@ -28,211 +32,30 @@ namespace ubx {
 
 namespace {
 
-// Shared-memory layout of one prefix CTA (tcgen05 operands, SWIZZLE_NONE
-// canonical layout: a tile of R rows x C 16-byte chunks is stored chunk-major,
-// [chunk][row][16 B], so 8 consecutive rows of one chunk form a contiguous
-// 128-byte core matrix):
-//   Q [D/8][128 rows][16 B]  (rows = (member, query head), member-major)
-//   K [D/8][128 tokens][16 B], V [D/8][128 tokens][16 B]
-//   P [128/8 token chunks][128 rows][16 B] over Q and K once S is complete
-//   2 mbarriers, the TMEM base address, the row max / sum of each half [2][128]
-constexpr int kTcRows = kCascadeRows;               // M of both MMAs
-constexpr int kTcTokens = kCascadeMaxPages * 16;    // N of S, K of O (at most)
-constexpr uint32_t kTcCols = 256;                   // TMEM: S (128 columns) + O (head_dim <= 128)
-constexpr int kTcThreads = 256;                     // two threads per row: one per column half
-constexpr int kTcTailBytes = 64 + 2 * 2 * kTcRows * 4 + (kCascadeMaxPages + kTcRows) * 4;
-
+// One work item per CTA (blockIdx.x: the item, blockIdx.y: the KV head).
 template <typename T, int D>
 __global__ void __launch_bounds__(kTcThreads) cascade_prefix_kernel(const CascadeParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  constexpr int CH = D / 8;  // 16-byte chunks of a head row
-  constexpr int R = kTcRows, TT = kTcTokens, NTH = kTcThreads;
-  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-  uint8_t* q_s = smem;
-  uint8_t* k_s = q_s + CH * R * 16;
-  uint8_t* v_s = k_s + CH * TT * 16;
-  uint8_t* p_s = smem;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(v_s + CH * TT * 16);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 2);
-  float* red_max = reinterpret_cast<float*>(smem + 3 * CH * R * 16 + 64);  // [2][R], 16-byte aligned
-  float* red_sum = red_max + 2 * R;                                        // [2][R]
-  int32_t* pg_s = reinterpret_cast<int32_t*>(red_sum + 2 * R);             // the chunk's page ids
-  int32_t* mem_s = pg_s + kCascadeMaxPages;                                // the item's member sequences
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int kvh = blockIdx.y;
+  const PrefixSmem sm = carve_prefix_smem<D>(smem);
+  const int tid = threadIdx.x;
   // Launched with programmatic overlap, this CTA may run while the previous
   // kernel drains: it reads only the plan arrays and the shared pages before
   // griddepcontrol.wait (the caller's promise), and q, the workspace and the
   // error word after it. Without the launch attribute the wait returns at once.
   griddep_launch_dependents();
-  const int32_t* item = p.work + kCascadeWorkInts * blockIdx.x;
-  const int m_off = __ldg(item + 0), n_mem = __ldg(item + 1), pg_off = __ldg(item + 2), n_pg = __ldg(item + 3),
-            chunk = __ldg(item + 4);
-  const int G = p.num_heads / p.num_kv_heads;
-  if (n_pg < 1 || n_pg > kCascadeMaxPages || n_mem < 1 || n_mem * G > R || chunk < 0 || chunk >= p.max_chunks) {
-    griddep_wait();
-    if (tid == 0) set_error(p.error, kErrBadWork);
-    return;
-  }
-  const int NT = n_pg * 16;  // tokens of this chunk: N of S, K of O (a multiple of 16)
-  if (warp == 0) tc::tmem_alloc(tmem_slot, kTcCols);
+  if (tid < 32) tc::tmem_alloc(sm.tmem_slot, kTcCols);
   if (tid == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
+    mbar_init(&sm.bar[0], 1);
+    mbar_init(&sm.bar[1], 1);
     fence_mbar_init();
   }
-  // the item's page ids and member sequences, read once (plan arrays)
-  if (tid < n_pg) pg_s[tid] = __ldg(&p.page_list[pg_off + tid]);
-  if (tid >= 128 && tid - 128 < n_mem) mem_s[tid - 128] = __ldg(&p.member_list[m_off + tid - 128]);
-  __syncthreads();
-
-  // ---- K and V of the chunk's pages (this KV head): 16-byte pieces, 8
-  // consecutive lanes = 8 consecutive tokens of one chunk (one core matrix)
-  bool bad_page = false;
-  for (int v = tid; v < 2 * NT * CH; v += NTH) {
-    const int is_v = v >= NT * CH;
-    const int u = is_v ? v - NT * CH : v;
-    const int t = (u / (8 * CH)) * 8 + (u & 7), c = (u >> 3) % CH;
-    uint8_t* dst = (is_v ? v_s : k_s) + (c * TT + t) * 16;
-    const int page = pg_s[t >> 4];
-    if (page >= 0 && (int64_t)page < p.num_blocks) {
-      const uint8_t* src = static_cast<const uint8_t*>(is_v ? p.v_cache : p.k_cache) +
-                           ((int64_t)page * p.c_sblk + (int64_t)(t & 15) * p.c_stok + (int64_t)kvh * D) * sizeof(T) +
-                           c * 16;
-      cp_async_16(dst, src);
-    } else {
-      if ((t & 15) == 0 && c == 0 && !is_v) bad_page = true;
-      *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
-    }
-  }
-  griddep_wait();  // the page copies stay in flight across the wait
-  if (bad_page) set_error(p.error, kErrBadPage);
-  // ---- Q rows: row r = (member r / G, query head kvh * G + r % G); rows past
-  // the members are zero
-  for (int v = tid; v < R * CH; v += NTH) {
-    const int r = (v / (8 * CH)) * 8 + (v & 7), c = (v >> 3) % CH;
-    uint8_t* dst = q_s + (c * R + r) * 16;
-    const int mi = r / G;
-    const int b = mi < n_mem ? mem_s[mi] : -1;
-    if (b >= 0 && b < p.batch) {
-      cp_async_16(dst, static_cast<const uint8_t*>(p.q) +
-                           ((int64_t)b * p.q_sb + (int64_t)(kvh * G + r % G) * p.q_sh) * sizeof(T) + c * 16);
-    } else {
-      *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
-    }
-  }
-  cp_async_commit_wait_all();
-  fence_proxy_async_smem();  // these generic-proxy writes before the MMAs' reads
   tc::fence_before_thread_sync();
   __syncthreads();
   tc::fence_after_thread_sync();
-  const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_s = tmem, tmem_o = tmem + TT;  // columns [0, 128) and [128, 128 + D)
-
-  // ---- S = Q K^T (M = 128 rows, N = NT tokens, K = D): A and B K-major
-  if (tid == 0) {
-    const uint32_t idesc = tc::instr_desc_f16(kBf16, R, NT, false, false);
-#pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks)
-      tc::mma_f16(tmem_s, tc::smem_desc(q_s + ks * 2 * R * 16, R * 16, 128),
-                  tc::smem_desc(k_s + ks * 2 * TT * 16, TT * 16, 128), idesc, ks > 0);
-    tc::commit(&bar[0]);
-  }
-  bool ok = mbar_wait_bounded(&bar[0], 0);
-  tc::fence_after_thread_sync();
-
-  // ---- softmax: warp w reads TMEM lanes 32 (w % 4) ..; thread = (row, column
-  // half h): tokens [64 h, 64 h + 64) of its row
-  const int row = (warp & 3) * 32 + lane, h = warp >> 2;
-  const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-  const int c0 = h * (TT / 2);
-  const float cs = p.scale_log2;
-  float s[TT / 2];
-#pragma unroll
-  for (int j = 0; j < TT / 32; ++j) {
-    if (c0 + j * 16 < NT) {
-      float v16[16];
-      tc::ld16(tmem_s + lane_off + c0 + j * 16, v16);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) s[j * 16 + i] = v16[i];
-    }
-  }
-  float mx = -INFINITY;
-#pragma unroll
-  for (int j = 0; j < TT / 2; ++j)
-    if (c0 + j < NT) mx = fmaxf(mx, s[j]);
-  red_max[h * R + row] = mx;
-  __syncthreads();
-  mx = fmaxf(red_max[row], red_max[R + row]);
-  const float mc = mx * cs;
-  float l = 0.f;
-#pragma unroll
-  for (int j8 = 0; j8 < TT / 16; ++j8) {
-    if (c0 + j8 * 8 < NT) {
-      float pv[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        pv[i] = exp2f(fmaf(s[j8 * 8 + i], cs, -mc));
-        l += pv[i];
-      }
-      *reinterpret_cast<uint4*>(p_s + ((c0 / 8 + j8) * R + row) * 16) = Elem<T>::pack(pv);
-    }
-  }
-  red_sum[h * R + row] = l;
-  fence_proxy_async_smem();
-  tc::fence_before_thread_sync();
-  __syncthreads();
-  tc::fence_after_thread_sync();
-
-  // ---- O = P V (M = 128 rows, N = D, K = NT tokens): P K-major, V MN-major
-  if (tid == 0) {
-    const uint32_t idesc = tc::instr_desc_f16(kBf16, R, D, false, true);
-    for (int ks = 0; ks < NT / 16; ++ks)
-      tc::mma_f16(tmem_o, tc::smem_desc(p_s + ks * 2 * R * 16, R * 16, 128),
-                  tc::smem_desc(v_s + ks * 2 * 128, 128, TT * 16), idesc, ks > 0);
-    tc::commit(&bar[1]);
-  }
-  ok = mbar_wait_bounded(&bar[1], 0) && ok;
-  tc::fence_after_thread_sync();
-
-  // ---- partial rows of this chunk: unnormalised O and (max in log2 units,
-  // sum). Staged through shared memory (rows of D floats + 16 bytes: 8
-  // consecutive rows fall in 8 different 16-byte bank groups) over Q, K and V,
-  // all consumed, then written row by row with whole warps on each row.
-  constexpr int HD = D / 2;
-  constexpr int OP = D * 4 + 16;  // staged row pitch (bytes)
-  uint8_t* o_s = smem;
-  int64_t* slot_s = reinterpret_cast<int64_t*>(red_max);  // [R], over the row max (consumed)
-#pragma unroll
-  for (int j = 0; j < HD / 8; ++j) {
-    float o8[8];
-    tc::ld8(tmem_o + lane_off + h * HD + j * 8, o8);
-    float4* dst = reinterpret_cast<float4*>(o_s + row * OP + (h * HD + j * 8) * 4);
-    dst[0] = make_float4(o8[0], o8[1], o8[2], o8[3]);
-    dst[1] = make_float4(o8[4], o8[5], o8[6], o8[7]);
-  }
-  if (h == 0) {
-    const int mi = row / G;
-    const int b = mi < n_mem ? mem_s[mi] : -1;
-    const bool real = ok && b >= 0 && b < p.batch;
-    const int64_t slot = ((int64_t)b * p.num_heads + kvh * G + row % G) * p.max_chunks + chunk;
-    slot_s[row] = real ? slot : -1;
-    if (real) p.part_ml[slot] = make_float2(mc, red_sum[row] + red_sum[R + row]);
-  }
-  __syncthreads();
-  for (int v = tid; v < R * (D / 4); v += NTH) {
-    const int r = v / (D / 4), q4 = v - r * (D / 4);
-    const int64_t slot = slot_s[r];
-    if (slot >= 0)
-      reinterpret_cast<float4*>(p.part_o + slot * D)[q4] = *reinterpret_cast<const float4*>(o_s + r * OP + q4 * 16);
-  }
-  if (!ok && tid == 0) set_error(p.error, kErrTimeout);
-  tc::fence_before_thread_sync();
-  __syncthreads();
-  if (warp == 0) {
-    tc::fence_after_thread_sync();
-    tc::tmem_dealloc(tmem, kTcCols);
-  }
+  const uint32_t tmem = *sm.tmem_slot;
+  uint32_t parity = 0;
+  prefix_item<T, D>(p, blockIdx.x, blockIdx.y, sm, tmem, parity, tid, [] { __syncthreads(); });
+  if (tid < 32) tc::tmem_dealloc(tmem, kTcCols);
 }
 
 // One warp task per (merge item, group of 32 / (D / 8) query heads); lanes are
@@ -375,11 +198,12 @@ cudaError_t launch_merge_t(int head_dim, const CascadeMergeParams& p, cudaStream
 
 }  // namespace
 
-// Q, K and V tiles of 128 rows of 16-bit elements, two mbarriers and the TMEM
-// address; never below 80 KB, so that at most two CTAs share an SM and their
+// One work item's tiles (Q, K with P over it, V), mbarriers, page ids and
+// members; never below 80 KB, so that at most two CTAs share an SM and their
 // tensor memory (2 x 256 columns) never has to wait for a free column.
 int cascade_smem_bytes(int head_dim) {
-  const int need = 3 * kTcRows * head_dim * 2 + kTcTailBytes;
+  const int need = head_dim == 64 ? prefix_item_smem_bytes<64>()
+                   : head_dim == 112 ? prefix_item_smem_bytes<112>() : prefix_item_smem_bytes<128>();
   return need > kCascadeMinSmem ? need : kCascadeMinSmem;
 }
 

@@ -37,6 +37,7 @@
 // its own loads in flight before the CTA exits.
 #include <type_traits>
 
+#include "ubx_cascade_prefix.cuh"
 #include "ubx_common.cuh"
 #include "ubx_internal.h"
 #include "ubx_mma.cuh"
@@ -71,6 +72,12 @@ __device__ __forceinline__ int warp_inclusive_scan(int v, int lane) {
   return v;
 }
 
+// Balanced schedule: this CTA's index among the CTAs that split the page
+// ranges, and their number (a fused cascade launch runs its shared-prefix CTAs
+// first, at indices below p.range_first).
+__device__ __forceinline__ int range_cta(const DecodeParams& p) { return (int)blockIdx.x - p.range_first; }
+__device__ __forceinline__ int range_ctas(const DecodeParams& p) { return (int)gridDim.x - p.range_first; }
+
 // prefix[b] = pages of sequences 0..b-1, prefix[B] = total. Whole CTA.
 __device__ void build_page_prefix(const DecodeParams& p, int32_t* prefix, int32_t* warp_tot) {
   const int B = p.batch;
@@ -78,7 +85,7 @@ __device__ void build_page_prefix(const DecodeParams& p, int32_t* prefix, int32_
   const int per = (B + nt - 1) / nt;
   const int b0 = min(B, (int)threadIdx.x * per);
   const int b1 = min(B, b0 + per);
-  const bool report = blockIdx.x == 0 && blockIdx.y == 0;
+  const bool report = range_cta(p) == 0 && blockIdx.y == 0;
   int local = 0;
   for (int b = b0; b < b1; ++b) local += pages_of(p, b, report);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = nt >> 5;
@@ -348,12 +355,13 @@ __device__ Work setup_work(const DecodeParams& p, const Smem& sm, int32_t* warp_
   if constexpr (BAL) {
     build_page_prefix(p, sm.prefix, warp_tot);
     w.total = sm.prefix[B];
-    w.w_eff = min((int)gridDim.x, w.total);
+    w.w_eff = min(range_ctas(p), w.total);
     // the last range keeps at least half of an even share
     if (w.w_eff > 1) w.trim = max(0, min(p.tail_trim, w.total / (2 * w.w_eff)));
-    if ((int)blockIdx.x < w.w_eff) {
-      w.g_begin = range_begin(w, blockIdx.x);
-      w.g_end = range_begin(w, blockIdx.x + 1);
+    const int x = range_cta(p);
+    if (x < w.w_eff) {
+      w.g_begin = range_begin(w, x);
+      w.g_end = range_begin(w, x + 1);
       int lo = 0, hi = B;  // last b with prefix[b] <= g_begin
       while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
@@ -378,7 +386,7 @@ template <typename T, int D, bool BAL>
 __device__ void write_zero_rows(const DecodeParams& p, const Work& w, const int32_t* prefix, int head_lo,
                                 int head_hi, int tid, int nthreads) {
   if constexpr (BAL) {
-    for (int b = blockIdx.x; b < p.batch; b += gridDim.x)
+    for (int b = range_cta(p); b < p.batch; b += range_ctas(p))
       if (prefix[b + 1] == prefix[b]) write_zero_row<T, D>(p, b, head_lo, head_hi, tid, nthreads);
   } else {
     if (w.n_split == 0 && w.chunk == 0) write_zero_row<T, D>(p, w.b_first, head_lo, head_hi, tid, nthreads);
@@ -513,7 +521,7 @@ __device__ void produce(const DecodeParams& p, const Work& w, const Smem& sm, in
 template <bool BAL>
 __device__ __forceinline__ int64_t partial_slot(const DecodeParams& p, const Work& w, int b, bool first_seg) {
   if constexpr (BAL)
-    return 2 * (int64_t)blockIdx.x + (first_seg ? 0 : 1);
+    return 2 * (int64_t)range_cta(p) + (first_seg ? 0 : 1);
   else
     return (int64_t)b * p.max_chunks + w.chunk;
 }
@@ -956,10 +964,10 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
   consume_fma<T, D, GW, BAL>(p, w, sm, kh, blockIdx.y * HG + kh, warp % WPK, lane);
 }
 
+// One CTA of the tensor-core decode (16-bit pools): 8 consumer warps, one per
+// KV head of the CTA's head group, and a producer warp.
 template <typename T, int D, bool BAL>
-__global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
-    paged_decode_mma_kernel(const DecodeParams p) {
-  extern __shared__ __align__(128) uint8_t smem_raw[];
+__device__ __forceinline__ void decode_mma_cta(const DecodeParams& p, uint8_t* smem_raw) {
   __shared__ int32_t warp_tot[32];
   const Smem sm = carve_smem(smem_raw, p);
   const int HG = p.heads_per_cta, NCW = HG;
@@ -989,7 +997,73 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
     return;
   }
   if (warp > NCW) return;
-  consume_mma<T, D, BAL>(p, w, sm, warp, blockIdx.y * HG + warp, lane);
+  consume_mma<T, D, BAL>(p, w, sm, warp, blockIdx.y * HG + warp, lane);}
+
+template <typename T, int D, bool BAL>
+__global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
+    paged_decode_mma_kernel(const DecodeParams p) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  decode_mma_cta<T, D, BAL>(p, smem_raw);
+}
+
+// Shared-prefix role of a fused cascade launch: CTA x (x < nctas) runs the
+// (work item, KV head) pairs x, x + nctas, x + 2 nctas, ... of cp on the
+// tensor cores as two independent 128-thread pipelines (warps 0-3 take every
+// other pair, warps 4-7 the rest; each with its own shared-memory tiles,
+// mbarriers, 256 tensor-memory columns and named barrier), so that one
+// pipeline's loads and softmax overlap the other's. The ninth warp leaves.
+template <typename T, int D>
+__device__ void prefix_role(const CascadeParams& cp, int nctas, uint8_t* smem) {
+  constexpr int GT = kTcThreads;  // threads of one pipeline
+  const int tid = threadIdx.x;
+  if (tid >= 2 * GT) return;
+  const int grp = tid / GT, gtid = tid % GT;
+  const PrefixSmem sm = carve_prefix_smem<D>(smem + grp * prefix_item_smem_bytes<D>());
+  uint32_t* tmem_slot = carve_prefix_smem<D>(smem).tmem_slot;  // one allocation for both pipelines
+  if (tid < 32) tc::tmem_alloc(tmem_slot, 2 * kTcCols);
+  if (gtid == 0) {
+    mbar_init(&sm.bar[0], 1);
+    mbar_init(&sm.bar[1], 1);
+    fence_mbar_init();
+  }
+  tc::fence_before_thread_sync();
+  asm volatile("bar.sync 1, %0;" ::"n"(2 * GT) : "memory");
+  tc::fence_after_thread_sync();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t tmem = tmem_base + grp * kTcCols;
+  auto sync = [grp] {
+    if (grp == 0)
+      asm volatile("bar.sync 2, %0;" ::"n"(GT) : "memory");
+    else
+      asm volatile("bar.sync 3, %0;" ::"n"(GT) : "memory");
+  };
+  const int pairs = cp.num_work * cp.num_kv_heads;
+  uint32_t parity = 0;
+  for (int i = blockIdx.x + grp * nctas; i < pairs; i += 2 * nctas)
+    prefix_item<T, D>(cp, i / cp.num_kv_heads, i % cp.num_kv_heads, sm, tmem, parity, gtid, sync);
+  tc::fence_before_thread_sync();
+  asm volatile("bar.sync 1, %0;" ::"n"(2 * GT) : "memory");  // both pipelines are done with tensor memory
+  if (tid < 32) {
+    tc::fence_after_thread_sync();
+    tc::tmem_dealloc(tmem_base, 2 * kTcCols);
+  }
+}
+
+// Fused cascade launch, one CTA per SM: CTAs [0, p.range_first) attend every
+// prefix group over its shared pages (prefix_role), CTAs [p.range_first,
+// gridDim.x) stream every request's suffix pages with the balanced schedule
+// (KV append fused, log-sum-exp out), side by side on disjoint SMs;
+// cascade_merge_kernel follows.
+template <typename T, int D>
+__global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
+    cascade_fused_kernel(const DecodeParams p, const CascadeParams cp) {
+  extern __shared__ __align__(128) uint8_t smem_fused[];
+  if ((int)blockIdx.x < p.range_first) {
+    griddep_launch_dependents();
+    prefix_role<T, D>(cp, p.range_first, smem_fused);
+    return;
+  }
+  decode_mma_cta<T, D, true>(p, smem_fused);
 }
 
 // Split schedule: merge the chunks of every sequence that has more than one.
@@ -1138,6 +1212,63 @@ static cudaError_t launch_t(int head_dim, int gw, bool bal, const DecodeParams& 
     case 64: return launch_d<T, 64>(gw, bal, p, s, st);
     case 112: return launch_d<T, 112>(gw, bal, p, s, st);
     case 128: return launch_d<T, 128>(gw, bal, p, s, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <typename T, int D>
+static cudaError_t launch_fused_d(const DecodeParams& p, const CascadeParams& cp, const LaunchShape& s,
+                                  cudaStream_t stream) {
+  static int granted[64] = {0};
+  auto kern = cascade_fused_kernel<T, D>;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64 || granted[dev] < s.smem_bytes) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, s.smem_bytes);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) granted[dev] = s.smem_bytes;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = s.grid;
+  cfg.blockDim = s.block;
+  cfg.dynamicSmemBytes = s.smem_bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = s.overlap ? 1 : 0;
+  e = cudaLaunchKernelEx(&cfg, kern, p, cp);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t launch_fused_t(int head_dim, const DecodeParams& p, const CascadeParams& cp,
+                                  const LaunchShape& s, cudaStream_t stream) {
+  switch (head_dim) {
+    case 64: return launch_fused_d<T, 64>(p, cp, s, stream);
+    case 112: return launch_fused_d<T, 112>(p, cp, s, stream);
+    case 128: return launch_fused_d<T, 128>(p, cp, s, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+int fused_prefix_smem_bytes(int head_dim) {
+  switch (head_dim) {
+    case 64: return 2 * prefix_item_smem_bytes<64>();
+    case 112: return 2 * prefix_item_smem_bytes<112>();
+    case 128: return 2 * prefix_item_smem_bytes<128>();
+    default: return 1 << 30;
+  }
+}
+
+cudaError_t launch_cascade_fused(int dtype, int head_dim, const DecodeParams& p, const CascadeParams& cp,
+                                 const LaunchShape& shape, cudaStream_t stream) {
+  switch (dtype) {
+    case UBX_DTYPE_BF16: return launch_fused_t<__nv_bfloat16>(head_dim, p, cp, shape, stream);
+    case UBX_DTYPE_F16: return launch_fused_t<__half>(head_dim, p, cp, shape, stream);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -62,6 +62,8 @@ struct DecodeParams {
   int split_pages;       // split schedule: pages per chunk
   int max_chunks;        // split schedule: chunk slots per sequence
   int tail_trim;         // balanced schedule: pages fewer for the last CTA's range (0: equal shares)
+  int range_first;       // balanced schedule: first CTA of the page ranges (0; a fused cascade launch runs
+                         // its shared-prefix CTAs below it)
   float* part_o;         // [slots][num_heads][D] unnormalised partial outputs
   float2* part_ml;       // [slots][num_heads] (running max in log2 units, denominator)
   int32_t* counters;     // [batch][num_kv_heads * warps_per_kv] merge counters (balanced)
@@ -181,7 +183,8 @@ struct KvCopyParams {
 cudaError_t launch_kv_pages_copy(const KvCopyParams& p, cudaStream_t stream);
 
 // Shared-prefix (cascade) pass (cascade.cu).
-constexpr int kCascadeMaxPages = 8;      // shared pages one CTA holds in shared memory (128 tokens)
+constexpr int kCascadeMaxPages = 8;      // shared pages of one chunk in shared memory (128 tokens)
+constexpr int kCascadeMaxItemPages = 64; // shared pages of one work item (up to 8 chunks, one after another)
 constexpr int kCascadeWorkInts = 6;      // ints per work item
 constexpr int kCascadeRows = 128;        // (member, query head) rows of one work item: M of the MMAs
 constexpr int kCascadeMinSmem = 80 * 1024;  // at most two prefix CTAs per SM
@@ -220,6 +223,13 @@ struct CascadeMergeParams {
 };
 
 int cascade_smem_bytes(int head_dim);
+// One launch of a cascade step's suffix pass (DecodeParams, balanced schedule,
+// CTAs from p.range_first on) and shared-prefix pass (CTAs below p.range_first);
+// 16-bit pools, one CTA per SM (paged_decode.cu).
+cudaError_t launch_cascade_fused(int dtype, int head_dim, const DecodeParams& p, const CascadeParams& cp,
+                                 const LaunchShape& shape, cudaStream_t stream);
+// Shared memory the prefix CTAs of that launch need (two pipelines of tiles).
+int fused_prefix_smem_bytes(int head_dim);
 cudaError_t launch_cascade_prefix(int dtype, int head_dim, const CascadeParams& p, cudaStream_t stream);
 cudaError_t launch_cascade_merge(int dtype, int head_dim, const CascadeMergeParams& p, cudaStream_t stream);
 

@@ -56,6 +56,10 @@ SIGNATURES = {
                                             _i32, _i32, _i32, _i32, _i32, _f32, _i32, _vp, _sz, _vp, _i32, _vp]),
     "ubx_cascade_merge": (_i32, [_vp, _i64, _i64, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _sz, _vp, _i32,
                                  _vp]),
+    "ubx_cascade_attention": (_i32, [_vp, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _vp, _i64,
+                                     _vp, _vp, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i64, _i32, _f32, _i32,
+                                     _i32, _vp, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _vp, _vp, _sz, _vp, _sz,
+                                     _vp]),
     "ubx_kv_wire_header_init": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, _i32, ctypes.c_uint64]),
     "ubx_kv_wire_header_check": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, ctypes.c_uint64]),
     "ubx_kv_pages_copy": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i32, _i32,

@@ -68,6 +68,12 @@ class DecodeWorkspace:
     def nbytes(self) -> int:
         return 0 if self.buf is None else self.buf.numel()
 
+    @property
+    def num_sms(self) -> int:
+        if not hasattr(self, "_num_sms"):
+            self._num_sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        return self._num_sms
+
     def ensure(self, batch: int, num_heads: int, head_dim: int, max_blocks: int, split_pages: int = 0,
                num_kv_heads: int = 0, dtype: Optional[torch.dtype] = None):
         """Grow to what a call with these sizes needs."""
