@@ -667,6 +667,39 @@ int ubx_cascade_workspace_size(int batch, int num_heads, int head_dim, int max_c
 
 namespace {
 
+// A K or V pool as the prefix pass's 3-D tensor map: dimension 0 = the 8
+// elements of a 16-byte chunk, 1 = the chunks of all KV heads' rows (16 bytes
+// apart: heads are contiguous within a token row), 2 = every token of every
+// page (c_s_tok elements apart); box = one chunk column of one page. Returns
+// false when the driver's encoder is missing or refuses the layout (the pass
+// then copies with cp.async).
+bool encode_prefix_map(CUtensorMap* map, const void* pool, int dtype, int64_t num_blocks, int num_kv_heads,
+                       int head_dim, int64_t c_s_tok) {
+  using Encode = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static Encode fn = nullptr;
+  static bool looked = false;
+  if (!looked) {
+    looked = true;
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess && f)
+      fn = reinterpret_cast<Encode>(f);
+  }
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {8, (cuuint64_t)num_kv_heads * head_dim / 8, (cuuint64_t)num_blocks * kBlockSize};
+  const cuuint64_t strides[2] = {16, (cuuint64_t)c_s_tok * 2};  // bytes, dimensions 1 and 2
+  const cuuint32_t box[3] = {8, 1, (cuuint32_t)kBlockSize};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(map, dtype == UBX_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        3, const_cast<void*>(pool), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // Checks the shared-prefix pass's arguments and fills its launch parameters
 // (error word and overlap flag left to the caller).
 int make_cascade_params(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache, const void* v_cache,
@@ -718,6 +751,8 @@ int make_cascade_params(const void* q, int64_t q_s_b, int64_t q_s_h, const void*
   p.part_o = reinterpret_cast<float*>(ws + cascade_ml_bytes(batch, num_heads, max_chunks));
   p.error = nullptr;
   p.overlap = false;
+  p.use_tma = encode_prefix_map(&p.tmap_k, k_cache, dtype, num_blocks, num_kv_heads, head_dim, c_s_tok) &&
+              encode_prefix_map(&p.tmap_v, v_cache, dtype, num_blocks, num_kv_heads, head_dim, c_s_tok);
   return UBX_OK;
 }
 

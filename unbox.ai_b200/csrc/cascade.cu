@@ -34,7 +34,7 @@ namespace {
 
 // One work item per CTA (blockIdx.x: the item, blockIdx.y: the KV head).
 template <typename T, int D>
-__global__ void __launch_bounds__(kTcThreads) cascade_prefix_kernel(const CascadeParams p) {
+__global__ void __launch_bounds__(kTcThreads) cascade_prefix_kernel(const __grid_constant__ CascadeParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const PrefixSmem sm = carve_prefix_smem<D>(smem);
   const int tid = threadIdx.x;
@@ -47,6 +47,7 @@ __global__ void __launch_bounds__(kTcThreads) cascade_prefix_kernel(const Cascad
   if (tid == 0) {
     mbar_init(&sm.bar[0], 1);
     mbar_init(&sm.bar[1], 1);
+    mbar_init(&sm.bar[2], 1);
     fence_mbar_init();
   }
   tc::fence_before_thread_sync();

@@ -1024,6 +1024,7 @@ __device__ void prefix_role(const CascadeParams& cp, int nctas, uint8_t* smem) {
   if (gtid == 0) {
     mbar_init(&sm.bar[0], 1);
     mbar_init(&sm.bar[1], 1);
+    mbar_init(&sm.bar[2], 1);
     fence_mbar_init();
   }
   tc::fence_before_thread_sync();
@@ -1056,7 +1057,7 @@ __device__ void prefix_role(const CascadeParams& cp, int nctas, uint8_t* smem) {
 // cascade_merge_kernel follows.
 template <typename T, int D>
 __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
-    cascade_fused_kernel(const DecodeParams p, const CascadeParams cp) {
+    cascade_fused_kernel(const DecodeParams p, const __grid_constant__ CascadeParams cp) {
   extern __shared__ __align__(128) uint8_t smem_fused[];
   if ((int)blockIdx.x < p.range_first) {
     griddep_launch_dependents();

@@ -37,7 +37,7 @@ constexpr float kRescaleSlack = 8.f;
 //   K [D/8][128 tokens][16 B]     P [16 token chunks][128 rows][16 B] over K once S is done
 //   (gap: P needs 32 KB)
 //   V [D/8][128 tokens][16 B]
-//   tail: 2 mbarriers, the TMEM address, the item's page ids and member sequences
+//   tail: 3 mbarriers, the TMEM address, the item's page ids and member sequences
 // The partial rows are staged over Q, K and V at the end (rows of D floats + 16 B).
 template <int D>
 struct PrefixLayout {
@@ -58,7 +58,7 @@ constexpr int prefix_item_smem_bytes() {
 
 struct PrefixSmem {
   uint8_t* base;
-  uint64_t* bar;       // [2]: S complete, O complete
+  uint64_t* bar;       // [3]: S complete, O complete, K and V tiles landed (tensor-map copies)
   uint32_t* tmem_slot;
   int32_t* pg_s;       // [kCascadeMaxItemPages]
   int32_t* mem_s;      // [kTcRows]
@@ -70,7 +70,7 @@ __device__ __forceinline__ PrefixSmem carve_prefix_smem(uint8_t* smem) {
   PrefixSmem s;
   s.base = smem;
   s.bar = reinterpret_cast<uint64_t*>(smem + L::kTail);
-  s.tmem_slot = reinterpret_cast<uint32_t*>(s.bar + 2);
+  s.tmem_slot = reinterpret_cast<uint32_t*>(s.bar + 3);
   s.pg_s = reinterpret_cast<int32_t*>(smem + L::kTail + 64);
   s.mem_s = s.pg_s + kCascadeMaxItemPages;
   return s;
@@ -78,8 +78,10 @@ __device__ __forceinline__ PrefixSmem carve_prefix_smem(uint8_t* smem) {
 
 // Work item `wi` of p.work for KV head kvh on kTcThreads threads (tid = 0 ..
 // 127, one per tile row) that synchronise with sync(). The caller owns `tmem`
-// (kTcCols columns) and the two mbarriers of `sm`, initialised with one arrival
-// each; `parity` is the phase they are in, advanced here once per chunk. The
+// (kTcCols columns) and the three mbarriers of `sm`, initialised with one
+// arrival each; `parity` is the phase they are in, advanced here once per chunk.
+// With p.use_tma the K and V tiles come by tensor-map copies (p must then live
+// in kernel parameter space: a __grid_constant__ argument), else by cp.async. The
 // first chunk's pages are requested before griddepcontrol.wait, q and the
 // partial rows are touched after it. Ends with sync(): the next item may reuse
 // the shared memory and the tensor memory at once. Returns false, with the
@@ -110,10 +112,38 @@ __device__ bool prefix_item(const CascadeParams& p, int wi, int kvh, const Prefi
   for (int i = tid; i < n_mem; i += NTH) sm.mem_s[i] = __ldg(&p.member_list[m_off + i]);
   sync();
 
-  // K and V of chunk c (pages 8c ..): 16-byte pieces, 8 consecutive threads =
-  // 8 consecutive tokens of one 16-byte chunk (one core matrix)
+  // K and V of chunk c (pages 8c ..) into the tiles' canonical layout. Tensor
+  // maps: one box per (page, 16-byte chunk column) -- 16 tokens x 16 bytes --
+  // counted on bar[2]. cp.async: 16-byte pieces, 8 consecutive threads = 8
+  // consecutive tokens of one 16-byte chunk (one core matrix). A page outside
+  // the pool reads as zeros.
   bool bad_page = false;
   auto load_kv = [&](int c, int nt) {
+    const int npg = nt / 16;
+    if (p.use_tma) {
+      if (tid == 0) {
+        int valid = 0;
+        for (int i = 0; i < npg; ++i) {
+          const int page = sm.pg_s[c * kCascadeMaxPages + i];
+          valid += page >= 0 && (int64_t)page < p.num_blocks;
+        }
+        mbar_arrive_expect_tx(&sm.bar[2], (uint32_t)(valid * 2 * CH * 256));
+      }
+      sync();  // the byte count is posted before any box can land
+      for (int j = tid; j < npg * 2 * CH; j += NTH) {
+        const int pc = j / (2 * CH), is_v = (j / CH) & 1, cc = j % CH;
+        uint8_t* dst = (is_v ? v_s : k_s) + (cc * TT + pc * 16) * 16;
+        const int page = sm.pg_s[c * kCascadeMaxPages + pc];
+        if (page >= 0 && (int64_t)page < p.num_blocks) {
+          tma_load_3d(dst, is_v ? &p.tmap_v : &p.tmap_k, 0, kvh * CH + cc, page * 16, &sm.bar[2]);
+        } else {
+          if (cc == 0 && !is_v) bad_page = true;
+#pragma unroll
+          for (int r = 0; r < 16; ++r) reinterpret_cast<uint4*>(dst)[r] = make_uint4(0, 0, 0, 0);
+        }
+      }
+      return;
+    }
     for (int v = tid; v < 2 * nt * CH; v += NTH) {
       const int is_v = v >= nt * CH;
       const int u = is_v ? v - nt * CH : v;
@@ -158,6 +188,7 @@ __device__ bool prefix_item(const CascadeParams& p, int wi, int kvh, const Prefi
     const int NT = min(n_pg - c * kCascadeMaxPages, kCascadeMaxPages) * 16;  // tokens: N of S, K of O
     if (c > 0) load_kv(c, NT);  // the previous chunk's O = P V has completed: P (over K) and V are free
     cp_async_commit_wait_all();
+    if (p.use_tma) ok = mbar_wait_bounded(&sm.bar[2], parity) && ok;
     fence_proxy_async_smem();  // these generic-proxy writes before the MMAs' reads
     tc::fence_before_thread_sync();
     sync();

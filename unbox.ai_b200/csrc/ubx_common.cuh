@@ -144,6 +144,26 @@ __device__ __forceinline__ void bulk_copy_g2s_hint(void* smem_dst, const void* g
       : "memory");
 }
 
+// Tiled tensor copy global -> shared (TMA engine) of the box at coordinates
+// (c0, c1, c2) of a 3-D tensor map, completing `bytes` on the mbarrier. The map
+// lives in kernel parameter space (a __grid_constant__ argument). c0 times the
+// element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* map, int c0, int c1, int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];"
+      ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2),
+        "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Asks L2 to fetch `bytes` of global memory (TMA engine, no shared memory, no
+// completion to wait for). Address 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* gmem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(gmem_src)), "r"(bytes)
+               : "memory");
+}
+
 // Bulk copy shared -> global (TMA engine, non-tensor), tracked in the issuing
 // thread's bulk async-groups. Both addresses 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_copy_s2g(void* gmem_dst, const void* smem_src, uint32_t bytes) {

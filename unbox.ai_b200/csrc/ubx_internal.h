@@ -190,6 +190,13 @@ constexpr int kCascadeRows = 128;        // (member, query head) rows of one wor
 constexpr int kCascadeMinSmem = 80 * 1024;  // at most two prefix CTAs per SM
 
 struct CascadeParams {
+  // K and V pools as 3-D tensor maps (8 elements of a 16-byte chunk, the chunks
+  // of every KV head's row, the tokens of every page): a box is one 16-byte
+  // chunk column of one page (16 tokens), the layout of the operand tiles.
+  // Filled, and use_tma set, when the driver encodes them.
+  CUtensorMap tmap_k;
+  CUtensorMap tmap_v;
+  int use_tma;
   const void* q;
   int64_t q_sb, q_sh;
   const void* k_cache;
