@@ -689,6 +689,23 @@ bool encode_prefix_map(CUtensorMap* map, const void* pool, int dtype, int64_t nu
       fn = reinterpret_cast<Encode>(f);
   }
   if (!fn) return false;
+  // the decode loop asks for the same pools every step: remember the last maps
+  struct Entry {
+    const void* pool;
+    int dtype, kv_heads, head_dim;
+    int64_t num_blocks, c_s_tok;
+    CUtensorMap map;
+  };
+  static thread_local Entry cache[64];
+  static thread_local int cache_n = 0, cache_next = 0;
+  for (int i = 0; i < cache_n; ++i) {
+    const Entry& c = cache[i];
+    if (c.pool == pool && c.dtype == dtype && c.kv_heads == num_kv_heads && c.head_dim == head_dim &&
+        c.num_blocks == num_blocks && c.c_s_tok == c_s_tok) {
+      *map = c.map;
+      return true;
+    }
+  }
   const cuuint64_t dims[3] = {8, (cuuint64_t)num_kv_heads * head_dim / 8, (cuuint64_t)num_blocks * kBlockSize};
   const cuuint64_t strides[2] = {16, (cuuint64_t)c_s_tok * 2};  // bytes, dimensions 1 and 2
   const cuuint32_t box[3] = {8, 1, (cuuint32_t)kBlockSize};
@@ -697,7 +714,11 @@ bool encode_prefix_map(CUtensorMap* map, const void* pool, int dtype, int64_t nu
                         3, const_cast<void*>(pool), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
+  if (r != CUDA_SUCCESS) return false;
+  cache[cache_next] = Entry{pool, dtype, num_kv_heads, head_dim, num_blocks, c_s_tok, *map};
+  cache_next = (cache_next + 1) % 64;
+  if (cache_n < 64) ++cache_n;
+  return true;
 }
 
 // Checks the shared-prefix pass's arguments and fills its launch parameters
