@@ -61,6 +61,7 @@ class CascadePlan:
     prefix_chunks: int = 0             # 8-page chunks of all work items (host count)
     _lse: Optional[torch.Tensor] = None
     _ws: Optional[torch.Tensor] = None
+    _split: dict = field(default_factory=dict)  # per-plan host caches: SM split, workspace sizing
 
     @property
     def num_work(self) -> int:
@@ -219,14 +220,19 @@ def paged_attention_cascade(q: torch.Tensor, k_cache: torch.Tensor, v_cache: tor
     lib = _L.load()
     if plan._lse is None or plan._lse.shape != (B, H) or plan._lse.device != dev:
         plan._lse = torch.empty((B, H), dtype=torch.float32, device=dev)
-    need = ctypes.c_size_t(0)
-    _L.check(lib.ubx_cascade_workspace_size(B, H, D, plan.max_chunks, ctypes.byref(need)), "cascade workspace")
-    if plan._ws is None or plan._ws.numel() < need.value or plan._ws.device != dev:
-        plan._ws = torch.empty(max(int(need.value), 256), dtype=torch.uint8, device=dev)
+    if plan._ws is None or plan._ws.device != dev or plan._split.get("ws") != (B, H, D):
+        need = ctypes.c_size_t(0)
+        _L.check(lib.ubx_cascade_workspace_size(B, H, D, plan.max_chunks, ctypes.byref(need)), "cascade workspace")
+        if plan._ws is None or plan._ws.numel() < need.value or plan._ws.device != dev:
+            plan._ws = torch.empty(max(int(need.value), 256), dtype=torch.uint8, device=dev)
+        plan._split["ws"] = (B, H, D)
     dws = workspace_for(dev)
     buf = dws.ensure(B, H, D, sbt.shape[1], 0, KVH, q.dtype)
     if prefix_ctas is None:
-        prefix_ctas = prefix_ctas_for(plan, KVH, dws.num_sms)
+        key = (KVH, dws.num_sms)
+        if key not in plan._split:
+            plan._split[key] = prefix_ctas_for(plan, KVH, dws.num_sms)
+        prefix_ctas = plan._split[key]
     if k_new is not None:
         _require_cuda(q, k_new, v_new)
         if k_new.shape != (B, KVH, D) or v_new.shape != k_new.shape or k_new.dtype != q.dtype or \

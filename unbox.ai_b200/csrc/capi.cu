@@ -472,9 +472,10 @@ int decode_impl(const void* q, int64_t q_s_b, int64_t q_s_h, const void* k_cache
   int sms = 0;
   st = num_sms_current_device(&sms);
   if (st != UBX_OK) return st;
-  // The log-sum-exp variant is the cascade's suffix pass: its prefix and merge
-  // launches follow with programmatic overlap, so leave their CTAs room.
-  const int reserve = lse ? kCascadeFollowerSmem : 0;
+  // The log-sum-exp variant is the cascade's suffix pass: when its prefix and
+  // merge launches follow with programmatic overlap, leave their CTAs room (the
+  // one-launch step keeps every stage: only the merge follows it).
+  const int reserve = (lse && !(fuse && prefix_ctas > 0)) ? kCascadeFollowerSmem : 0;
   Plan pl;
   st = make_plan(batch, num_heads, num_kv_heads, head_dim, dtype, max_blocks_per_seq, schedule, split_pages, sms, &pl,
                  reserve);
