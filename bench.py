@@ -119,9 +119,10 @@ def peaks():
         return 6650.0, "fallback"
 
 
-def profiled_traffic(workload: str):
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary (or None)."""
-    path = os.path.join(ROOT, "profiles", f"paged_decode_{workload}.md")
+def profiled_traffic(summary: str):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary
+    profiles/<summary>.md (or None)."""
+    path = os.path.join(ROOT, "profiles", f"{summary}.md")
     try:
         for line in open(path):
             if line.startswith("traffic_bytes_per_launch:"):
@@ -1178,7 +1179,8 @@ def main():
                                        "between launches (the engine's eager loop)"}
     achieved = kernel_bytes / (kernel_avg_ms / 1e3) / 1e9
     line["roofline"] = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                        "frac": round(achieved / peak, 4), "traffic": profiled_traffic(args.workload),
+                        "frac": round(achieved / peak, 4), "traffic": profiled_traffic(f"cascade_{args.workload}" if args.cascade
+                                                               else f"paged_decode_{args.workload}"),
                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                         else "fallback 6650 GB/s",
                         "kernel": ("cascade layer-call: cascade_fused_kernel (suffix pages, KV append fused, and "
