@@ -32,7 +32,9 @@ unbox_platform/infer/kvcache.py of the reference):
   k_cache, v_cache, block_table, context_lens, eps)`` -- norm, rotary, append
   and attention of one decode layer (engine.py:201-224) in one launch.
 * ``prefill_kv_write`` / ``prefill_prep`` -- a prefill chunk's KV write
-  (engine.py:126-128), alone or with its norm and rotary steps (:121-128).
+  (engine.py:126-128), alone or with its norm and rotary steps (:121-128);
+  ``prefill_positions_and_slots`` computes the chunk's positions and slots once
+  per step for all layers.
 * ``rope_table(head_dim, num_positions, theta)`` -- the (cos, sin) table of
   precompute_freqs_cis (model.py:30-34).
 * ``plan_cascade(block_table, context_lens, H, KVH)`` /
@@ -48,15 +50,15 @@ from . import workloads  # noqa: F401  (pure Python, no CUDA needed)
 __all__ = [
     "paged_decode_attention", "paged_attention", "paged_attention_split", "kv_append",
     "slot_mapping", "DecodeWorkspace", "workloads", "library", "sharding", "qk_norm_rope",
-    "paged_decode_prep_attention", "prefill_kv_write", "prefill_prep", "prefill_slots", "rope_table", "handoff",
-    "cascade", "plan_cascade", "paged_attention_cascade",
+    "paged_decode_prep_attention", "prefill_kv_write", "prefill_prep", "prefill_slots",
+    "prefill_positions_and_slots", "rope_table", "handoff", "cascade", "plan_cascade", "paged_attention_cascade",
 ]
 
 
 _OPS = ("paged_decode_attention", "paged_attention", "paged_attention_split", "kv_append", "slot_mapping",
         "DecodeWorkspace", "check_device_errors", "workspace_for", "paged_decode_append_attention",
         "qk_norm_rope", "paged_decode_prep_attention", "prefill_kv_write", "prefill_prep", "prefill_slots",
-        "rope_table")
+        "prefill_positions_and_slots", "rope_table")
 
 
 def __getattr__(name):

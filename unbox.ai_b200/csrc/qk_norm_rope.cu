@@ -11,6 +11,8 @@
 // write: kvcache.py:330-340). One warp handles one (token, head) row at a time (a
 // block per token, its warps over the heads); the warps
 // of K heads also store the token's K and V rows into the pool.
+#include <algorithm>
+
 #include "ubx_common.cuh"
 #include "ubx_internal.h"
 #include "ubx_prep.cuh"
@@ -134,11 +136,135 @@ __global__ void __launch_bounds__(kPrepWarps * 32) qk_norm_rope_kernel(const Pre
   }
 }
 
+// 16-bit rows with 16-byte-aligned rows and a head_dim that is a multiple of 8:
+// each lane takes one 16-byte chunk (8 elements, 4 rotary pairs) of a row, the
+// CH = head_dim / 8 lanes of a row sit in a segment of W lanes (W the power of
+// two >= CH), so a warp works on 32 / W rows at once and a row's sum of squares
+// is a W-lane butterfly. A block is one token (grid-stride), its warps over the
+// token's q and k rows; every load of a row (x, weight, rotary pairs, the V row)
+// is issued before the sum is reduced. Same rounding points as
+// qk_norm_rope_kernel.
+constexpr int kVecTokens = 2;
+
+template <typename T, int W>
+__global__ void __launch_bounds__(kPrepWarps * 32) qk_norm_rope_vec_kernel(const PrepParams p) {
+  constexpr int RPW = 32 / W;  // rows of one warp at a time
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int seg = lane / W, c = lane % W;
+  const int CH = p.head_dim / 8;
+  const int rows_per_token = p.num_heads + p.num_kv_heads;
+  const float inv_d = 1.f / (float)p.head_dim;
+  const int64_t limit = p.num_blocks * p.block_size;
+  const int bs_shift = (p.block_size & (p.block_size - 1)) == 0 ? __ffs(p.block_size) - 1 : -1;
+  // kVecTokens tokens per block and pass over their rows together, so that every
+  // warp has a row set on every pass
+  const int rows = kVecTokens * rows_per_token;
+  for (int64_t t0 = (int64_t)blockIdx.x * kVecTokens; t0 < p.num_tokens; t0 += (int64_t)gridDim.x * kVecTokens) {
+    for (int r0 = warp * RPW; r0 < rows; r0 += nwarps * RPW) {
+      const int r = r0 + seg;
+      const int64_t t = t0 + r / rows_per_token;
+      const int h = r % rows_per_token;
+      const bool live = c < CH && r < rows && t < p.num_tokens;  // segment-uniform
+      const int pos = live ? __ldg(&p.positions[t]) : 0;
+      const bool pos_ok = pos >= 0 && pos < p.rope_n;
+      if (live && !pos_ok && c == 0 && h == 0) set_error(p.error, kErrBadPosition);
+      const int64_t slot = (live && p.k_cache) ? __ldg(&p.slots[t]) : -1;
+      const float4* rope_row = reinterpret_cast<const float4*>(p.rope + (int64_t)(pos_ok ? pos : 0) * p.rope_sp);
+      const bool is_q = h < p.num_heads;
+      const int hk = h - p.num_heads;
+      const bool to_cache = !is_q && slot >= 0 && slot < limit;
+      float x[8], w[8];
+      float4 cs[2] = {make_float4(1.f, 0.f, 1.f, 0.f), make_float4(1.f, 0.f, 1.f, 0.f)};
+      uint4 vrow = make_uint4(0, 0, 0, 0);
+      float ss = 0.f;
+      if (live) {
+        const T* src = is_q ? static_cast<const T*>(p.q_in) + t * p.q_st + (int64_t)h * p.q_sh
+                            : static_cast<const T*>(p.k_in) + t * p.k_st + (int64_t)hk * p.k_sh;
+        const uint4 xr = __ldg(reinterpret_cast<const uint4*>(src) + c);
+        const uint4 wr = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(is_q ? p.q_w : p.k_w)) + c);
+        if (pos_ok) {
+          cs[0] = __ldg(rope_row + 2 * c);
+          cs[1] = __ldg(rope_row + 2 * c + 1);
+        }
+        if (to_cache)
+          vrow = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(p.v_in) + t * p.v_st +
+                                                      (int64_t)hk * p.v_sh) + c);
+        Elem<T>::unpack(xr, x);
+        Elem<T>::unpack(wr, w);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss += rounded_square<T>(x[e]);
+      }
+#pragma unroll
+      for (int off = W / 2; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      if (!live) continue;
+      const float rf = rms_factor<T>(ss, inv_d, p.eps);
+      float out[8];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const int e = 4 * j + 2 * k;
+          const float y0 = rms_apply<T>(x[e], rf, w[e]), y1 = rms_apply<T>(x[e + 1], rf, w[e + 1]);
+          const float2 o = rotate_pair(y0, y1, k ? cs[j].z : cs[j].x, k ? cs[j].w : cs[j].y);
+          out[e] = round_to<T>(o.x);
+          out[e + 1] = round_to<T>(o.y);
+        }
+      }
+      const uint4 packed = Elem<T>::pack(out);
+      if (is_q) {
+        reinterpret_cast<uint4*>(static_cast<T*>(p.q_out) + t * p.qo_st + (int64_t)h * p.qo_sh)[c] = packed;
+        continue;
+      }
+      if (p.k_out) reinterpret_cast<uint4*>(static_cast<T*>(p.k_out) + t * p.ko_st + (int64_t)hk * p.ko_sh)[c] = packed;
+      if (p.k_cache && slot >= limit && c == 0 && hk == 0) set_error(p.error, kErrBadSlot);
+      if (to_cache) {
+        const int64_t blk = bs_shift >= 0 ? slot >> bs_shift : slot / p.block_size;
+        const int64_t off = blk * p.c_sblk + (slot - blk * p.block_size) * p.c_stok + (int64_t)hk * p.c_sh;
+        reinterpret_cast<uint4*>(static_cast<T*>(p.k_cache) + off)[c] = packed;
+        reinterpret_cast<uint4*>(static_cast<T*>(p.v_cache) + off)[c] = vrow;
+      }
+    }
+  }
+}
+
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+// Rows, strides, weights and rotary rows on 16-byte boundaries, head_dim a
+// multiple of 8 (at most 256): the 16-byte-per-lane kernel applies.
+bool vec_ok(const PrepParams& p) {
+  const auto m8 = [](int64_t s) { return (s & 7) == 0; };  // element strides of 16-bit rows
+  bool ok = p.head_dim % 8 == 0 && p.head_dim <= 256 && aligned16(p.q_in) && aligned16(p.k_in) &&
+            aligned16(p.q_out) && aligned16(p.q_w) && aligned16(p.k_w) && aligned16(p.rope) &&
+            (p.rope_sp & 3) == 0 && m8(p.q_st) && m8(p.q_sh) && m8(p.k_st) && m8(p.k_sh) && m8(p.qo_st) &&
+            m8(p.qo_sh);
+  if (p.k_out) ok = ok && aligned16(p.k_out) && m8(p.ko_st) && m8(p.ko_sh);
+  if (p.k_cache)
+    ok = ok && aligned16(p.k_cache) && aligned16(p.v_cache) && aligned16(p.v_in) && m8(p.c_sblk) && m8(p.c_stok) &&
+         m8(p.c_sh) && m8(p.v_st) && m8(p.v_sh);
+  return ok;
+}
+
+template <typename T>
+cudaError_t launch_vec(const PrepParams& p, int blocks, cudaStream_t stream) {
+  const int ch = p.head_dim / 8;
+  const int w = ch <= 8 ? 8 : ch <= 16 ? 16 : 32;
+  const dim3 block(kPrepWarps * 32);
+  if (w == 8) qk_norm_rope_vec_kernel<T, 8><<<blocks, block, 0, stream>>>(p);
+  else if (w == 16) qk_norm_rope_vec_kernel<T, 16><<<blocks, block, 0, stream>>>(p);
+  else qk_norm_rope_vec_kernel<T, 32><<<blocks, block, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_qk_norm_rope(int dtype, const PrepParams& p, cudaStream_t stream) {
   if (p.num_tokens == 0) return cudaSuccess;
   const int blocks = (int)(p.num_tokens < 148 * 32 ? p.num_tokens : 148 * 32);  // a block per token
+  if (dtype != 0 && vec_ok(p)) {
+    const int64_t vb = (p.num_tokens + kVecTokens - 1) / kVecTokens;
+    const int vblocks = (int)(vb < 148 * 32 ? vb : 148 * 32);
+    return dtype == 1 ? launch_vec<__nv_bfloat16>(p, vblocks, stream) : launch_vec<__half>(p, vblocks, stream);
+  }
   switch (dtype) {
     case 0: qk_norm_rope_kernel<float><<<blocks, kPrepWarps * 32, 0, stream>>>(p); break;
     case 1: qk_norm_rope_kernel<__nv_bfloat16><<<blocks, kPrepWarps * 32, 0, stream>>>(p); break;

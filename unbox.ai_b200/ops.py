@@ -542,19 +542,31 @@ def prefill_kv_write(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_
     return slots
 
 
-def prefill_prep(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor,
-                 rope: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table_row: torch.Tensor,
-                 start_pos: int, eps: float = 1e-6):
-    """A prefill chunk's q_norm / k_norm / rotary embedding at positions
-    start_pos.. and its KV write (engine.py:121-128) in one launch (plus the slot
-    computation). Returns (q_rot, k_rot) for the chunk's own attention."""
-    T = q.shape[0]
-    dev = _require_cuda(q)
-    positions = torch.arange(start_pos, start_pos + T, dtype=torch.int32, device=dev)
+def prefill_positions_and_slots(block_table_row: torch.Tensor, start_pos: int, num_tokens: int,
+                                block_size: int = 16):
+    """Positions start_pos .. and their KV slots for a prefill chunk; the same for
+    every layer of the step, so computed once and passed to ``prefill_prep``."""
     row = _int32(block_table_row, "block_table_row").contiguous()
     if row.dim() != 1:
         raise ValueError("block_table_row must be 1-D")
-    # the same positions feed the slot computation and the kernel (one arange)
-    slots = slot_mapping(row.unsqueeze(0).expand(T, -1), positions, k_cache.shape[1])
+    positions = torch.arange(start_pos, start_pos + num_tokens, dtype=torch.int32, device=row.device)
+    return positions, slot_mapping(row.unsqueeze(0).expand(num_tokens, -1), positions, block_size)
+
+
+def prefill_prep(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor,
+                 rope: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table_row: torch.Tensor,
+                 start_pos: int, eps: float = 1e-6, positions_and_slots=None):
+    """A prefill chunk's q_norm / k_norm / rotary embedding at positions
+    start_pos.. and its KV write (engine.py:121-128) in one launch (plus the slot
+    computation, unless ``positions_and_slots`` -- from
+    ``prefill_positions_and_slots``, once per step -- is given). Returns (q_rot,
+    k_rot) for the chunk's own attention."""
+    T = q.shape[0]
+    _require_cuda(q)
+    if positions_and_slots is None:
+        positions_and_slots = prefill_positions_and_slots(block_table_row, start_pos, T, k_cache.shape[1])
+    positions, slots = positions_and_slots
+    if positions.shape != (T,) or slots.shape != (T,):
+        raise ValueError(f"positions and slots must hold the chunk's {T} tokens")
     return qk_norm_rope(q, k, q_weight, k_weight, rope, positions, eps, v=v, k_cache=k_cache, v_cache=v_cache,
                         slot_mapping=slots)
