@@ -1,5 +1,5 @@
-"""Time the reference's own CPU path for one decode layer-call. TEST / BASELINE
-INFRASTRUCTURE ONLY (nothing in the library imports it).
+"""Time the reference's own CPU path for one decode layer-call. Test and
+CPU-baseline infrastructure only (nothing in the library imports it).
 
 The reference's only working decode-attention path is the Python
 ``paged_decode_attention_ref`` (unbox_platform/infer/kernels/
