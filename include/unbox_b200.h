@@ -279,8 +279,8 @@ int ubx_paged_decode_attention_lse(const void* k_new, const void* v_new, int64_t
  *   page_list:   int32, the shared page ids of every group, concatenated
  *   member_list: int32, the member sequences of every group, concatenated
  *   work_items:  int32 [num_work_items][6] = (member offset, member count, page
- *                offset, page count <= 8, chunk index < max_chunks, 0); member
- *                count * (num_heads / num_kv_heads) <= 128
+ *                offset, page count <= 64 (taken 8 at a time), chunk index <
+ *                max_chunks, 0); member count * (num_heads / num_kv_heads) <= 128
  *   merge_items: int32 [num_merge_items][2] = (sequence, number of its prefix chunks)
  *   cascade_ws:  ubx_cascade_workspace_size bytes, 16-byte aligned (no initialisation needed)
  *   flags:       UBX_FLAG_OVERLAP_PREVIOUS = programmatic dependent launch: the

@@ -88,6 +88,37 @@ def test_cascade_one_launch_split_of_sms(prefix_ctas, pkg, oracle):
     close(out, ref)
 
 
+@pytest.mark.parametrize("prefix_ctas", [0, 20])
+def test_members_with_empty_suffix(prefix_ctas, pkg, oracle):
+    """Group members whose suffix is empty (their context ends with the shared
+    pages): the result is their attention over the shared pages alone, and the
+    suffix log-sum-exp reads -inf."""
+    wl = pkg.workloads
+    lay = wl.layout_radix_prefix(95, batch=40, prefix_pages=24, suffix_lo=1, suffix_hi=120)
+    t = wl.materialize_host(lay, 95, dtype="bfloat16", value_scale=0.7)
+    d = to_dev(t)
+    plan = pkg.plan_cascade(lay.block_table, lay.context_lens, 16, 8, device=DEV)
+    assert plan.num_work > 0
+    members = sorted(b for mem, _ in plan.groups for b in mem)
+    shared = {b: len(pages) for mem, pages in plan.groups for b in mem}
+    empty = members[::3]
+    sctx = plan.suffix_context_lens.cpu()
+    ctx = t["context_lens"].clone()
+    for b in empty:
+        sctx[b] = 0
+        ctx[b] = shared[b] * 16
+    plan.suffix_context_lens = sctx.to(DEV)
+    out = pkg.paged_attention_cascade(d["q"], d["k_cache"], d["v_cache"], plan, prefix_ctas=prefix_ctas)
+    torch.cuda.synchronize()
+    pkg.check_device_errors()
+    ref, st = oracle.paged_decode_attention(t["q"], t["k_cache"], t["v_cache"], t["block_table"], ctx)
+    assert st == 0
+    close(out, ref)
+    lse = plan._lse.cpu()
+    assert torch.isinf(lse[empty]).all() and (lse[empty] < 0).all()
+    assert torch.isfinite(lse[[b for b in members if b not in empty]]).all()
+
+
 def test_cascade_two_groups_and_unshared_requests(pkg, oracle):
     """Two prefix groups side by side with requests that share nothing: the
     unshared ones go through the suffix pass alone."""
