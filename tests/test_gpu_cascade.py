@@ -119,6 +119,33 @@ def test_members_with_empty_suffix(prefix_ctas, pkg, oracle):
     assert torch.isfinite(lse[[b for b in members if b not in empty]]).all()
 
 
+@pytest.mark.parametrize("prefix_ctas", [0, 24])
+def test_cascade_pool_with_interleaved_pages(prefix_ctas, pkg, oracle):
+    """K and V pages interleaved in one allocation, (pages, 2, 16, KVH, D): the
+    page stride is twice 16 token rows, so the shared pages are copied by
+    address (page stride, token stride), not as one run of rows; with the
+    append, pools bit-exact, output within tolerance."""
+    wl = pkg.workloads
+    lay = wl.layout_radix_prefix(97, batch=48, prefix_pages=26, suffix_lo=1, suffix_hi=200)
+    t = wl.materialize_host(lay, 97, dtype="bfloat16", value_scale=0.7)
+    d = to_dev(t)
+    kv = torch.stack([d["k_cache"], d["v_cache"]], dim=1).contiguous()
+    kc_dev, vc_dev = kv[:, 0], kv[:, 1]
+    assert kc_dev.stride(0) == 2 * kc_dev.stride(1) * kc_dev.shape[1]
+    plan = pkg.plan_cascade(lay.block_table, lay.context_lens, 16, 8, device=DEV)
+    assert plan.num_work > 0
+    out = pkg.paged_attention_cascade(d["q"], kc_dev, vc_dev, plan, k_new=d["k_new"], v_new=d["v_new"],
+                                      prefix_ctas=prefix_ctas)
+    torch.cuda.synchronize()
+    pkg.check_device_errors()
+    kc, vc = t["k_cache"].clone(), t["v_cache"].clone()
+    oracle.kv_append(t["k_new"], t["v_new"], kc, vc, t["slot_mapping"])
+    assert torch.equal(kc_dev.cpu(), kc) and torch.equal(vc_dev.cpu(), vc)
+    ref, st = oracle.paged_decode_attention(t["q"], kc, vc, t["block_table"], t["context_lens"])
+    assert st == 0
+    close(out, ref)
+
+
 def test_cascade_two_groups_and_unshared_requests(pkg, oracle):
     """Two prefix groups side by side with requests that share nothing: the
     unshared ones go through the suffix pass alone."""

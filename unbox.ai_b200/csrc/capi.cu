@@ -773,7 +773,10 @@ int make_cascade_params(const void* q, int64_t q_s_b, int64_t q_s_h, const void*
   p.part_o = reinterpret_cast<float*>(ws + cascade_ml_bytes(batch, num_heads, max_chunks));
   p.error = nullptr;
   p.overlap = false;
-  p.use_tma = encode_prefix_map(&p.tmap_k, k_cache, dtype, num_blocks, num_kv_heads, head_dim, c_s_tok) &&
+  // the tensor maps address token t of page g as row 16 g + t at one stride:
+  // packed pages only (a padded or interleaved pool copies with cp.async)
+  p.use_tma = c_s_block == (int64_t)kBlockSize * c_s_tok &&
+              encode_prefix_map(&p.tmap_k, k_cache, dtype, num_blocks, num_kv_heads, head_dim, c_s_tok) &&
               encode_prefix_map(&p.tmap_v, v_cache, dtype, num_blocks, num_kv_heads, head_dim, c_s_tok);
   return UBX_OK;
 }
