@@ -162,8 +162,12 @@ __global__ void __launch_bounds__(kPrepWarps * 32) qk_norm_rope_vec_kernel(const
   for (int64_t t0 = (int64_t)blockIdx.x * kVecTokens; t0 < p.num_tokens; t0 += (int64_t)gridDim.x * kVecTokens) {
     for (int r0 = warp * RPW; r0 < rows; r0 += nwarps * RPW) {
       const int r = r0 + seg;
-      const int64_t t = t0 + r / rows_per_token;
-      const int h = r % rows_per_token;
+      int h = r, ti = 0;  // (token, head) of row r, without an integer division
+      while (h >= rows_per_token) {
+        h -= rows_per_token;
+        ++ti;
+      }
+      const int64_t t = t0 + ti;
       const bool live = c < CH && r < rows && t < p.num_tokens;  // segment-uniform
       const int pos = live ? __ldg(&p.positions[t]) : 0;
       const bool pos_ok = pos >= 0 && pos < p.rope_n;
@@ -192,22 +196,33 @@ __global__ void __launch_bounds__(kPrepWarps * 32) qk_norm_rope_vec_kernel(const
         Elem<T>::unpack(xr, x);
         Elem<T>::unpack(wr, w);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) ss += rounded_square<T>(x[e]);
+        for (int e = 0; e < 8; e += 2) {  // rounded squares, summed in element order
+          float s0 = __fmul_rn(x[e], x[e]), s1 = __fmul_rn(x[e + 1], x[e + 1]);
+          round2<T>(s0, s1);
+          ss += s0;
+          ss += s1;
+        }
       }
 #pragma unroll
       for (int off = W / 2; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
       if (!live) continue;
       const float rf = rms_factor<T>(ss, inv_d, p.eps);
+      // (x * r) * w with each product rounded (pairwise: the values of
+      // rms_apply), the rotation, and the output rounded once by the packing
       float out[8];
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
           const int e = 4 * j + 2 * k;
-          const float y0 = rms_apply<T>(x[e], rf, w[e]), y1 = rms_apply<T>(x[e + 1], rf, w[e + 1]);
+          float y0 = __fmul_rn(x[e], rf), y1 = __fmul_rn(x[e + 1], rf);
+          round2<T>(y0, y1);
+          y0 = __fmul_rn(y0, w[e]);
+          y1 = __fmul_rn(y1, w[e + 1]);
+          round2<T>(y0, y1);
           const float2 o = rotate_pair(y0, y1, k ? cs[j].z : cs[j].x, k ? cs[j].w : cs[j].y);
-          out[e] = round_to<T>(o.x);
-          out[e + 1] = round_to<T>(o.y);
+          out[e] = o.x;
+          out[e + 1] = o.y;
         }
       }
       const uint4 packed = Elem<T>::pack(out);

@@ -30,6 +30,26 @@ __device__ __forceinline__ float round_to<__nv_bfloat16>(float x) { return __bfl
 template <>
 __device__ __forceinline__ float round_to<__half>(float x) { return __half2float(__float2half_rn(x)); }
 
+// Rounds two values to the dtype at once (one packed conversion, then back to
+// fp32): the same values as round_to on each.
+template <typename T>
+__device__ __forceinline__ void round2(float& a, float& b);
+template <>
+__device__ __forceinline__ void round2<float>(float&, float&) {}
+template <>
+__device__ __forceinline__ void round2<__nv_bfloat16>(float& a, float& b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  const uint32_t r = *reinterpret_cast<uint32_t*>(&h);
+  a = __uint_as_float(r << 16);
+  b = __uint_as_float(r & 0xffff0000u);
+}
+template <>
+__device__ __forceinline__ void round2<__half>(float& a, float& b) {
+  const float2 f = __half22float2(__floats2half2_rn(a, b));
+  a = f.x;
+  b = f.y;
+}
+
 // x.pow(2) of one element (the product is not fused into the running sum)
 template <typename T>
 __device__ __forceinline__ float rounded_square(float x) { return round_to<T>(__fmul_rn(x, x)); }
