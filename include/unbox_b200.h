@@ -286,10 +286,12 @@ int ubx_paged_decode_attention_lse(const void* k_new, const void* v_new, int64_t
  *   flags:       UBX_FLAG_OVERLAP_PREVIOUS = programmatic dependent launch: the
  *                kernel may start while the previous kernel on the stream drains.
  *                The prefix pass then loads its shared pages before waiting for
- *                that kernel (the caller promises it writes neither those pages
- *                nor page_list / member_list / work_items, which holds for the
- *                suffix pass of step 1: its append lands in private pages); q, the
- *                workspace and the outputs are touched only after the wait.
+ *                that kernel, and the merge reads merge_items before it (the
+ *                caller promises that kernel writes neither those pages nor
+ *                page_list / member_list / work_items / merge_items, which holds
+ *                for the suffix pass of step 1: its append lands in private
+ *                pages); q, the workspace and the outputs are touched only after
+ *                the wait.
  * bf16/f16, head_dim 64/112/128, page 16, GQA 1/2/4/8.
  */
 int ubx_cascade_workspace_size(int batch, int num_heads, int head_dim, int max_chunks, size_t* bytes);

@@ -68,13 +68,12 @@ __global__ void __launch_bounds__(kTcThreads) cascade_prefix_kernel(const __grid
 constexpr int kMergeBatch = 8;
 
 template <typename T, int D>
-__device__ __forceinline__ void merge_task(const CascadeMergeParams& p, int64_t task, int hgroups, int lane) {
+__device__ __forceinline__ void merge_task(const CascadeMergeParams& p, int64_t task, int hgroups, int b, int nch,
+                                           int lane) {
   constexpr int EPC = Elem<T>::kPerChunk;
   constexpr int DCH = D / EPC;   // output chunks per row
   constexpr int HPW = 32 / DCH;  // heads per warp
-  const int it = (int)(task / hgroups);
   const int h = (int)(task % hgroups) * HPW + lane / DCH, c = lane % DCH;
-  const int b = __ldg(&p.items[2 * it]), nch = __ldg(&p.items[2 * it + 1]);
   if (b < 0 || b >= p.batch || nch < 0 || nch > p.max_chunks) {
     if (lane == 0) set_error(p.error, kErrBadWork);
     return;
@@ -136,10 +135,15 @@ __global__ void __launch_bounds__(128) cascade_merge_kernel(const CascadeMergePa
   constexpr int HPW = 32 / (D / Elem<T>::kPerChunk);
   const int lane = threadIdx.x & 31;
   griddep_launch_dependents();
-  griddep_wait();  // the suffix and prefix passes have completed
   const int hgroups = (p.num_heads + HPW - 1) / HPW;
   const int64_t t = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
-  if (t < (int64_t)p.num_items * hgroups) merge_task<T, D>(p, t, hgroups, lane);
+  const bool has_task = t < (int64_t)p.num_items * hgroups;
+  // the merge item is a plan array (not written by the passes): read it while
+  // they drain, one memory round trip off the merge
+  const int it = has_task ? (int)(t / hgroups) : 0;
+  const int b = has_task ? __ldg(&p.items[2 * it]) : 0, nch = has_task ? __ldg(&p.items[2 * it + 1]) : 0;
+  griddep_wait();  // the suffix and prefix passes have completed
+  if (has_task) merge_task<T, D>(p, t, hgroups, b, nch, lane);
 }
 
 // Launch with or without programmatic dependent launch (the kernel may start
