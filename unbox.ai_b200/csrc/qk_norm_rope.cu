@@ -177,7 +177,7 @@ __global__ void __launch_bounds__(kPrepWarps * 32) qk_norm_rope_vec_kernel(const
       const bool is_q = h < p.num_heads;
       const int hk = h - p.num_heads;
       const bool to_cache = !is_q && slot >= 0 && slot < limit;
-      float x[8], w[8];
+      uint32_t xw[4] = {0u, 0u, 0u, 0u}, ww[4] = {0u, 0u, 0u, 0u};  // element pairs of x and of the weight
       float4 cs[2] = {make_float4(1.f, 0.f, 1.f, 0.f), make_float4(1.f, 0.f, 1.f, 0.f)};
       uint4 vrow = make_uint4(0, 0, 0, 0);
       float ss = 0.f;
@@ -193,39 +193,31 @@ __global__ void __launch_bounds__(kPrepWarps * 32) qk_norm_rope_vec_kernel(const
         if (to_cache)
           vrow = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(p.v_in) + t * p.v_st +
                                                       (int64_t)hk * p.v_sh) + c);
-        Elem<T>::unpack(xr, x);
-        Elem<T>::unpack(wr, w);
+        xw[0] = xr.x, xw[1] = xr.y, xw[2] = xr.z, xw[3] = xr.w;
+        ww[0] = wr.x, ww[1] = wr.y, ww[2] = wr.z, ww[3] = wr.w;
 #pragma unroll
-        for (int e = 0; e < 8; e += 2) {  // rounded squares, summed in element order
-          float s0 = __fmul_rn(x[e], x[e]), s1 = __fmul_rn(x[e + 1], x[e + 1]);
-          round2<T>(s0, s1);
-          ss += s0;
-          ss += s1;
+        for (int i = 0; i < 4; ++i) {  // rounded squares (packed), summed in element order
+          const float2 sq = unpack_word<T>(mul2_rn<T>(xw[i], xw[i]));
+          ss += sq.x;
+          ss += sq.y;
         }
       }
 #pragma unroll
       for (int off = W / 2; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
       if (!live) continue;
-      const float rf = rms_factor<T>(ss, inv_d, p.eps);
-      // (x * r) * w with each product rounded (pairwise: the values of
-      // rms_apply), the rotation, and the output rounded once by the packing
-      float out[8];
+      const float rf = rms_factor<T>(ss, inv_d, p.eps);  // a dtype value
+      const uint32_t rf2 = Elem<T>::pack2(rf, rf);
+      // (x * r) * w with each product rounded (packed multiplies: the values of
+      // rms_apply), the rotation in fp32, and the output rounded by the packing
+      uint32_t ow[4];
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const int e = 4 * j + 2 * k;
-          float y0 = __fmul_rn(x[e], rf), y1 = __fmul_rn(x[e + 1], rf);
-          round2<T>(y0, y1);
-          y0 = __fmul_rn(y0, w[e]);
-          y1 = __fmul_rn(y1, w[e + 1]);
-          round2<T>(y0, y1);
-          const float2 o = rotate_pair(y0, y1, k ? cs[j].z : cs[j].x, k ? cs[j].w : cs[j].y);
-          out[e] = o.x;
-          out[e + 1] = o.y;
-        }
+      for (int i = 0; i < 4; ++i) {
+        const float2 y = unpack_word<T>(mul2_rn<T>(mul2_rn<T>(xw[i], rf2), ww[i]));
+        const float4& c4 = cs[i >> 1];
+        const float2 o = rotate_pair(y.x, y.y, (i & 1) ? c4.z : c4.x, (i & 1) ? c4.w : c4.y);
+        ow[i] = Elem<T>::pack2(o.x, o.y);
       }
-      const uint4 packed = Elem<T>::pack(out);
+      const uint4 packed = make_uint4(ow[0], ow[1], ow[2], ow[3]);
       if (is_q) {
         reinterpret_cast<uint4*>(static_cast<T*>(p.q_out) + t * p.qo_st + (int64_t)h * p.qo_sh)[c] = packed;
         continue;

@@ -30,24 +30,21 @@ __device__ __forceinline__ float round_to<__nv_bfloat16>(float x) { return __bfl
 template <>
 __device__ __forceinline__ float round_to<__half>(float x) { return __half2float(__float2half_rn(x)); }
 
-// Rounds two values to the dtype at once (one packed conversion, then back to
-// fp32): the same values as round_to on each.
+// Product of two element pairs of a 16-bit row (one 32-bit word each), rounded
+// to the dtype by one packed multiply. The exact product of two bf16 (or two
+// fp16) values fits an fp32 significand, so this equals the fp32 product
+// rounded to the dtype, element by element: the value of round_to(a * b).
 template <typename T>
-__device__ __forceinline__ void round2(float& a, float& b);
+__device__ __forceinline__ uint32_t mul2_rn(uint32_t a, uint32_t b);
 template <>
-__device__ __forceinline__ void round2<float>(float&, float&) {}
-template <>
-__device__ __forceinline__ void round2<__nv_bfloat16>(float& a, float& b) {
-  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  const uint32_t r = *reinterpret_cast<uint32_t*>(&h);
-  a = __uint_as_float(r << 16);
-  b = __uint_as_float(r & 0xffff0000u);
+__device__ __forceinline__ uint32_t mul2_rn<__nv_bfloat16>(uint32_t a, uint32_t b) {
+  __nv_bfloat162 r = __hmul2_rn(*reinterpret_cast<const __nv_bfloat162*>(&a), *reinterpret_cast<const __nv_bfloat162*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
 }
 template <>
-__device__ __forceinline__ void round2<__half>(float& a, float& b) {
-  const float2 f = __half22float2(__floats2half2_rn(a, b));
-  a = f.x;
-  b = f.y;
+__device__ __forceinline__ uint32_t mul2_rn<__half>(uint32_t a, uint32_t b) {
+  __half2 r = __hmul2_rn(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
 }
 
 // x.pow(2) of one element (the product is not fused into the running sum)
