@@ -681,27 +681,29 @@ __device__ __forceinline__ void prep_q(const DecodeParams& p, int pos, bool real
   const float inv_d = 1.f / (float)D;
   bool pos_ok;
   const float2* rope_row = rope_row_of(p, pos, lane == 0, pos_ok);
+  // the rounded products of the norm as packed multiplies (mul2_rn: the same
+  // values as rounded_square / rms_apply on each element)
   float ss = 0.f;
 #pragma unroll
   for (int ks = 0; ks < KS; ++ks)
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const float2 x = unpack_word<T>(qa[ks][h]);
-      ss += rounded_square<T>(x.x) + rounded_square<T>(x.y);
+      const float2 sq = unpack_word<T>(mul2_rn<T>(qa[ks][h], qa[ks][h]));
+      ss += sq.x + sq.y;
     }
   ss += __shfl_xor_sync(kFull, ss, 1);
   ss += __shfl_xor_sync(kFull, ss, 2);
   const float rf = rms_factor<T>(ss, inv_d, p.eps);
+  const uint32_t rf2 = Elem<T>::pack2(rf, rf);
   const uint32_t* w = static_cast<const uint32_t*>(p.q_w);
 #pragma unroll
   for (int ks = 0; ks < KS; ++ks)
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int j = 8 * ks + 4 * h + qc;  // element pair index of column 16ks + 8h + 2qc
-      const float2 x = unpack_word<T>(qa[ks][h]);
-      const float2 wv = unpack_word<T>(__ldg(w + j));
+      const float2 y = unpack_word<T>(mul2_rn<T>(mul2_rn<T>(qa[ks][h], rf2), __ldg(w + j)));
       const float2 cs = pos_ok ? __ldg(rope_row + j) : make_float2(1.f, 0.f);
-      const float2 o = rotate_pair(rms_apply<T>(x.x, rf, wv.x), rms_apply<T>(x.y, rf, wv.y), cs.x, cs.y);
+      const float2 o = rotate_pair(y.x, y.y, cs.x, cs.y);
       qa[ks][h] = real_row ? Elem<T>::pack2(o.x, o.y) : 0u;
     }
 }
@@ -713,31 +715,35 @@ __device__ __forceinline__ void prep_k(const DecodeParams& p, int pos, int lane,
   const float inv_d = 1.f / (float)D;
   bool pos_ok;
   const float2* rope_row = rope_row_of(p, pos, false, pos_ok);  // the q rows' call reports it
-  float f[8];
-  Elem<T>::unpack(a_row, f);
+  const uint32_t xw[4] = {a_row.x, a_row.y, a_row.z, a_row.w};  // element pairs
   const bool k_lane = lane < RC;
   float ss = 0.f;
   if (k_lane) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) ss += rounded_square<T>(f[i]);
+    for (int i = 0; i < 4; ++i) {  // rounded squares (packed), summed in element order
+      const float2 sq = unpack_word<T>(mul2_rn<T>(xw[i], xw[i]));
+      ss += sq.x;
+      ss += sq.y;
+    }
   }
   ss = warp_sum(ss);
   if (k_lane) {
     const float rf = rms_factor<T>(ss, inv_d, p.eps);
-    float wf[8];
-    Elem<T>::unpack(__ldg(static_cast<const uint4*>(p.k_w) + lane), wf);
+    const uint32_t rf2 = Elem<T>::pack2(rf, rf);
+    const uint4 wr = __ldg(static_cast<const uint4*>(p.k_w) + lane);
+    const uint32_t ww[4] = {wr.x, wr.y, wr.z, wr.w};
     const float4* rp = reinterpret_cast<const float4*>(rope_row + 4 * lane);
     const float4 r01 = pos_ok ? __ldg(rp) : make_float4(1.f, 0.f, 1.f, 0.f);
     const float4 r23 = pos_ok ? __ldg(rp + 1) : make_float4(1.f, 0.f, 1.f, 0.f);
     const float cs[8] = {r01.x, r01.y, r01.z, r01.w, r23.x, r23.y, r23.z, r23.w};
+    uint32_t ow[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float2 o = rotate_pair(rms_apply<T>(f[2 * i], rf, wf[2 * i]), rms_apply<T>(f[2 * i + 1], rf, wf[2 * i + 1]),
-                                   cs[2 * i], cs[2 * i + 1]);
-      f[2 * i] = o.x;
-      f[2 * i + 1] = o.y;
+      const float2 y = unpack_word<T>(mul2_rn<T>(mul2_rn<T>(xw[i], rf2), ww[i]));
+      const float2 o = rotate_pair(y.x, y.y, cs[2 * i], cs[2 * i + 1]);
+      ow[i] = Elem<T>::pack2(o.x, o.y);
     }
-    a_row = Elem<T>::pack(f);
+    a_row = make_uint4(ow[0], ow[1], ow[2], ow[3]);
   }
 }
 
