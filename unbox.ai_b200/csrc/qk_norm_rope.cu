@@ -146,8 +146,10 @@ __global__ void __launch_bounds__(kPrepWarps * 32) qk_norm_rope_kernel(const Pre
 // qk_norm_rope_kernel.
 constexpr int kVecTokens = 2;
 
+// Five blocks per SM (48 registers, no spills): more warps to hide each row's
+// memory round trip than the four that 64 registers allow.
 template <typename T, int W>
-__global__ void __launch_bounds__(kPrepWarps * 32) qk_norm_rope_vec_kernel(const PrepParams p) {
+__global__ void __launch_bounds__(kPrepWarps * 32, 5) qk_norm_rope_vec_kernel(const PrepParams p) {
   constexpr int RPW = 32 / W;  // rows of one warp at a time
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int seg = lane / W, c = lane % W;
