@@ -103,3 +103,31 @@ def test_bad_position_is_reported_and_unrotated(oracle):
     q, kk, bad = oracle.qk_norm_rope(x, k, w, w, rope, np.array([1, 9]), 1e-6)
     assert bad.tolist() == [False, True]
     np.testing.assert_allclose(q[1], oracle.rms_norm(x[1].numpy(), w.numpy(), 1e-6, oracle.F32))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_sixteen_bit_products_are_exact_in_fp32(dtype):
+    """The kernels' norm multiplies two 16-bit values with one packed 16-bit
+    multiply instead of an fp32 multiply followed by a rounding to the dtype.
+    Both give the same value because the exact product of two bf16 (or two
+    fp16) values fits an fp32 significand whenever it is a normal fp32 number:
+    checked here against float64 on values spread over the whole range, with
+    the one-rounding result (float64 product rounded once to the dtype) equal to
+    the two-rounding one (fp32 product rounded to the dtype)."""
+    g = torch.Generator().manual_seed(7)
+    n = 200_000
+    finfo = torch.finfo(dtype)
+    mag = torch.exp2(torch.empty(n).uniform_(-40.0, 40.0, generator=g)) if dtype == torch.bfloat16 else \
+        torch.exp2(torch.empty(n).uniform_(-12.0, 12.0, generator=g))
+    sign = torch.where(torch.rand(n, generator=g) < 0.5, -1.0, 1.0)
+    a = (mag * sign).to(dtype)
+    b = (torch.exp2(torch.empty(n).uniform_(-20.0, 20.0, generator=g)) * sign.flip(0)).to(dtype)
+    if dtype == torch.float16:
+        b = (torch.exp2(torch.empty(n).uniform_(-6.0, 6.0, generator=g)) * sign.flip(0)).to(dtype)
+    exact = a.double() * b.double()
+    f32 = a.float() * b.float()
+    normal = (exact.abs() >= torch.finfo(torch.float32).tiny) & (exact.abs() <= torch.finfo(torch.float32).max)
+    assert normal.float().mean() > 0.99
+    assert torch.equal(f32.double()[normal], exact[normal])                      # no rounding in fp32
+    in_range = normal & (exact.abs() <= finfo.max)
+    assert torch.equal(f32[in_range].to(dtype), exact[in_range].to(dtype))       # one rounding = two

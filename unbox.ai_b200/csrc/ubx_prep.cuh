@@ -34,6 +34,9 @@ __device__ __forceinline__ float round_to<__half>(float x) { return __half2float
 // to the dtype by one packed multiply. The exact product of two bf16 (or two
 // fp16) values fits an fp32 significand, so this equals the fp32 product
 // rounded to the dtype, element by element: the value of round_to(a * b).
+// The one exception is a product below the smallest normal fp32 (2^-126; for a
+// square, |x| below 2^-63): the fp32 path then rounds twice and the last bit
+// may differ.
 template <typename T>
 __device__ __forceinline__ uint32_t mul2_rn(uint32_t a, uint32_t b);
 template <>
