@@ -140,16 +140,17 @@ __global__ void __launch_bounds__(kPrepWarps * 32) qk_norm_rope_kernel(const Pre
 // each lane takes one 16-byte chunk (8 elements, 4 rotary pairs) of a row, the
 // CH = head_dim / 8 lanes of a row sit in a segment of W lanes (W the power of
 // two >= CH), so a warp works on 32 / W rows at once and a row's sum of squares
-// is a W-lane butterfly. A block is one token (grid-stride), its warps over the
-// token's q and k rows; every load of a row (x, weight, rotary pairs, the V row)
+// is a W-lane butterfly. The launch's (token, head) rows are taken 16 per block
+// pass (8 warps x 2 rows) by a persistent grid, so every SM gets the same number
+// of passes within one; every load of a row (x, weight, rotary pairs, the V row)
 // is issued before the sum is reduced. Same rounding points as
 // qk_norm_rope_kernel.
-constexpr int kVecTokens = 2;
-
 // Five blocks per SM (48 registers, no spills): more warps to hide each row's
 // memory round trip than the four that 64 registers allow.
+constexpr int kVecBlocksPerSm = 5;
+
 template <typename T, int W>
-__global__ void __launch_bounds__(kPrepWarps * 32, 5) qk_norm_rope_vec_kernel(const PrepParams p) {
+__global__ void __launch_bounds__(kPrepWarps * 32, kVecBlocksPerSm) qk_norm_rope_vec_kernel(const PrepParams p) {
   constexpr int RPW = 32 / W;  // rows of one warp at a time
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int seg = lane / W, c = lane % W;
@@ -158,19 +159,16 @@ __global__ void __launch_bounds__(kPrepWarps * 32, 5) qk_norm_rope_vec_kernel(co
   const float inv_d = 1.f / (float)p.head_dim;
   const int64_t limit = p.num_blocks * p.block_size;
   const int bs_shift = (p.block_size & (p.block_size - 1)) == 0 ? __ffs(p.block_size) - 1 : -1;
-  // kVecTokens tokens per block and pass over their rows together, so that every
-  // warp has a row set on every pass
-  const int rows = kVecTokens * rows_per_token;
-  for (int64_t t0 = (int64_t)blockIdx.x * kVecTokens; t0 < p.num_tokens; t0 += (int64_t)gridDim.x * kVecTokens) {
-    for (int r0 = warp * RPW; r0 < rows; r0 += nwarps * RPW) {
-      const int r = r0 + seg;
-      int h = r, ti = 0;  // (token, head) of row r, without an integer division
-      while (h >= rows_per_token) {
-        h -= rows_per_token;
-        ++ti;
-      }
-      const int64_t t = t0 + ti;
-      const bool live = c < CH && r < rows && t < p.num_tokens;  // segment-uniform
+  // every (token, head) row of the launch, 16 rows per block pass, grid-stride
+  const int64_t total_rows = p.num_tokens * rows_per_token;
+  const int rows_per_pass = nwarps * RPW;
+  for (int64_t base = (int64_t)blockIdx.x * rows_per_pass; base < total_rows;
+       base += (int64_t)gridDim.x * rows_per_pass) {
+    {
+      const int64_t R = base + warp * RPW + seg;
+      const int64_t t = R / rows_per_token;
+      const int h = (int)(R - t * rows_per_token);
+      const bool live = c < CH && R < total_rows;  // segment-uniform
       const int pos = live ? __ldg(&p.positions[t]) : 0;
       const bool pos_ok = pos >= 0 && pos < p.rope_n;
       if (live && !pos_ok && c == 0 && h == 0) set_error(p.error, kErrBadPosition);
@@ -238,6 +236,19 @@ __global__ void __launch_bounds__(kPrepWarps * 32, 5) qk_norm_rope_vec_kernel(co
 
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
+// SMs of the current device (looked up once per device; 148 if the query fails).
+int num_sms() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
 // Rows, strides, weights and rotary rows on 16-byte boundaries, head_dim a
 // multiple of 8 (at most 256): the 16-byte-per-lane kernel applies.
 bool vec_ok(const PrepParams& p) {
@@ -270,8 +281,10 @@ cudaError_t launch_qk_norm_rope(int dtype, const PrepParams& p, cudaStream_t str
   if (p.num_tokens == 0) return cudaSuccess;
   const int blocks = (int)(p.num_tokens < 148 * 32 ? p.num_tokens : 148 * 32);  // a block per token
   if (dtype != 0 && vec_ok(p)) {
-    const int64_t vb = (p.num_tokens + kVecTokens - 1) / kVecTokens;
-    const int vblocks = (int)(vb < 148 * 32 ? vb : 148 * 32);
+    // a persistent grid of kVecBlocksPerSm blocks per SM over every row, 16 at a time
+    const int64_t vb = (p.num_tokens * (p.num_heads + p.num_kv_heads) + 15) / 16;
+    const int64_t cap = (int64_t)kVecBlocksPerSm * num_sms();
+    const int vblocks = (int)(vb < cap ? vb : cap);
     return dtype == 1 ? launch_vec<__nv_bfloat16>(p, vblocks, stream) : launch_vec<__half>(p, vblocks, stream);
   }
   switch (dtype) {
