@@ -164,72 +164,70 @@ __global__ void __launch_bounds__(kPrepWarps * 32, kVecBlocksPerSm) qk_norm_rope
   const int rows_per_pass = nwarps * RPW;
   for (int64_t base = (int64_t)blockIdx.x * rows_per_pass; base < total_rows;
        base += (int64_t)gridDim.x * rows_per_pass) {
-    {
-      const int64_t R = base + warp * RPW + seg;
-      const int64_t t = R / rows_per_token;
-      const int h = (int)(R - t * rows_per_token);
-      const bool live = c < CH && R < total_rows;  // segment-uniform
-      const int pos = live ? __ldg(&p.positions[t]) : 0;
-      const bool pos_ok = pos >= 0 && pos < p.rope_n;
-      if (live && !pos_ok && c == 0 && h == 0) set_error(p.error, kErrBadPosition);
-      const int64_t slot = (live && p.k_cache) ? __ldg(&p.slots[t]) : -1;
-      const float4* rope_row = reinterpret_cast<const float4*>(p.rope + (int64_t)(pos_ok ? pos : 0) * p.rope_sp);
-      const bool is_q = h < p.num_heads;
-      const int hk = h - p.num_heads;
-      const bool to_cache = !is_q && slot >= 0 && slot < limit;
-      uint32_t xw[4] = {0u, 0u, 0u, 0u}, ww[4] = {0u, 0u, 0u, 0u};  // element pairs of x and of the weight
-      float4 cs[2] = {make_float4(1.f, 0.f, 1.f, 0.f), make_float4(1.f, 0.f, 1.f, 0.f)};
-      uint4 vrow = make_uint4(0, 0, 0, 0);
-      float ss = 0.f;
-      if (live) {
-        const T* src = is_q ? static_cast<const T*>(p.q_in) + t * p.q_st + (int64_t)h * p.q_sh
-                            : static_cast<const T*>(p.k_in) + t * p.k_st + (int64_t)hk * p.k_sh;
-        const uint4 xr = __ldg(reinterpret_cast<const uint4*>(src) + c);
-        const uint4 wr = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(is_q ? p.q_w : p.k_w)) + c);
-        if (pos_ok) {
-          cs[0] = __ldg(rope_row + 2 * c);
-          cs[1] = __ldg(rope_row + 2 * c + 1);
-        }
-        if (to_cache)
-          vrow = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(p.v_in) + t * p.v_st +
-                                                      (int64_t)hk * p.v_sh) + c);
-        xw[0] = xr.x, xw[1] = xr.y, xw[2] = xr.z, xw[3] = xr.w;
-        ww[0] = wr.x, ww[1] = wr.y, ww[2] = wr.z, ww[3] = wr.w;
+    const int64_t R = base + warp * RPW + seg;
+    const int64_t t = R / rows_per_token;
+    const int h = (int)(R - t * rows_per_token);
+    const bool live = c < CH && R < total_rows;  // segment-uniform
+    const int pos = live ? __ldg(&p.positions[t]) : 0;
+    const bool pos_ok = pos >= 0 && pos < p.rope_n;
+    if (live && !pos_ok && c == 0 && h == 0) set_error(p.error, kErrBadPosition);
+    const int64_t slot = (live && p.k_cache) ? __ldg(&p.slots[t]) : -1;
+    const float4* rope_row = reinterpret_cast<const float4*>(p.rope + (int64_t)(pos_ok ? pos : 0) * p.rope_sp);
+    const bool is_q = h < p.num_heads;
+    const int hk = h - p.num_heads;
+    const bool to_cache = !is_q && slot >= 0 && slot < limit;
+    uint32_t xw[4] = {0u, 0u, 0u, 0u}, ww[4] = {0u, 0u, 0u, 0u};  // element pairs of x and of the weight
+    float4 cs[2] = {make_float4(1.f, 0.f, 1.f, 0.f), make_float4(1.f, 0.f, 1.f, 0.f)};
+    uint4 vrow = make_uint4(0, 0, 0, 0);
+    float ss = 0.f;
+    if (live) {
+      const T* src = is_q ? static_cast<const T*>(p.q_in) + t * p.q_st + (int64_t)h * p.q_sh
+                          : static_cast<const T*>(p.k_in) + t * p.k_st + (int64_t)hk * p.k_sh;
+      const uint4 xr = __ldg(reinterpret_cast<const uint4*>(src) + c);
+      const uint4 wr = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(is_q ? p.q_w : p.k_w)) + c);
+      if (pos_ok) {
+        cs[0] = __ldg(rope_row + 2 * c);
+        cs[1] = __ldg(rope_row + 2 * c + 1);
+      }
+      if (to_cache)
+        vrow = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(p.v_in) + t * p.v_st +
+                                                    (int64_t)hk * p.v_sh) + c);
+      xw[0] = xr.x, xw[1] = xr.y, xw[2] = xr.z, xw[3] = xr.w;
+      ww[0] = wr.x, ww[1] = wr.y, ww[2] = wr.z, ww[3] = wr.w;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {  // rounded squares (packed), summed in element order
-          const float2 sq = unpack_word<T>(mul2_rn<T>(xw[i], xw[i]));
-          ss += sq.x;
-          ss += sq.y;
-        }
+      for (int i = 0; i < 4; ++i) {  // rounded squares (packed), summed in element order
+        const float2 sq = unpack_word<T>(mul2_rn<T>(xw[i], xw[i]));
+        ss += sq.x;
+        ss += sq.y;
       }
+    }
 #pragma unroll
-      for (int off = W / 2; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-      if (!live) continue;
-      const float rf = rms_factor<T>(ss, inv_d, p.eps);  // a dtype value
-      const uint32_t rf2 = Elem<T>::pack2(rf, rf);
-      // (x * r) * w with each product rounded (packed multiplies: the values of
-      // rms_apply), the rotation in fp32, and the output rounded by the packing
-      uint32_t ow[4];
+    for (int off = W / 2; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if (!live) continue;
+    const float rf = rms_factor<T>(ss, inv_d, p.eps);  // a dtype value
+    const uint32_t rf2 = Elem<T>::pack2(rf, rf);
+    // (x * r) * w with each product rounded (packed multiplies: the values of
+    // rms_apply), the rotation in fp32, and the output rounded by the packing
+    uint32_t ow[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 y = unpack_word<T>(mul2_rn<T>(mul2_rn<T>(xw[i], rf2), ww[i]));
-        const float4& c4 = cs[i >> 1];
-        const float2 o = rotate_pair(y.x, y.y, (i & 1) ? c4.z : c4.x, (i & 1) ? c4.w : c4.y);
-        ow[i] = Elem<T>::pack2(o.x, o.y);
-      }
-      const uint4 packed = make_uint4(ow[0], ow[1], ow[2], ow[3]);
-      if (is_q) {
-        reinterpret_cast<uint4*>(static_cast<T*>(p.q_out) + t * p.qo_st + (int64_t)h * p.qo_sh)[c] = packed;
-        continue;
-      }
-      if (p.k_out) reinterpret_cast<uint4*>(static_cast<T*>(p.k_out) + t * p.ko_st + (int64_t)hk * p.ko_sh)[c] = packed;
-      if (p.k_cache && slot >= limit && c == 0 && hk == 0) set_error(p.error, kErrBadSlot);
-      if (to_cache) {
-        const int64_t blk = bs_shift >= 0 ? slot >> bs_shift : slot / p.block_size;
-        const int64_t off = blk * p.c_sblk + (slot - blk * p.block_size) * p.c_stok + (int64_t)hk * p.c_sh;
-        reinterpret_cast<uint4*>(static_cast<T*>(p.k_cache) + off)[c] = packed;
-        reinterpret_cast<uint4*>(static_cast<T*>(p.v_cache) + off)[c] = vrow;
-      }
+    for (int i = 0; i < 4; ++i) {
+      const float2 y = unpack_word<T>(mul2_rn<T>(mul2_rn<T>(xw[i], rf2), ww[i]));
+      const float4& c4 = cs[i >> 1];
+      const float2 o = rotate_pair(y.x, y.y, (i & 1) ? c4.z : c4.x, (i & 1) ? c4.w : c4.y);
+      ow[i] = Elem<T>::pack2(o.x, o.y);
+    }
+    const uint4 packed = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+    if (is_q) {
+      reinterpret_cast<uint4*>(static_cast<T*>(p.q_out) + t * p.qo_st + (int64_t)h * p.qo_sh)[c] = packed;
+      continue;
+    }
+    if (p.k_out) reinterpret_cast<uint4*>(static_cast<T*>(p.k_out) + t * p.ko_st + (int64_t)hk * p.ko_sh)[c] = packed;
+    if (p.k_cache && slot >= limit && c == 0 && hk == 0) set_error(p.error, kErrBadSlot);
+    if (to_cache) {
+      const int64_t blk = bs_shift >= 0 ? slot >> bs_shift : slot / p.block_size;
+      const int64_t off = blk * p.c_sblk + (slot - blk * p.block_size) * p.c_stok + (int64_t)hk * p.c_sh;
+      reinterpret_cast<uint4*>(static_cast<T*>(p.k_cache) + off)[c] = packed;
+      reinterpret_cast<uint4*>(static_cast<T*>(p.v_cache) + off)[c] = vrow;
     }
   }
 }
